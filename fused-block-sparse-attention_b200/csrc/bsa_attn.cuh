@@ -1,0 +1,57 @@
+// Parameter blocks and tile traits shared by the attention kernels and their
+// host launchers.
+#pragma once
+#include "bsa_common.cuh"
+
+namespace bsa {
+
+struct AttnParams {
+  int B, Hq, Hkv, grp, L, nblk, kk, bs, mask_mode, causal;
+  int Lp;        // nblk * bs (row count of lse / Dvec)
+  float scale;   // softmax scale
+  float scale2;  // scale * log2(e)
+  const int32_t *sel;
+  int64_t sel_sb, sel_sh, sel_sn;
+  const float *gate;
+  int64_t gate_sb, gate_sh, gate_sn;
+  // forward
+  void *o;
+  int64_t o_sb, o_sh, o_sl;
+  const void *og;
+  int64_t og_sb, og_sh, og_sl;
+  float *lse;
+  // backward
+  const void *q, *k, *v, *dout;  // used by the fp32 SIMT kernels (no TMA)
+  int64_t q_sb, q_sh, q_sl, k_sb, k_sh, k_sl, v_sb, v_sh, v_sl, do_sb, do_sh, do_sl;
+  const void *oin;
+  int64_t oi_sb, oi_sh, oi_sl;
+  void *dq, *dk, *dv;
+  int64_t dq_sb, dq_sh, dq_sl, dk_sb, dk_sh, dk_sl, dv_sb, dv_sh, dv_sl;
+  float *dgate;
+  float *dvec;  // (B,Hq,Lp) rowsum(dO * O)
+  int32_t *status;
+};
+
+// Backward CSR / chunk plan (device pointers into the workspace).
+struct BwdPlan {
+  int Hs;        // selection heads
+  int Y;         // KV heads per selection head
+  int nbins;     // B * Hs * nblk
+  int C;         // entries per dK/dV chunk
+  const int32_t *row_ptr;  // nbins + 1
+  const int32_t *col;      // entries qblk*kk + slot
+  const unsigned long long *plan;  // nbins + 1: (chunk_off << 32) | part_off (exclusive)
+  float *part;             // partial dK/dV tiles
+};
+
+template <int BS, int D>
+struct TileCfg {
+  static constexpr int NW = BS / 16;          // warps, 16 rows each
+  static constexpr int NT = NW * 32;
+  static constexpr int KC = BS < 64 ? BS : 64;  // rows per streamed chunk
+  static constexpr int NCH = BS / KC;         // chunks per block
+  static constexpr int TILE = BS * D * 2;     // bytes of a full 16-bit block tile
+  static constexpr int CH = KC * D * 2;       // bytes of one 16-bit chunk
+};
+
+}  // namespace bsa

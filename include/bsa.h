@@ -1,0 +1,213 @@
+/*
+ * bsa.h — C ABI of the B200-native fused block-sparse attention library
+ * (libbsa_b200.so).  Plain pointers, sizes and strides only; no torch types.
+ *
+ * The reference (apoc/fused-block-sparse-attention, Python + Triton) has no C
+ * interface: its boundary is the Python functions listed beside each entry
+ * point.  Each entry point here replaces the device work behind one of them,
+ * and the Python modules in fused-block-sparse-attention_b200/ bind these
+ * symbols through ctypes with the reference's call signatures.
+ *
+ * Conventions
+ *  - All device pointers are on the current CUDA device; all work is enqueued
+ *    on `stream` (a cudaStream_t, 0 = legacy default stream); no entry point
+ *    synchronises the host.
+ *  - Tensors of shape (B, H, L, D) are described by a bsa_view: a base pointer
+ *    plus element strides of the B, H and L axes; the D axis must be
+ *    unit-stride.  bf16/f16 views read through TMA need 16-byte aligned base
+ *    pointers and strides that are multiples of 8 elements.
+ *  - Every call returns a bsa_status.  On an error nothing is launched and
+ *    bsa_last_error() returns a one-line message (thread-local).
+ *  - `status` (optional, may be NULL) points at one int32 in device memory.
+ *    Kernels OR error bits into it: BSA_DEVERR_INDEX when a selected block id
+ *    is outside [0, nblk) (that slot is then treated as masked), and
+ *    BSA_DEVERR_TIMEOUT when a bounded wait on a TMA barrier gave up.
+ *    The caller clears and reads it.
+ */
+#ifndef BSA_B200_H
+#define BSA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st *bsa_stream_t; /* == cudaStream_t */
+
+typedef enum {
+  BSA_OK = 0,
+  BSA_ERR_SHAPE = 1,       /* inconsistent or out-of-range sizes            */
+  BSA_ERR_DTYPE = 2,       /* unsupported element type                      */
+  BSA_ERR_STRIDE = 3,      /* stride/alignment not accepted (copy first)    */
+  BSA_ERR_UNSUPPORTED = 4, /* valid, but no kernel instance for this shape  */
+  BSA_ERR_INDEX = 5,       /* reported by bsa_status_decode for INDEX bits  */
+  BSA_ERR_LAUNCH = 6,      /* CUDA launch / driver error                    */
+  BSA_ERR_TIMEOUT = 7,     /* reported by bsa_status_decode for TIMEOUT     */
+  BSA_ERR_WORKSPACE = 8,   /* workspace pointer NULL or too small           */
+  BSA_ERR_ARG = 9          /* NULL required pointer / bad enum value        */
+} bsa_status;
+
+#define BSA_DEVERR_INDEX 1
+#define BSA_DEVERR_TIMEOUT 2
+
+typedef enum { BSA_BF16 = 0, BSA_F16 = 1, BSA_F32 = 2 } bsa_dtype;
+
+/* How selected slots are masked.
+ *  BSA_MASK_SLOT  — triton_kernel.py semantics (reference src/triton_kernel.py:57-61):
+ *                   causal: slot 0 gets the triu mask (key row > query row),
+ *                   slot j>0 is dropped when its block id >= the query block;
+ *                   non-causal: nothing is masked, duplicates count twice.
+ *  BSA_MASK_TOKEN — qwen gather semantics (reference src/qwen_blocksparse.py:67-72):
+ *                   a key is valid iff its position <= the query position
+ *                   (only when causal != 0), < L, and its slot is the first
+ *                   occurrence of that block id in the row. */
+typedef enum { BSA_MASK_SLOT = 0, BSA_MASK_TOKEN = 1 } bsa_mask_mode;
+
+typedef struct {
+  void *ptr;
+  int64_t sb, sh, sl; /* element strides of the B, H and L axes */
+} bsa_view;
+
+/* One struct for the forward and backward attention calls.
+ * q: (B,Hq,L,D); k, v: (B,Hkv,L,D); Hq % Hkv == 0, query head h reads KV head
+ * h / (Hq/Hkv).  L <= nblk*bs; rows past L read as zero (padding).
+ * sel: int32 (B, Hs, nblk, kk) block ids addressed as
+ *      sel[b*sel_sb + (h/(Hq/Hkv))*sel_sh + qblk*sel_sn + slot]; sel_sh = 0
+ *      shares one selection over all heads (the reference layout (B,nblk,kk)).
+ *      sel == NULL means the identity selection (kk == nblk, slot j -> block j).
+ * gate: optional fp32 additive bias per selected block, addressed like sel.
+ * lse: fp32 (B, Hq, nblk*bs), row log2-sum-exp written by the forward and
+ *      read by the backward (internal format: log2 domain, scale folded in).
+ * out_gate: optional (same dtype as q) sigmoid output gate, o *= sigmoid(g),
+ *      addressed like o (reference src/patch_qwen.py:55). */
+typedef struct {
+  int32_t dtype;
+  int32_t B, Hq, Hkv, L, D;
+  int32_t bs, nblk, kk;
+  int32_t mask_mode, causal;
+  float scale;
+  bsa_view q, k, v, o;
+  bsa_view dout, dq, dk, dv; /* backward only */
+  bsa_view out_gate;         /* forward only, ptr NULL = none */
+  const int32_t *sel;
+  int64_t sel_sb, sel_sh, sel_sn;
+  const float *gate;
+  int64_t gate_sb, gate_sh, gate_sn;
+  float *lse;
+  float *dgate; /* backward, optional: fp32 (B,Hq,nblk,kk) per-head d(loss)/d(gate) */
+  int32_t *status;
+} bsa_attn_args;
+
+/* Forward: o = softmax(q k^T * scale + gate + mask) v over the selected blocks.
+ * Replaces triton_kernel.bsattn_forward (reference src/triton_kernel.py:184-207,
+ * kernel :20-74) and the gather core of qwen_blocksparse.blocksparse_forward
+ * (src/qwen_blocksparse.py:57-84), including GQA (:39,:74-81) and the sigmoid
+ * output gate of patch_qwen (src/patch_qwen.py:55). */
+bsa_status bsa_attn_fwd(const bsa_attn_args *a, bsa_stream_t stream);
+
+/* Backward: dq, dk, dv (and optional dgate) from dout, o and the forward's lse.
+ * Replaces triton_kernel.bsattn_backward (reference src/triton_kernel.py:210-234,
+ * kernel :77-181).  dk/dv are produced per key block over a CSR transpose of
+ * sel (no float atomics; bitwise deterministic).  Needs a device workspace of
+ * bsa_attn_bwd_workspace(a) bytes, 256-byte aligned. */
+size_t bsa_attn_bwd_workspace(const bsa_attn_args *a);
+bsa_status bsa_attn_bwd(const bsa_attn_args *a, void *workspace, size_t workspace_bytes,
+                        bsa_stream_t stream);
+
+/* Block pooling: per (b, output head, block) mean / min / max over the bs rows
+ * of the block (rows past L count as zeros, as after F.pad).  With grp > 1 the
+ * mean first averages grp consecutive input heads per row (output head
+ * hk = input head / grp), as qwen SelectMax does (src/qwen_blocksparse.py:113);
+ * min/max need grp == 1 (src/qwen_blocksparse.py:115-116).  Summation order is
+ * sequential (heads, then rows) in fp32, so results are bitwise reproducible.
+ * Outputs are contiguous fp32 (B, H/grp, nblk, D); any of them may be NULL.
+ * Replaces the pooling of BlockSparseSSA._scores (src/ssa_model.py:113-117). */
+typedef struct {
+  int32_t dtype;
+  int32_t B, H, L, D, bs, nblk, grp;
+  bsa_view x;
+  float *mean, *vmin, *vmax;
+  int32_t *status;
+} bsa_pool_args;
+bsa_status bsa_pool(const bsa_pool_args *a, bsa_stream_t stream);
+
+/* Block-pair scoring fused with a streaming top-k; the nblk x nblk score matrix
+ * is never stored.  G independent groups (e.g. b*H + h), each with nblk query
+ * summaries a[g,i,:] and key summaries b1/b2[g,j,:] (fp32, contiguous, dim wide).
+ *  score_kind DOT:     s = sum_d a_d*b1_d                 (mean-pooled q.k)
+ *             MAXDOT2: s = max(sum a*b1, sum a*b2)        (src/ssa_model.py:118-119)
+ *             QUEST:   s = sum_d a_d*(a_d>=0 ? b1_d : b2_d), b1=kmax, b2=kmin
+ *                                                         (src/qwen_blocksparse.py:117-120)
+ *  each sum is one fp32 fma chain over d = 0..dim-1 starting from 0.
+ *  Ranking: higher score first, ties to the lower block id.
+ *  layout SSA:    row i = [i, top-T content blocks by rank], T = min(topk, nblk-1);
+ *                 candidates j != i (and j < i when causal); missing picks are
+ *                 filled with i (src/ssa_model.py:151-162).
+ *  layout FINISH: top-T over j <= i with T = min(topk, nblk), missing picks -> i,
+ *                 then append i (and block 0 when sink), sorted ascending
+ *                 (src/qwen_blocksparse.py:87-99).
+ *  score_out / gate_out (optional, SSA only): the score of each selected block
+ *  and logsigmoid(score) (src/ssa_model.py:189-191).  topk <= 32. */
+typedef enum { BSA_SCORE_DOT = 0, BSA_SCORE_MAXDOT2 = 1, BSA_SCORE_QUEST = 2 } bsa_score_kind;
+typedef enum { BSA_SEL_SSA = 0, BSA_SEL_FINISH = 1 } bsa_sel_layout;
+typedef struct {
+  int32_t G, nblk, dim;
+  int32_t score_kind, layout, causal, topk, sink;
+  const float *a, *b1, *b2;
+  int32_t *sel;      /* (G, nblk, width) */
+  float *score_out;  /* optional (G, nblk, width) */
+  float *gate_out;   /* optional (G, nblk, width) */
+  int32_t *status;
+} bsa_select_args;
+int32_t bsa_select_width(const bsa_select_args *a);
+bsa_status bsa_select(const bsa_select_args *a, bsa_stream_t stream);
+
+/* CSR transpose of a selection: for every (b, sel head, key block) the list of
+ * entries e = qblk*kk + slot whose slot is active under the mask rules of
+ * bsa_attn_args, in ascending e.  row_ptr: int32 (B*Hs*nblk + 1);
+ * col: int32, capacity B*Hs*nblk*kk.  Used internally by bsa_attn_bwd and
+ * exported for testing.  Has no single reference counterpart: it replaces the
+ * atomic scatter of src/triton_kernel.py:178-179. */
+typedef struct {
+  int32_t B, Hs, nblk, kk, bs, L;
+  int32_t mask_mode, causal;
+  const int32_t *sel;
+  int64_t sel_sb, sel_sh, sel_sn;
+  int32_t *row_ptr, *col;
+  int32_t *status;
+} bsa_csr_args;
+size_t bsa_csr_workspace(const bsa_csr_args *a);
+bsa_status bsa_sel_csr(const bsa_csr_args *a, void *workspace, size_t workspace_bytes,
+                       bsa_stream_t stream);
+
+/* Partial rotary embedding with the arithmetic of transformers'
+ * apply_rotary_pos_emb (qwen3_5_moe, v5.5.0): on the first `rot` dims,
+ * y = x*cos + rotate_half(x)*sin with each product and the sum rounded to the
+ * tensor dtype; dims >= rot are copied.  cos/sin: (B, L, rot) in x's dtype with
+ * element strides cs_sb, cs_sl.  y may alias x.  Used by the Qwen variant
+ * (reference src/patch_qwen.py:47-48). */
+typedef struct {
+  int32_t dtype;
+  int32_t B, H, L, D, rot;
+  bsa_view x, y;
+  const void *cos, *sin;
+  int64_t cs_sb, cs_sl;
+} bsa_rope_args;
+bsa_status bsa_rope(const bsa_rope_args *a, bsa_stream_t stream);
+
+/* Turns a device status word (already copied to the host) into a bsa_status. */
+bsa_status bsa_status_decode(int32_t device_word);
+
+/* Thread-local message of the last failing call ("" if none). */
+const char *bsa_last_error(void);
+
+/* Library version (major*10000 + minor*100 + patch). */
+int32_t bsa_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BSA_B200_H */
