@@ -1,0 +1,109 @@
+"""Drop-in for the reference's BlockSparseSSA module (src/ssa_model.py:93-201)
+on sm_100a.
+
+BlockSparseSSA(d, h, block=64, topk=8, sel_dim=32, gate=False, causal=False,
+               use_triton=False).forward(x, needle_pos=None)
+
+Same parameters (qkv, o, sel_q, sel_k MLP selectors) and outputs.  Selection
+runs on device: the selector features are block-pooled (mean for queries,
+mean and max for keys) and scored max(sq.sk_mean, sq.sk_max) by the fused
+scoring/top-k kernel, which keeps the own block first and the top-k content
+blocks after it (ties to the lower block id).  Attention runs on the fused
+block-sparse kernels for both settings of use_triton:
+  use_triton=True   the gate gets no gradient (reference Triton path, :185-192)
+  use_triton=False  the gate is differentiated (reference gather path, :194,
+                    :71-74), so the selector MLPs learn through it.
+"""
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+import _bsa
+from triton_kernel import bsattn
+
+__all__ = ["BlockSparseSSA"]
+
+
+def _mlp_sel(d, sel_dim):
+    return nn.Sequential(nn.Linear(d, sel_dim), nn.GELU(), nn.Linear(sel_dim, sel_dim))
+
+
+class BlockSparseSSA(nn.Module):
+    """Content-dependent block-sparse attention with device-side selection."""
+
+    def __init__(self, d, h, block=64, topk=8, sel_dim=32, gate=False, causal=False,
+                 use_triton=False):
+        super().__init__()
+        self.h, self.dh = h, d // h
+        self.block, self.topk = block, topk
+        self.qkv = nn.Linear(d, 3 * d)
+        self.o = nn.Linear(d, d)
+        self.sel_q = _mlp_sel(d, sel_dim)
+        self.sel_k = _mlp_sel(d, sel_dim)
+        self.sel_dim = sel_dim
+        self.gate = gate
+        self.causal = causal
+        self.use_triton = use_triton
+        self.distill = False
+        self.last_hit = None
+        self.last_block_logits = None
+        self.distill_logits = None
+        self.distill_target = None
+
+    def forward(self, x, needle_pos=None):
+        B, L, D = x.shape
+        Bs = self.block
+        pad = (Bs - L % Bs) % Bs
+        if pad:
+            x = F.pad(x, (0, 0, 0, pad))
+        Lp = L + pad
+        nblk = Lp // Bs
+        H, dh = self.h, self.dh
+        q, k, v = self.qkv(x).chunk(3, -1)
+        q = q.view(B, Lp, H, dh).transpose(1, 2)
+        k = k.view(B, Lp, H, dh).transpose(1, 2)
+        v = v.view(B, Lp, H, dh).transpose(1, 2)
+
+        sqf, skf = self.sel_q(x), self.sel_k(x)                 # (B, Lp, s)
+        # exact device selection from block-pooled selector features
+        with torch.no_grad():
+            (sqp,) = _bsa.pool(sqf.detach().float().unsqueeze(1), Bs)
+            skm, skx = _bsa.pool(skf.detach().float().unsqueeze(1), Bs, mean=True, vmax=True)
+            sel, _, _ = _bsa.select(sqp, skm, skx, kind=_bsa.SCORE_MAXDOT2, layout=_bsa.SEL_SSA,
+                                    causal=self.causal, topk=self.topk)
+        sel = sel[:, 0]                                         # (B, nblk, kk) int32
+
+        # differentiable pooled features for the gate and the logged logits
+        sq = sqf.view(B, nblk, Bs, self.sel_dim).mean(2)
+        skv = skf.view(B, nblk, Bs, self.sel_dim)
+        sk_mean, sk_max = skv.mean(2), skv.max(2).values
+        self.last_block_logits = torch.maximum(sq[:, -1:] @ sk_mean.transpose(-1, -2),
+                                               sq[:, -1:] @ sk_max.transpose(-1, -2))[:, 0]
+        if self.distill:
+            raw = torch.maximum(sq @ sk_mean.transpose(-1, -2), sq @ sk_max.transpose(-1, -2))
+            att = (q @ k.transpose(-1, -2)) * dh ** -0.5
+            cm = torch.triu(torch.ones(Lp, Lp, dtype=torch.bool, device=x.device), 1)
+            att = att.masked_fill(cm, float("-inf")).softmax(-1)
+            am = att.view(B, H, nblk, Bs, nblk, Bs).sum(-1).mean(3)
+            self.distill_target = am.mean(1).detach()
+            ar = torch.arange(nblk, device=x.device)
+            self.distill_logits = raw.masked_fill((ar.view(nblk, 1) < ar.view(1, nblk)).unsqueeze(0), -1e9)
+
+        gate_bias = None
+        if self.gate:
+            idx = sel.long()
+            kk = idx.shape[-1]
+            flat = idx.view(B, nblk * kk, 1).expand(-1, -1, self.sel_dim)
+            gm = torch.gather(sk_mean, 1, flat).view(B, nblk, kk, self.sel_dim)
+            gx = torch.gather(sk_max, 1, flat).view(B, nblk, kk, self.sel_dim)
+            raw_sel = torch.maximum((sq.unsqueeze(2) * gm).sum(-1), (sq.unsqueeze(2) * gx).sum(-1))
+            gate_bias = F.logsigmoid(raw_sel.float())
+            if self.use_triton:
+                gate_bias = gate_bias.detach()
+        out = bsattn(q, k, v, sel, gate_bias, causal=self.causal,
+                     gate_grad=(self.gate and not self.use_triton))
+        out = out.reshape(B, H, Lp, dh).transpose(1, 2).reshape(B, Lp, D)[:, :L]
+        if needle_pos is not None:
+            chosen_last = sel[:, nblk - 1, :].long()
+            self.last_hit = (chosen_last == (needle_pos // Bs).unsqueeze(-1)).any(-1).float().mean().item()
+        return self.o(out)
