@@ -1,0 +1,162 @@
+"""Generates the golden fixtures in tests/golden/ by running the REFERENCE's own
+code (apoc/fused-block-sparse-attention, src/) on seeded inputs on the CPU.
+
+Run from the repo root, in a container where the reference is mounted:
+    python tests/golden/make_golden.py --ref /path/to/reference
+
+Fixtures (npz, fp32 / int32):
+  ssa_gather_*.npz    BlockSparseSSA gather path (src/ssa_model.py:121-201, _gather_and_attend
+                      :57-90): selection from a supplied raw score matrix, output and
+                      autograd gradients w.r.t. q, k, v.  The raw scores are exact
+                      products of small-integer features plus a j/1024 tie breaker, so
+                      the ranking is identical in any summation order.
+  triton_interp_*.npz the reference Triton kernel (src/triton_kernel.py) run by the Triton
+                      CPU interpreter (TRITON_INTERPRET=1): forward + backward with gate,
+                      causal and non-causal (duplicates in sel).
+  qwen_*.npz          qwen_blocksparse.blocksparse_forward with SelectMax / SelectAll / the
+                      all-blocks fast path (src/qwen_blocksparse.py:29-121), GQA, padded L.
+  rope.npz            transformers' apply_rotary_pos_emb (qwen3_5_moe) on bf16 inputs, and
+                      the cos/sin of Qwen3_5MoeTextRotaryEmbedding for text positions.
+"""
+import argparse
+import os
+import sys
+
+import numpy as np
+import torch
+
+OUT = os.path.dirname(os.path.abspath(__file__))
+
+
+def save(name, **arrs):
+    path = os.path.join(OUT, name)
+    out = {}
+    for k, v in arrs.items():
+        if isinstance(v, torch.Tensor):
+            v = v.detach().cpu()
+            v = v.float().numpy() if v.is_floating_point() else v.to(torch.int32).numpy()
+        out[k] = np.asarray(v)
+    np.savez_compressed(path, **out)
+    print("wrote", path, sum(a.nbytes for a in out.values()), "bytes")
+
+
+def ssa_gather_case(name, B, H, L, dh, bs, topk, causal, gate, seed):
+    import ssa_model
+    torch.manual_seed(seed)
+    d = H * dh
+    nblk = L // bs
+    m = ssa_model.BlockSparseSSA(d, H, block=bs, topk=topk, causal=causal, gate=gate)
+    m.eval()
+    qkv = torch.randn(B, L, 3 * d, requires_grad=True)
+    fa = torch.randint(-4, 5, (B, nblk, 16)).float()
+    fb = torch.randint(-4, 5, (B, nblk, 16)).float()
+    fa[..., 0] = 1.0
+    fb[..., 0] = torch.arange(nblk).float() / 1024.0
+    raw = fa @ fb.transpose(-1, -2)
+    del m.qkv
+    m.qkv = lambda x: qkv
+    del m.o
+    m.o = lambda x: x
+    m._scores = lambda x, B_, nblk_, Bs_: raw
+    captured = {}
+    orig = ssa_model._gather_and_attend
+
+    def spy(q, k, v, sel, *a, **kw):
+        captured["sel"] = sel.clone()
+        return orig(q, k, v, sel, *a, **kw)
+
+    ssa_model._gather_and_attend = spy
+    try:
+        out = m(torch.zeros(B, L, d))                   # (B, L, d)
+    finally:
+        ssa_model._gather_and_attend = orig
+    do = torch.randn_like(out)
+    (out * do).sum().backward()
+    g = qkv.grad.view(B, L, 3, H, dh)
+    qkv_v = qkv.detach().view(B, L, 3, H, dh)
+    to_bhld = lambda t: t.permute(0, 2, 1, 3).contiguous()
+    save(name, q=to_bhld(qkv_v[:, :, 0]), k=to_bhld(qkv_v[:, :, 1]), v=to_bhld(qkv_v[:, :, 2]),
+         fa=fa, fb=fb, sel=captured["sel"], o=to_bhld(out.detach().view(B, L, H, dh)),
+         do=to_bhld(do.view(B, L, H, dh)), dq=to_bhld(g[:, :, 0]), dk=to_bhld(g[:, :, 1]),
+         dv=to_bhld(g[:, :, 2]),
+         meta=np.array([B, H, L, dh, bs, topk, int(causal), int(gate)], np.int32))
+
+
+def triton_interp_case(name, B, H, L, dh, bs, kk, causal, seed):
+    os.environ["TRITON_INTERPRET"] = "1"
+    import triton_kernel
+    torch.manual_seed(seed)
+    nblk = L // bs
+    q, k, v, do = (torch.randn(B, H, L, dh) for _ in range(4))
+    own = torch.arange(nblk).view(1, nblk, 1).expand(B, nblk, 1)
+    rnd = torch.randint(0, nblk, (B, nblk, kk - 1))
+    sel = torch.cat([own, rnd], -1).to(torch.int32)
+    gate = torch.randn(B, nblk, kk) * 0.5
+    o = triton_kernel.bsattn_forward(q, k, v, sel, gate, causal=causal)
+    dq, dk, dv = triton_kernel.bsattn_backward(q, k, v, sel, o, do, gate, causal=causal)
+    save(name, q=q, k=k, v=v, do=do, sel=sel, gate=gate, o=o, dq=dq, dk=dk, dv=dv,
+         meta=np.array([B, H, L, dh, bs, kk, int(causal)], np.int32))
+
+
+def qwen_case(name, B, Hq, Hkv, L, d, bs, topk, seed, selector):
+    import qwen_blocksparse as qb
+    torch.manual_seed(seed)
+    q = torch.randn(B, Hq, L, d)
+    k = torch.randn(B, Hkv, L, d)
+    v = torch.randn(B, Hkv, L, d)
+    if selector == "max":
+        S = qb.SelectMax(topk, bs, sink=True)
+        idx = S.select(q, k)
+        out = qb.blocksparse_forward(q, k, v, selector=S, topk=topk, bs=bs, causal=True, q_chunk=3)
+    elif selector == "all":
+        S = qb.SelectAll(bs)
+        idx = S.select(q, k)
+        out = qb.blocksparse_forward(q, k, v, selector=S, topk=0, bs=bs, causal=True, q_chunk=3)
+    else:  # all-blocks fast path (SDPA)
+        idx = torch.zeros(1, dtype=torch.int32)
+        out = qb.blocksparse_forward(q, k, v, selector=None, topk=10 ** 6, bs=bs, causal=True)
+    save(name, q=q, k=k, v=v, idx=idx, o=out, meta=np.array([B, Hq, Hkv, L, d, bs, topk], np.int32))
+
+
+def rope_case(name):
+    import transformers.models.qwen3_5_moe.modeling_qwen3_5_moe as M
+    from transformers.models.qwen3_5_moe.configuration_qwen3_5_moe import Qwen3_5MoeTextConfig
+    torch.manual_seed(7)
+    B, Hq, Hkv, L, D, rot, theta = 1, 4, 2, 96, 256, 64, 1e7
+    cfg = Qwen3_5MoeTextConfig(head_dim=D, hidden_size=512, num_attention_heads=Hq,
+                               num_key_value_heads=Hkv,
+                               rope_parameters={"rope_type": "default", "rope_theta": theta,
+                                                "partial_rotary_factor": rot / D,
+                                                "mrope_section": [11, 11, 10]})
+    emb = M.Qwen3_5MoeTextRotaryEmbedding(cfg)
+    x = torch.zeros(B, L, 8, dtype=torch.bfloat16)
+    cos, sin = emb(x, torch.arange(L).view(1, L))      # (B, L, rot) bf16
+    q = torch.randn(B, Hq, L, D).to(torch.bfloat16)
+    k = torch.randn(B, Hkv, L, D).to(torch.bfloat16)
+    qe, ke = M.apply_rotary_pos_emb(q, k, cos, sin)
+    save(name, q=q.float(), k=k.float(), cos=cos.float(), sin=sin.float(), qe=qe.float(),
+         ke=ke.float(), meta=np.array([B, Hq, Hkv, L, D, rot], np.int32), theta=np.array([theta]))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--ref", default=os.environ.get("BSA_REFERENCE", ""))
+    a = ap.parse_args()
+    src = os.path.join(a.ref, "src")
+    if not os.path.isdir(src):
+        sys.exit("reference src/ not found; pass --ref")
+    sys.path.insert(0, src)
+    torch.set_num_threads(min(8, os.cpu_count() or 1))
+    ssa_gather_case("ssa_gather_causal_gate.npz", 1, 2, 512, 64, 64, 3, True, True, 1)
+    ssa_gather_case("ssa_gather_causal.npz", 2, 1, 256, 64, 32, 4, True, False, 2)
+    ssa_gather_case("ssa_gather_noncausal_gate.npz", 1, 2, 256, 64, 64, 2, False, True, 3)
+    triton_interp_case("triton_interp_causal.npz", 1, 2, 256, 64, 64, 4, True, 4)
+    triton_interp_case("triton_interp_noncausal.npz", 1, 2, 256, 64, 64, 4, False, 5)
+    qwen_case("qwen_selectmax.npz", 1, 4, 2, 448, 64, 64, 3, 6, "max")
+    qwen_case("qwen_selectall.npz", 1, 4, 2, 200, 64, 32, 0, 8, "all")
+    qwen_case("qwen_fastpath.npz", 1, 4, 2, 256, 64, 64, 0, 9, "fast")
+    rope_case("rope.npz")
+
+
+if __name__ == "__main__":
+    main()
