@@ -1,0 +1,175 @@
+"""GPU parity of the attention kernels (through the C ABI) against the float64
+oracle and the reference's golden outputs.
+
+Tolerances: bf16/f16 — max-abs 2e-2 and max-abs / max|ref| 1e-2 (the north-star
+bound); fp32 — max-abs 1e-5 (gradients 2e-5, the golden's own fp32 noise)."""
+import pytest
+import torch
+import torch.nn.functional as F
+
+from conftest import golden
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+BF16_ABS, BF16_REL, F32_ABS = 2e-2, 1e-2, 1e-5
+
+
+def _cmp(got, ref, dtype, what, abs_tol=None):
+    got = got.detach().double().cpu()
+    ref = torch.as_tensor(ref).double().cpu()
+    err = (got - ref).abs().max().item()
+    if dtype == torch.float32:
+        tol = F32_ABS if abs_tol is None else abs_tol
+        assert err <= tol, "%s: max-abs %.3g > %.3g" % (what, err, tol)
+    else:
+        rel = err / (ref.abs().max().item() + 1e-12)
+        assert err <= (BF16_ABS if abs_tol is None else abs_tol) and rel <= BF16_REL, \
+            "%s: max-abs %.3g rel %.3g" % (what, err, rel)
+
+
+def _dev(g, names, dtype, dev):
+    return [torch.from_numpy(g[n]).to(dev, dtype) for n in names]
+
+
+@pytest.mark.parametrize("name", ["triton_interp_causal.npz", "triton_interp_noncausal.npz"])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_bsattn_matches_reference_triton_kernel(cuda, name, dtype):
+    import triton_kernel as tk
+    g = golden(name)
+    B, H, L, dh, bs, kk, causal = [int(x) for x in g["meta"]]
+    q, k, v, do = _dev(g, ["q", "k", "v", "do"], dtype, cuda)
+    sel = torch.from_numpy(g["sel"]).to(cuda)
+    gate = torch.from_numpy(g["gate"]).to(cuda)
+    o = tk.bsattn_forward(q, k, v, sel, gate, causal=bool(causal))
+    dq, dk, dv = tk.bsattn_backward(q, k, v, sel, o, do, gate, causal=bool(causal))
+    torch.cuda.synchronize()
+    if dtype == torch.float32:
+        refs = (g["o"], g["dq"], g["dk"], g["dv"])
+    else:   # low precision: the oracle on the same rounded inputs
+        c = [t.cpu() for t in (q, k, v, sel, do, gate)]
+        ro = O.attention(c[0], c[1], c[2], c[3], c[5], bs=bs, causal=bool(causal))
+        rq, rk, rv, _ = O.attention_grads(c[0], c[1], c[2], c[3], c[4], c[5], bs=bs, causal=bool(causal))
+        refs = (ro, rq, rk, rv)
+    for got, ref, w in zip((o, dq, dk, dv), refs, "o dq dk dv".split()):
+        tol = (1e-5 if w == "o" else 2e-5) if dtype == torch.float32 else None
+        _cmp(got, ref, dtype, w, abs_tol=tol)
+
+
+@pytest.mark.parametrize("name", ["ssa_gather_causal_gate.npz", "ssa_gather_causal.npz",
+                                  "ssa_gather_noncausal_gate.npz"])
+def test_bsattn_matches_reference_gather_path_fp32(cuda, name):
+    import triton_kernel as tk
+    g = golden(name)
+    B, H, L, dh, bs, topk, causal, gate = [int(x) for x in g["meta"]]
+    q, k, v, do = _dev(g, ["q", "k", "v", "do"], torch.float32, cuda)
+    sel = torch.from_numpy(g["sel"]).to(cuda)
+    gt = None
+    if gate:
+        raw = torch.from_numpy(g["fa"]) @ torch.from_numpy(g["fb"]).transpose(-1, -2)
+        gt = F.logsigmoid(torch.gather(raw, -1, sel.cpu().long())).to(cuda)
+    for t in (q, k, v):
+        t.requires_grad_(True)
+    o = tk.bsattn(q, k, v, sel, gt, causal=bool(causal))
+    (o * do).sum().backward()
+    _cmp(o, g["o"], torch.float32, "o")
+    _cmp(q.grad, g["dq"], torch.float32, "dq", 2e-5)
+    _cmp(k.grad, g["dk"], torch.float32, "dk", 2e-5)
+    _cmp(v.grad, g["dv"], torch.float32, "dv", 2e-5)
+
+
+def _random_case(B, H, L, D, bs, kk, dtype, dev, seed, shared=False):
+    gen = torch.Generator().manual_seed(seed)
+    nblk = L // bs
+    q, k, v, do = (torch.randn(B, H, L, D, generator=gen) for _ in range(4))
+    shape = (B, nblk, kk) if shared else (B, H, nblk, kk)
+    sel = torch.randint(0, nblk, shape, generator=gen)
+    sel[..., 0] = torch.arange(nblk).view(*([1] * (len(shape) - 2)), nblk)
+    gate = torch.randn(shape, generator=gen) * 0.3
+    return [t.to(dev, dtype) for t in (q, k, v, do)] + [sel.to(dev, torch.int32), gate.to(dev)]
+
+
+@pytest.mark.parametrize("bs,D", [(16, 64), (32, 64), (64, 64), (128, 64), (64, 128)])
+@pytest.mark.parametrize("shared", [False, True])
+def test_bf16_shapes_vs_oracle(cuda, bs, D, shared):
+    import triton_kernel as tk
+    B, H, L, kk = 2, 2, 1024, 5
+    q, k, v, do, sel, gate = _random_case(B, H, L, D, bs, kk, torch.bfloat16, cuda, bs + D, shared)
+    for t in (q, k, v):
+        t.requires_grad_(True)
+    o = tk.bsattn(q, k, v, sel, gate, causal=True)
+    (o.float() * do.float()).sum().backward()
+    qc, kc, vc, dc = (t.detach().cpu() for t in (q, k, v, do))
+    ro = O.attention(qc, kc, vc, sel.cpu(), gate.cpu(), bs=bs, causal=True)
+    rq, rk, rv, _ = O.attention_grads(qc, kc, vc, sel.cpu(), dc, gate.cpu(), bs=bs, causal=True)
+    _cmp(o, ro, torch.bfloat16, "o")
+    _cmp(q.grad, rq, torch.bfloat16, "dq")
+    _cmp(k.grad, rk, torch.bfloat16, "dk")
+    _cmp(v.grad, rv, torch.bfloat16, "dv")
+
+
+def test_gate_gradient_vs_oracle(cuda):
+    import triton_kernel as tk
+    B, H, L, D, bs, kk = 1, 2, 512, 64, 64, 4
+    q, k, v, do, sel, gate = _random_case(B, H, L, D, bs, kk, torch.float32, cuda, 11, shared=True)
+    gate.requires_grad_(True)
+    o = tk.bsattn(q, k, v, sel, gate, causal=True, gate_grad=True)
+    (o * do).sum().backward()
+    _, _, _, rg = O.attention_grads(q.cpu(), k.cpu(), v.cpu(), sel.cpu(), do.cpu(), gate.detach().cpu(),
+                                    bs=bs, causal=True, want_dgate=True)
+    _cmp(gate.grad, rg, torch.float32, "dgate", 1e-4)
+
+
+def test_backward_is_deterministic_with_hub_blocks(cuda):
+    """Every query block selects blocks 0 and 1, so those bins span many dK/dV chunks."""
+    import triton_kernel as tk
+    B, H, L, D, bs, kk = 1, 2, 8192, 64, 64, 6
+    q, k, v, do, sel, gate = _random_case(B, H, L, D, bs, kk, torch.bfloat16, cuda, 5)
+    sel[..., 1] = 0
+    sel[..., 2] = 1
+    r1 = tk.bsattn_backward(q, k, v, sel, None, do, gate, causal=True)
+    r2 = tk.bsattn_backward(q, k, v, sel, None, do, gate, causal=True)
+    for a, b in zip(r1, r2):
+        assert torch.equal(a, b)
+    qc, kc, vc, dc = (t.cpu() for t in (q, k, v, do))
+    rq, rk, rv, _ = O.attention_grads(qc, kc, vc, sel.cpu(), dc, gate.cpu(), bs=bs, causal=True)
+    _cmp(r1[0], rq, torch.bfloat16, "dq")
+    _cmp(r1[1], rk, torch.bfloat16, "dk")
+    _cmp(r1[2], rv, torch.bfloat16, "dv")
+
+
+def test_strided_inputs_read_in_place(cuda):
+    """q/k/v as transposed views of a (B, L, 3, H, D) projection (no copies)."""
+    import triton_kernel as tk
+    B, H, L, D, bs, kk = 1, 4, 1024, 64, 64, 4
+    gen = torch.Generator().manual_seed(3)
+    qkv = torch.randn(B, L, 3, H, D, generator=gen).to(cuda, torch.bfloat16)
+    q, k, v = (qkv[:, :, i].transpose(1, 2) for i in range(3))
+    sel = _random_case(B, H, L, D, bs, kk, torch.bfloat16, cuda, 4, shared=True)[4]
+    o = tk.bsattn_forward(q, k, v, sel, None, causal=True)
+    ro = O.attention(q.cpu(), k.cpu(), v.cpu(), sel.cpu(), bs=bs, causal=True)
+    _cmp(o, ro, torch.bfloat16, "o")
+
+
+def test_bad_index_sets_status_word(cuda):
+    import _bsa
+    import triton_kernel as tk
+    B, H, L, D, bs, kk = 1, 1, 256, 64, 64, 3
+    q, k, v, do, sel, gate = _random_case(B, H, L, D, bs, kk, torch.bfloat16, cuda, 9, shared=True)
+    _bsa.check_status(cuda)
+    sel[0, 2, 1] = 99
+    tk.bsattn_forward(q, k, v, sel, None, causal=True)
+    with pytest.raises(_bsa.BsaError) as e:
+        _bsa.check_status(cuda)
+    assert e.value.status == _bsa.ERR_INDEX
+
+
+def test_module_drop_in_runs_and_trains(cuda):
+    import ssa_model
+    torch.manual_seed(0)
+    m = ssa_model.BlockSparseSSA(256, 4, block=64, topk=4, causal=True, gate=True).to(cuda)
+    x = torch.randn(2, 1000, 256, device=cuda)
+    y = m(x, needle_pos=torch.tensor([5, 700], device=cuda))
+    y.sum().backward()
+    assert y.shape == x.shape and torch.isfinite(y).all()
+    assert m.sel_q[0].weight.grad is not None and m.sel_q[0].weight.grad.abs().sum() > 0
