@@ -424,7 +424,8 @@ struct DkvCfg : TileCfg<BS, D> {
   static constexpr int NST = 2;
   static constexpr bool KREG = D <= 64;  // K/V fragments kept in registers
   static constexpr int ROWB = B_::KC * 4;  // bytes of one lse / Dvec chunk
-  static constexpr int STAGE = 2 * B_::CH + 2 * ROWB;
+  // stage stride rounded to 1024 B: swizzled TMA destinations need 1024-B alignment
+  static constexpr int STAGE = (2 * B_::CH + 2 * ROWB + 1023) / 1024 * 1024;
   static constexpr int SMEM = 1024 + 2 * B_::TILE + NST * STAGE;
 };
 
@@ -479,7 +480,7 @@ __global__ void __launch_bounds__(TileCfg<BS, D>::NT)
     const int qblk = e / p.kk;
     const int h = hk * p.grp + g;
     uint8_t *base = sST + st * Cfg::STAGE;
-    mbar_expect_tx(&bar[st], Cfg::STAGE);
+    mbar_expect_tx(&bar[st], 2 * Cfg::CH + 2 * Cfg::ROWB);
     const int row = qblk * p.bs + c * KC;
 #pragma unroll
     for (int r = 0; r < D / 64; ++r) {
