@@ -144,5 +144,5 @@ def test_qwen_variant_bf16_vs_oracle(cuda):
     sel, _, _ = O.select(qp, kmax, kmin, kind=O.SCORE_QUEST, layout=O.SEL_FINISH, topk=topk, sink=True)
     ref = O.attention(qr, kr, v, torch.from_numpy(sel), bs=bs, causal=True, mask_mode=O.MASK_TOKEN)
     ref = ref.transpose(1, 2).reshape(B, L, Hq * D) * torch.sigmoid(gate.double())
-    err = (out.double().cpu() - ref).abs().max().item()
-    assert err <= 2e-2 and err / ref.abs().max().item() <= 1e-2, err
+    diff = (out.double().cpu() - ref).abs()
+    assert (diff <= 2e-2 + 1e-2 * ref.abs()).all(), diff.max().item()
