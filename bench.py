@@ -1,0 +1,394 @@
+"""Benchmark of the fused block-sparse attention hot path (selection + forward +
+backward) on B200, following the driver contract.
+
+Workload (BASELINE config 3a, the north star): B=1, H=8, N=262144, D=64,
+block 64, top-16 content blocks + the own block (kk=17), causal, bf16.
+One step = mean-pooled block selection + fused forward + fused backward over
+synthetic N(0,1) inputs resident in HBM.  With --gpus N the heads are sharded
+over the ranks (H/N heads each, no collective: every head is independent), so
+the total work is fixed ("strong" scaling); value = tokens of the whole job
+per second, timed on the device as the max over ranks.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+--impl reference times the CPU restatement of the reference's gather path
+(oracle/, the reference is Python and cannot be installed on the GPU box) on
+a bounded sample of the same workload, with all host threads.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "fused-block-sparse-attention_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+METRIC = "fwd+bwd tokens/s at 262k tok (selection+forward+backward)"
+UNIT = "tokens/s"
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d["hbm_gbs"], d["bf16_tflops"], d.get("bf16_tflops_sustained", d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def workload(a):
+    H = 8
+    cfg = dict(B=1, H=H, N=a.n, D=64, bs=64, topk=16, dtype="bf16", causal=True)
+    cfg["nblk"] = cfg["N"] // cfg["bs"]
+    cfg["kk"] = cfg["topk"] + 1
+    return cfg
+
+
+def flops(cfg, heads):
+    """Algorithmic FLOPs (SURVEY 8d convention): fwd 4*B*H*N*kk*bs*D, bwd 2.5x fwd,
+    selection 2*D per causal block pair plus the two pooling passes (negligible)."""
+    fwd = 4.0 * cfg["B"] * heads * cfg["N"] * cfg["kk"] * cfg["bs"] * cfg["D"]
+    nb = cfg["nblk"]
+    sel = 2.0 * cfg["D"] * cfg["B"] * heads * nb * (nb - 1) / 2
+    return fwd, 2.5 * fwd, sel
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples nvidia-smi clocks / throttle reasons while the timed loop runs."""
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", "clocks_%d.csv" % index)
+
+    def __enter__(self):
+        os.makedirs(os.path.dirname(self.path), exist_ok=True)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), "--query-gpu=" + q,
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            self.proc.wait()
+            self.f.close()
+
+    def summary(self):
+        if self.proc is None or not os.path.exists(self.path):
+            return None
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- our arm
+def make_inputs(cfg, heads, h0, dev):
+    """Seeded N(0,1) q, k, v, dO of the local heads (one generator per head, so the
+    data of a head does not depend on the rank count)."""
+    B, N, D = cfg["B"], cfg["N"], cfg["D"]
+    out = []
+    for name in range(4):
+        t = torch.empty(B, heads, N, D, dtype=torch.bfloat16, device=dev)
+        for j in range(heads):
+            g = torch.Generator(device=dev).manual_seed(1000 * (h0 + j) + name)
+            t[:, j].copy_(torch.randn(B, N, D, generator=g, device=dev))
+        out.append(t)
+    return out
+
+
+def step(cfg, q, k, v, do, ph=None):
+    """selection + forward + backward through the C ABI; ph: events per phase."""
+    import _bsa
+    import selection
+    bs, causal = cfg["bs"], cfg["causal"]
+    if ph:
+        ph[0].record()
+    sel, _, _ = selection.select_meanpool(q, k, bs=bs, topk=cfg["topk"], causal=causal)
+    if ph:
+        ph[1].record()
+    o, lse = _bsa.attn_fwd(q, k, v, sel, None, bs=bs, causal=causal)
+    if ph:
+        ph[2].record()
+    dq, dk, dv, _ = _bsa.attn_bwd(q, k, v, o, do, sel, lse, None, bs=bs, causal=causal)
+    if ph:
+        ph[3].record()
+    return o, dq, dk, dv
+
+
+def count_launches(cfg, q, k, v, do):
+    """Kernels of this library launched by one step (torch profiler / CUPTI)."""
+    from torch.profiler import ProfilerActivity, profile
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        step(cfg, q, k, v, do)
+        torch.cuda.synchronize()
+    names = [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+    ours = [n for n in names if "bsa::" in n or "cub::" in n or "bsa" in n.split("(")[0]]
+    return len(ours), sorted(set(n.split("(")[0][:60] for n in ours))
+
+
+def e2e_run(cfg, heads, q, k, v, do, steps, warmup):
+    """Same step through the public drop-in API with host buffers: pinned H2D of
+    q, k, v, dO, then selection + bsattn forward/backward, then D2H of o, dq, dk, dv."""
+    import selection
+    import triton_kernel as tk
+    hs = [t.cpu().pin_memory() for t in (q, k, v, do)]
+    outs = [torch.empty_like(h).pin_memory() for h in hs]
+    dev_in = [torch.empty_like(t) for t in (q, k, v, do)]
+    s = torch.cuda.current_stream()
+
+    def one():
+        for d, h in zip(dev_in, hs):
+            d.copy_(h, non_blocking=True)
+        qd, kd, vd, dod = dev_in
+        sel, _, _ = selection.select_meanpool(qd, kd, bs=cfg["bs"], topk=cfg["topk"])
+        qd.requires_grad_(True)
+        kd.requires_grad_(True)
+        vd.requires_grad_(True)
+        o = tk.bsattn(qd, kd, vd, sel, None, causal=cfg["causal"])
+        o.backward(dod)
+        for h, d in zip(outs, (o, qd.grad, kd.grad, vd.grad)):
+            h.copy_(d.detach(), non_blocking=True)
+        for t in (qd, kd, vd):
+            t.grad = None
+            t.requires_grad_(False)
+
+    for _ in range(warmup):
+        one()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(steps):
+        one()
+    e1.record(s)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    nbytes = sum(t.numel() * t.element_size() for t in hs)
+    return ms, nbytes, sum(t.numel() * t.element_size() for t in outs)
+
+
+def run_ours(a):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+    cfg = workload(a)
+    if cfg["H"] % world:
+        raise SystemExit("H=%d heads cannot be split over %d ranks" % (cfg["H"], world))
+    heads = cfg["H"] // world
+    h0 = rank * heads
+    q, k, v, do = make_inputs(cfg, heads, h0, dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)   # 256 MB > 126 MB L2
+
+    for _ in range(a.warmup):
+        step(cfg, q, k, v, do)
+    torch.cuda.synchronize()
+    nlaunch, kernel_names = count_launches(cfg, q, k, v, do)
+
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(a.steps)]
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        for i in range(a.steps):
+            flush.zero_()                          # L2 flush between timed steps
+            step(cfg, q, k, v, do, evs[i])
+        torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ph = [[e[j].elapsed_time(e[j + 1]) for e in evs] for j in range(3)]
+    ms_sel, ms_fwd, ms_bwd = (statistics.mean(x) for x in ph)
+    ms_step = ms_sel + ms_fwd + ms_bwd
+    vals = torch.tensor([ms_step, ms_sel, ms_fwd, ms_bwd], device=dev)
+    if dist:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    ms_step, ms_sel, ms_fwd, ms_bwd = vals.tolist()
+
+    e2e_ms, h2d, d2h = e2e_run(cfg, heads, q, k, v, do, max(2, a.steps // 4), 1)
+    ev = torch.tensor([e2e_ms], device=dev)
+    if dist:
+        dist.all_reduce(ev, op=dist.ReduceOp.MAX)
+    e2e_ms = ev.item()
+
+    if rank == 0:
+        hbm, tf_burst, tf_sus, src = load_peaks()
+        f_fwd, f_bwd, f_sel = flops(cfg, heads)
+        tokens = cfg["B"] * cfg["N"]
+        phases = {}
+        for name, ms, fl in (("select", ms_sel, f_sel), ("attn_fwd", ms_fwd, f_fwd),
+                             ("attn_bwd", ms_bwd, f_bwd)):
+            phases[name] = {"ms": round(ms, 4), "tflops": round(fl / ms / 1e9, 1),
+                            "frac_tensor": round(fl / ms / 1e9 / tf_sus, 4)}
+        dom = max(phases, key=lambda n: phases[n]["ms"])
+        dom_fl = {"select": f_sel, "attn_fwd": f_fwd, "attn_bwd": f_bwd}[dom]
+        achieved = dom_fl / (phases[dom]["ms"] * 1e-3) / 1e12
+        line = {
+            "metric": METRIC, "value": round(tokens / (ms_step * 1e-3), 1), "unit": UNIT,
+            "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms_step, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic N(0,1), seeded",
+            "config": {"workload": "BASELINE config 3a: selection+fwd+bwd, B1 H8 N%d D64 block64 "
+                                   "top16 (+own) causal" % cfg["N"],
+                       "B": cfg["B"], "H": cfg["H"], "N": cfg["N"], "D": cfg["D"], "block": cfg["bs"],
+                       "kk": cfg["kk"], "parallelism": "heads sharded %d/rank" % heads,
+                       "l2": "256 MB buffer written between timed steps; inputs %.0f MB per rank"
+                             % (4 * q.numel() * 2 / 1e6)},
+            "roofline": {"kernel": dom, "bound": "tensor", "achieved": round(achieved, 2),
+                         "peak": tf_sus, "unit": "TFLOP/s", "frac": round(achieved / tf_sus, 4),
+                         "peak_source": "%s bf16_tflops_sustained" % src, "traffic": None},
+            "phases": phases,
+            "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 1), "unit": UNIT,
+                    "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d * world,
+                    "d2h_bytes_per_step": d2h * world},
+            "gpu_launches": nlaunch * a.steps,
+            "launches_per_step": nlaunch,
+            "clocks": clk.summary(),
+        }
+        if world == 1 and not a.no_cpu:
+            line["cpu_baseline"] = cpu_baseline(cfg, a.cpu_sample)
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------- CPU baseline
+class CpuSample:
+    """The reference's CPU gather path (restated in oracle/, fp32, all host threads)
+    on a bounded sample: S query blocks [nblk-S, nblk) of every head, with the
+    reference's own selection algorithm for those rows (score against every key
+    block, mask, top-k: src/ssa_model.py:151-162) and the gather attention forward
+    + autograd backward (src/ssa_model.py:57-90).  Cost per query block is
+    independent of its position, so tokens/s = S*bs / sample time."""
+
+    def __init__(self, cfg, heads, S):
+        from oracle import oracle as O
+        self.O = O
+        torch.set_num_threads(os.cpu_count() or 1)
+        self.cfg, self.heads, self.S = cfg, heads, S
+        B, N, D = cfg["B"], cfg["N"], cfg["D"]
+        g = torch.Generator().manual_seed(7)
+        self.q, self.k, self.v, self.do = (
+            torch.randn(B, heads, N, D, generator=g).to(torch.bfloat16).float() for _ in range(4))
+
+    def run(self):
+        cfg, S = self.cfg, self.S
+        bs, nblk = cfg["bs"], cfg["nblk"]
+        i0 = nblk - S
+        B, H, N, D = self.q.shape
+        t0 = time.perf_counter()
+        qp = self.q[:, :, i0 * bs:].reshape(B, H, S, bs, D).mean(3)
+        kp = self.k.reshape(B, H, nblk, bs, D).mean(3)
+        raw = qp @ kp.transpose(-1, -2)                          # (B,H,S,nblk)
+        rows = torch.arange(i0, nblk).view(S, 1)
+        cols = torch.arange(nblk).view(1, nblk)
+        raw = raw.masked_fill((cols >= rows), float("-inf"))     # exclude own + future
+        top = raw.topk(cfg["topk"], dim=-1).indices
+        own = rows.view(1, 1, S, 1).expand(B, H, S, 1)
+        sel_rows = torch.cat([own, top], -1)
+        sel = torch.zeros(B, H, nblk, cfg["kk"], dtype=torch.long)
+        sel[:, :, i0:] = sel_rows
+        self.O.attention_grads(self.q, self.k, self.v, sel, self.do, None, bs=bs, causal=True,
+                               dtype=torch.float32, qblk_range=(i0, nblk))
+        return time.perf_counter() - t0
+
+    def tokens(self):
+        return self.cfg["B"] * self.S * self.cfg["bs"]
+
+
+def cpu_baseline(cfg, S):
+    smp = CpuSample(cfg, cfg["H"], S)
+    smp.run()                                                     # warm-up
+    t = smp.run()
+    return {"value": round(smp.tokens() / t, 1), "unit": UNIT, "cores": torch.get_num_threads(),
+            "kind": "port",
+            "sample": "query blocks %d..%d of all %d heads at N=%d (%d tokens), selection + gather "
+                      "fwd + autograd bwd in fp32, %.2f s" % (cfg["nblk"] - S, cfg["nblk"], cfg["H"],
+                                                               cfg["N"], smp.tokens(), t)}
+
+
+def run_reference(a):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cfg = workload(a)
+    smp = CpuSample(cfg, cfg["H"], a.cpu_sample)
+    for _ in range(a.warmup):
+        smp.run()
+    ts = [smp.run() for _ in range(a.steps)]
+    t = statistics.mean(ts)
+    value = smp.tokens() / t
+    cores = torch.get_num_threads()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 1), "unit": UNIT,
+        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": a.steps, "warmup": a.warmup,
+        "ms_per_step": round(cfg["B"] * cfg["N"] / value * 1e3, 2), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32 (bf16-rounded inputs)",
+        "data": "synthetic N(0,1), seeded",
+        "config": {"workload": "BASELINE config 3a: selection+fwd+bwd, B1 H8 N%d D64 block64 "
+                               "top16 (+own) causal" % cfg["N"], "N": cfg["N"], "block": cfg["bs"],
+                   "kk": cfg["kk"]},
+        "cpu_baseline": {"value": round(value, 1), "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": "%d query blocks x %d heads per step (%d tokens), mean of %d "
+                                   "steps" % (a.cpu_sample, cfg["H"], smp.tokens(), a.steps)},
+        "e2e": {"value": round(value, 1), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--n", type=int, default=262144, help="sequence length (default 262144)")
+    ap.add_argument("--cpu-sample", type=int, default=64, help="query blocks in the CPU sample")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    a = ap.parse_args()
+    if a.warmup < 3:
+        a.warmup = 3
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_ours(a)
+
+
+if __name__ == "__main__":
+    main()
