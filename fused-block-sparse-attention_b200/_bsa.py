@@ -98,6 +98,7 @@ SYMBOLS = {
     "bsa_csr_workspace": (ctypes.c_size_t, [ctypes.POINTER(CsrArgs)]),
     "bsa_sel_csr": (ctypes.c_int, [ctypes.POINTER(CsrArgs), ctypes.c_void_p, ctypes.c_size_t,
                                    ctypes.c_void_p]),
+    "bsa_sel_csr_noalloc": (ctypes.c_int, [ctypes.POINTER(CsrArgs), ctypes.c_void_p]),
     "bsa_rope": (ctypes.c_int, [ctypes.POINTER(RopeArgs), ctypes.c_void_p]),
     "bsa_status_decode": (ctypes.c_int, [ctypes.c_int32]),
     "bsa_last_error": (ctypes.c_char_p, []),

@@ -182,6 +182,16 @@ size_t bsa_csr_workspace(const bsa_csr_args *a);
 bsa_status bsa_sel_csr(const bsa_csr_args *a, void *workspace, size_t workspace_bytes,
                        bsa_stream_t stream);
 
+/* The same CSR transpose for callers that cannot allocate device memory (a
+ * locked or exhausted memory pool, a host runtime that owns every device
+ * allocation, a loop that must not enter the allocator).  No counterpart in the
+ * reference.  Its scratch is a fixed 16 MiB device array inside the library
+ * (held by every GPU that loads it until exit); selections needing more are
+ * rejected with BSA_ERR_UNSUPPORTED.  The first call on a device resolves the
+ * array's address and should precede any stream capture; calls share the array,
+ * so calls that overlap on the GPU race.  Allocates nothing. */
+bsa_status bsa_sel_csr_noalloc(const bsa_csr_args *a, bsa_stream_t stream);
+
 /* Partial rotary embedding with the arithmetic of transformers'
  * apply_rotary_pos_emb (qwen3_5_moe, v5.5.0): on the first `rot` dims,
  * y = x*cos + rotate_half(x)*sin with each product and the sum rounded to the
