@@ -1,0 +1,344 @@
+// Block-sparse attention forward on the 5th-generation tensor cores (tcgen05,
+// accumulators in tensor memory) for block 64, head dim 64.
+//
+// One CTA computes two adjacent query blocks (tiles A and B) of one head.  A
+// 64-row UMMA accumulator occupies TMEM lanes 0-15 of each 32-lane quadrant,
+// so tile B's accumulators are placed at lane offset 16: every one of the 128
+// softmax threads then owns one full query row (no shuffles for row max / sum).
+//
+// Warp roles (192 threads):
+//   warps 0-3  softmax: TMEM -> registers (32x32b loads), scale, gate, masks,
+//              lazy-rescaled online softmax, P (bf16) -> shared memory in the
+//              128B-swizzled K-major layout the MMA reads, final O / l.
+//   warp 4     TMA producer: Q tiles once, then K and V blocks of both tiles
+//              per step into a 2-deep ring.
+//   warp 5     TMEM allocation (256 columns) and the single MMA-issuing thread:
+//              S_j = Q K_j^T into a double-buffered TMEM S, PV_{j-1} = P V into
+//              the TMEM O accumulator, completions signalled by tcgen05.commit.
+// TMEM columns: S buffers [0,64) and [64,128), O [128,192).
+//
+// The running max is only raised (and O, l rescaled) when a row's new maximum
+// exceeds the one in use by more than 2^8, so the rescale of O in TMEM is rare;
+// the final O / l uses the same maximum as every P, so the result is exact.
+#include <type_traits>
+
+#include "bsa_attn.cuh"
+#include "bsa_host.h"
+#include "bsa_tc05.cuh"
+
+namespace bsa {
+
+namespace {
+constexpr int F5_BS = 64, F5_D = 64, F5_NST = 2;
+constexpr int F5_TILE = F5_BS * F5_D * 2;  // 8 KB
+constexpr int F5_SMEM = 1024 + 2 * F5_TILE + F5_NST * 4 * F5_TILE + 2 * F5_TILE;
+constexpr uint32_t F5_TMEM_COLS = 256;
+constexpr int F5_SCOL0 = 0, F5_OCOL = 128;
+constexpr float F5_RESCALE = 8.f;  // log2 units
+}  // namespace
+
+template <typename T>
+__global__ void __launch_bounds__(192, 1)
+    attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tq,
+                          const __grid_constant__ CUtensorMap tk,
+                          const __grid_constant__ CUtensorMap tv, const int perm_q,
+                          const int perm_k, const int perm_v, const AttnParams p) {
+  constexpr bool kBF16 = sizeof(T) == 2 && std::is_same<T, __nv_bfloat16>::value;
+  constexpr uint32_t IDESC_S = tc05::idesc_f16(kBF16, 64, 64, false);
+  constexpr uint32_t IDESC_PV = tc05::idesc_f16(kBF16, 64, F5_D, true);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~uintptr_t(1023));
+  uint8_t *sQ = smem;                          // tile t at sQ + t*TILE
+  uint8_t *sKV = smem + 2 * F5_TILE;           // (stage, tile): K, V
+  uint8_t *sP = sKV + F5_NST * 4 * F5_TILE;    // tile t at sP + t*TILE
+  __shared__ __align__(8) uint64_t bar_q, kv_full[F5_NST], kv_empty[F5_NST], s_full[2],
+      s_empty[2], p_full, o_full;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ int s_item[2][kMaxKK];  // (kb << 3) | kind of the j-th live slot
+  __shared__ int s_islot[2][kMaxKK];
+  __shared__ int s_n[2];
+
+  // ---- CTA coordinates: (b, kv head, query-block pair, head in group)
+  const int npairs = (p.nblk + 1) >> 1;
+  long long id = blockIdx.x;
+  const int gi = (int)(id % p.grp);
+  id /= p.grp;
+  const int pair = (int)(id % npairs);
+  id /= npairs;
+  const int hk = (int)(id % p.Hkv);
+  const int b = (int)(id / p.Hkv);
+  const int h = hk * p.grp + gi;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int qb0 = 2 * pair;
+  const bool validB = qb0 + 1 < p.nblk;
+
+  // ---- live-slot lists of both tiles (one thread per tile)
+  if (tid == 0 || tid == 32) {
+    const int t = tid >> 5;
+    const int qblk = qb0 + t;
+    int n = 0;
+    if (t == 0 || validB) {
+      const int32_t *selrow = p.sel + b * p.sel_sb + hk * p.sel_sh + (long long)qblk * p.sel_sn;
+      for (int slot = 0; slot < p.kk; ++slot) {
+        const int kb = __ldg(selrow + slot);
+        bool dup = false;
+        if (p.mask_mode == BSA_MASK_TOKEN)
+          for (int i = 0; i < slot && !dup; ++i) dup = __ldg(selrow + i) == kb;
+        const int kind = slot_kind(kb, slot, dup, qblk, p.nblk, p.bs, p.L, p.mask_mode, p.causal,
+                                   p.status);
+        if (kind != KIND_SKIP) {
+          s_item[t][n] = (kb << 3) | kind;
+          s_islot[t][n] = slot;
+          ++n;
+        }
+      }
+    }
+    s_n[t] = n;
+  }
+  if (tid == 0) {
+    mbar_init(&bar_q, 1);
+    for (int s = 0; s < F5_NST; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_empty[s], 128);
+    }
+    mbar_init(&p_full, 128);
+    mbar_init(&o_full, 1);
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    tc05::alloc(&tmem_base_sh, F5_TMEM_COLS);
+    tc05::relinquish();
+  }
+  tc05::fence_before();
+  __syncthreads();
+  tc05::fence_after();
+  const uint32_t tmem = tmem_base_sh;
+  const int nA = s_n[0], nB = s_n[1];
+  const int nsteps = nA > nB ? nA : nB;
+
+  if (warp == 4) {
+    // ================= TMA producer
+    if (lane == 0) {
+      mbar_expect_tx(&bar_q, (validB ? 2 : 1) * F5_TILE);
+      tma_load_rhb(sQ, &tq, &bar_q, perm_q, 0, qb0 * p.bs, h, b);
+      if (validB) tma_load_rhb(sQ + F5_TILE, &tq, &bar_q, perm_q, 0, (qb0 + 1) * p.bs, h, b);
+      for (int j = 0; j < nsteps; ++j) {
+        const int st = j % F5_NST;
+        if (j >= F5_NST && !mbar_wait(&kv_empty[st], ((j / F5_NST) - 1) & 1))
+          report(p.status, BSA_DEVERR_TIMEOUT);
+        const int act = (j < nA ? 1 : 0) + (j < nB ? 1 : 0);
+        mbar_expect_tx(&kv_full[st], act * 2 * F5_TILE);
+        for (int t = 0; t < 2; ++t) {
+          if (j >= (t ? nB : nA)) continue;
+          const int kb = s_item[t][j] >> 3;
+          uint8_t *dk = sKV + (st * 4 + t * 2) * F5_TILE;
+          tma_load_rhb(dk, &tk, &kv_full[st], perm_k, 0, kb * p.bs, hk, b);
+          tma_load_rhb(dk + F5_TILE, &tv, &kv_full[st], perm_v, 0, kb * p.bs, hk, b);
+        }
+      }
+    }
+  } else if (warp == 5) {
+    // ================= MMA issuer
+    if (lane == 0) {
+      if (!mbar_wait(&bar_q, 0)) report(p.status, BSA_DEVERR_TIMEOUT);
+      const uint32_t q_addr = smem_u32(sQ), p_addr = smem_u32(sP);
+      for (int j = 0; j <= nsteps; ++j) {
+        if (j < nsteps) {
+          const int st = j % F5_NST, bb = j & 1;
+          if (!mbar_wait(&kv_full[st], (j / F5_NST) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
+          if (j >= 2 && !mbar_wait(&s_empty[bb], ((j >> 1) - 1) & 1))
+            report(p.status, BSA_DEVERR_TIMEOUT);
+          tc05::fence_after();
+          for (int t = 0; t < 2; ++t) {
+            if (j >= (t ? nB : nA)) continue;
+            const uint32_t k_addr = smem_u32(sKV + (st * 4 + t * 2) * F5_TILE);
+            const uint32_t d = tc05::taddr(tmem, 16 * t, F5_SCOL0 + 64 * bb);
+#pragma unroll
+            for (int ks = 0; ks < F5_D / 16; ++ks)
+              tc05::mma_f16(d, tc05::sdesc(q_addr + t * F5_TILE + ks * 32, 16, 1024),
+                            tc05::sdesc(k_addr + ks * 32, 16, 1024), IDESC_S, ks > 0);
+          }
+          tc05::commit(&s_full[bb]);
+        }
+        if (j >= 1) {
+          const int jj = j - 1, st = jj % F5_NST;
+          if (!mbar_wait(&p_full, jj & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
+          tc05::fence_after();
+          for (int t = 0; t < 2; ++t) {
+            if (jj >= (t ? nB : nA)) continue;
+            const uint32_t v_addr = smem_u32(sKV + (st * 4 + t * 2 + 1) * F5_TILE);
+            const uint32_t d = tc05::taddr(tmem, 16 * t, F5_OCOL);
+#pragma unroll
+            for (int ks = 0; ks < F5_BS / 16; ++ks)
+              tc05::mma_f16(d, tc05::sdesc(p_addr + t * F5_TILE + ks * 32, 16, 1024),
+                            tc05::sdesc(v_addr + ks * 2048, F5_BS * 128, 1024), IDESC_PV,
+                            (jj > 0 || ks > 0) ? 1u : 0u);
+          }
+          tc05::commit(&o_full);
+          tc05::commit(&kv_empty[st]);
+        }
+      }
+    }
+  } else {
+    // ================= softmax warps 0-3
+    const int t = lane >> 4;            // tile of this thread
+    const int r = warp * 16 + (lane & 15);  // query row within its block
+    const int qblk = qb0 + t;
+    const int nmine = t ? nB : nA;
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const float *gaterow =
+        (p.gate && qblk < p.nblk)
+            ? p.gate + b * p.gate_sb + hk * p.gate_sh + (long long)qblk * p.gate_sn
+            : nullptr;
+    float m_used = -INFINITY, l = 0.f;
+    float s[64];
+    for (int j = 0; j < nsteps; ++j) {
+      const int bb = j & 1;
+      if (!mbar_wait(&s_full[bb], (j >> 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
+      tc05::fence_after();
+      tc05::ld32(tmem + lane_base + F5_SCOL0 + 64 * bb, s);
+      tc05::ld32(tmem + lane_base + F5_SCOL0 + 64 * bb + 32, s + 32);
+      tc05::wait_ld();
+      tc05::fence_before();
+      tc05::mbar_arrive(&s_empty[bb]);
+      const bool active = j < nmine;
+      float mx = -INFINITY;
+      int kind = 0, kb = 0;
+      if (active) {
+        const int item = s_item[t][j];
+        kind = item & 7;
+        kb = item >> 3;
+        const float g2 = gaterow ? __ldg(gaterow + s_islot[t][j]) * kLog2e : 0.f;
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          float x = fmaf(s[c], p.scale2, g2);
+          if ((kind & KIND_TRIU) && c > r) x = -INFINITY;
+          if ((kind & KIND_PAD) && kb * p.bs + c >= p.L) x = -INFINITY;
+          s[c] = x;
+          mx = fmaxf(mx, x);
+        }
+      }
+      const bool need = active && mx > -INFINITY && (m_used == -INFINITY || mx > m_used + F5_RESCALE);
+      // P buffer / O accumulator are free once PV_{j-1} has completed
+      if (j >= 1) {
+        if (!mbar_wait(&o_full, (j - 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
+        tc05::fence_after();
+      }
+      float alpha = 1.f;
+      if (need) {
+        alpha = m_used == -INFINITY ? 0.f : ex2(m_used - mx);
+        m_used = mx;
+        l *= alpha;
+      }
+      if (__any_sync(0xffffffffu, need) && j >= 1) {
+        float o[32];
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          const uint32_t ta = tmem + lane_base + F5_OCOL + 32 * half;
+          tc05::ld32(ta, o);
+          tc05::wait_ld();
+#pragma unroll
+          for (int c = 0; c < 32; ++c) o[c] *= alpha;
+          tc05::st32(ta, o);
+        }
+        tc05::wait_st();
+      }
+      if (active) {
+        const float base = m_used == -INFINITY ? 0.f : m_used;
+        float sum = 0.f;
+        const uint32_t prow = smem_u32(sP + t * F5_TILE);
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8) {
+          uint32_t w[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float p0 = ex2(s[c8 * 8 + 2 * e] - base);
+            const float p1 = ex2(s[c8 * 8 + 2 * e + 1] - base);
+            sum += p0 + p1;
+            w[e] = Mma<T>::pack(p0, p1);
+          }
+          asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(swz(prow, F5_BS, r, c8 * 8)),
+                       "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3])
+                       : "memory");
+        }
+        l += sum;
+      }
+      fence_proxy_async_smem();
+      tc05::fence_before();
+      tc05::mbar_arrive(&p_full);
+    }
+    // ---- epilogue: O / l
+    if (nsteps > 0) {
+      if (!mbar_wait(&o_full, (nsteps - 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
+      tc05::fence_after();
+    }
+    float o[64];
+    tc05::ld32(tmem + lane_base + F5_OCOL, o);
+    tc05::ld32(tmem + lane_base + F5_OCOL + 32, o + 32);
+    tc05::wait_ld();
+    if (nmine == 0) {  // never accumulated: the TMEM columns hold stale data
+#pragma unroll
+      for (int c = 0; c < 64; ++c) o[c] = 0.f;
+    }
+    const long long grow = (long long)qblk * p.bs + r;
+    if (qblk < p.nblk) {
+      const long long bh = (long long)b * p.Hq + h;
+      if (p.lse) p.lse[bh * p.Lp + grow] = l > 0.f ? m_used + __log2f(l) : INFINITY;
+      if (grow < p.L) {
+        const float inv = (nmine > 0 && l > 0.f) ? 1.f / l : 0.f;
+        T *orow = reinterpret_cast<T *>(p.o) + b * p.o_sb + h * p.o_sh + grow * p.o_sl;
+#pragma unroll
+        for (int c8 = 0; c8 < 8; ++c8) {
+          uint4 w;
+          w.x = Mma<T>::pack(o[c8 * 8 + 0] * inv, o[c8 * 8 + 1] * inv);
+          w.y = Mma<T>::pack(o[c8 * 8 + 2] * inv, o[c8 * 8 + 3] * inv);
+          w.z = Mma<T>::pack(o[c8 * 8 + 4] * inv, o[c8 * 8 + 5] * inv);
+          w.w = Mma<T>::pack(o[c8 * 8 + 6] * inv, o[c8 * 8 + 7] * inv);
+          *reinterpret_cast<uint4 *>(orow + c8 * 8) = w;
+        }
+      }
+    }
+  }
+  tc05::fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc05::fence_after();
+    tc05::dealloc(tmem, F5_TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ launcher
+bool fwd_sm100_applicable(const bsa_attn_args *a) {
+  return a->dtype != BSA_F32 && a->bs == 64 && a->D == 64 && a->sel && a->kk <= kMaxKK &&
+         !a->out_gate.ptr && !getenv("BSA_FWD_LEGACY");
+}
+
+bsa_status launch_fwd_sm100(const bsa_attn_args *a, const AttnParams &p, cudaStream_t st) {
+  TensorMap4 mq, mk, mv;
+  bsa_status s;
+  if ((s = make_tmap(&mq, a->q.ptr, a->dtype, a->B, a->Hq, a->L, 64, a->q.sb, a->q.sh, a->q.sl, 64, "q")))
+    return s;
+  if ((s = make_tmap(&mk, a->k.ptr, a->dtype, a->B, a->Hkv, a->L, 64, a->k.sb, a->k.sh, a->k.sl, 64, "k")))
+    return s;
+  if ((s = make_tmap(&mv, a->v.ptr, a->dtype, a->B, a->Hkv, a->L, 64, a->v.sb, a->v.sh, a->v.sl, 64, "v")))
+    return s;
+  auto pk = [](const TensorMap4 &m) { return m.perm[0] | (m.perm[1] << 2) | (m.perm[2] << 4); };
+  const long long grid = (long long)a->B * a->Hq * ((a->nblk + 1) / 2);
+  if (a->dtype == BSA_BF16) {
+    auto kern = attn_fwd_sm100_kernel<__nv_bfloat16>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, F5_SMEM);
+    kern<<<(unsigned)grid, 192, F5_SMEM, st>>>(mq.map, mk.map, mv.map, pk(mq), pk(mk), pk(mv), p);
+  } else {
+    auto kern = attn_fwd_sm100_kernel<__half>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, F5_SMEM);
+    kern<<<(unsigned)grid, 192, F5_SMEM, st>>>(mq.map, mk.map, mv.map, pk(mq), pk(mk), pk(mv), p);
+  }
+  return check_launch("attn_fwd_sm100");
+}
+
+}  // namespace bsa
