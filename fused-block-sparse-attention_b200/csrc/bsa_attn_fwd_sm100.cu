@@ -6,15 +6,20 @@
 // so tile B's accumulators are placed at lane offset 16: every one of the 128
 // softmax threads then owns one full query row (no shuffles for row max / sum).
 //
-// Warp roles (192 threads):
+// Warp roles (192 threads; 6 warps x <=168 registers keeps two CTAs resident
+// per SM, since each SM sub-partition holds 16K registers):
 //   warps 0-3  softmax: TMEM -> registers (32x32b loads), scale, gate, masks,
 //              lazy-rescaled online softmax, P (bf16) -> shared memory in the
 //              128B-swizzled K-major layout the MMA reads, final O / l.
-//   warp 4     TMA producer: Q tiles once, then K and V blocks of both tiles
-//              per step into a 2-deep ring.
-//   warp 5     TMEM allocation (256 columns) and the single MMA-issuing thread:
-//              S_j = Q K_j^T into a double-buffered TMEM S, PV_{j-1} = P V into
-//              the TMEM O accumulator, completions signalled by tcgen05.commit.
+//   warp 4     TMA producer (one thread): Q tiles once, then K blocks into a
+//              ring that is freed as soon as S_j completes and V blocks into a
+//              ring freed when PV_j completes; it polls both rings without
+//              blocking so neither stream waits behind the other.
+//   warp 5     TMEM allocation (256 columns); lane 0 issues the MMAs, polling
+//              two queues without blocking: PV_j = P_j V_j into the TMEM O
+//              accumulator as soon as P_j is ready (first priority), and
+//              S_j = Q K_j^T into a double-buffered TMEM S as soon as K_j has
+//              landed.  Completions are signalled by tcgen05.commit.
 // TMEM columns: S buffers [0,64) and [64,128), O [128,192).
 //
 // The running max is only raised (and O, l rescaled) when a row's new maximum
@@ -28,16 +33,44 @@
 
 namespace bsa {
 
+// Optional pipeline trace of CTA 0 (compile with -DBSA_TRACE): slot
+// [event * 64 + step] receives clock64() at that event.
+#ifdef BSA_TRACE
+#define F5_TRACE(ev, j)                                                           \
+  do {                                                                            \
+    if (p.trace && blockIdx.x == p.trace[1023] && (j) < 64) p.trace[(ev) * 64 + (j)] = clock64(); \
+  } while (0)
+#else
+#define F5_TRACE(ev, j) \
+  do {                  \
+  } while (0)
+#endif
+
+#ifdef BSA_TRACE
+__device__ __forceinline__ unsigned long long f5_gtime() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ unsigned f5_smid() {
+  unsigned r;
+  asm volatile("mov.u32 %0, %smid;" : "=r"(r));
+  return r;
+}
+#endif
+
 namespace {
-constexpr int F5_BS = 64, F5_D = 64, F5_NST = 2;
+constexpr int F5_BS = 64, F5_D = 64;
 constexpr int F5_TILE = F5_BS * F5_D * 2;  // 8 KB
-constexpr int F5_SMEM = 1024 + 2 * F5_TILE + F5_NST * 4 * F5_TILE + 2 * F5_TILE;
+constexpr int F5_MAXN = 64;                // live slots per tile kept in shared memory
+template <int NST>
+constexpr int f5_smem() { return 1024 + 2 * F5_TILE + NST * 4 * F5_TILE + 2 * F5_TILE; }
 constexpr uint32_t F5_TMEM_COLS = 256;
 constexpr int F5_SCOL0 = 0, F5_OCOL = 128;
 constexpr float F5_RESCALE = 8.f;  // log2 units
 }  // namespace
 
-template <typename T>
+template <typename T, int F5_NST>
 __global__ void __launch_bounds__(192, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tq,
                           const __grid_constant__ CUtensorMap tk,
@@ -50,13 +83,14 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~uintptr_t(1023));
   uint8_t *sQ = smem;                          // tile t at sQ + t*TILE
-  uint8_t *sKV = smem + 2 * F5_TILE;           // (stage, tile): K, V
-  uint8_t *sP = sKV + F5_NST * 4 * F5_TILE;    // tile t at sP + t*TILE
-  __shared__ __align__(8) uint64_t bar_q, kv_full[F5_NST], kv_empty[F5_NST], s_full[2],
-      s_empty[2], p_full, o_full;
+  uint8_t *sK = smem + 2 * F5_TILE;              // K ring: (stage, tile)
+  uint8_t *sV = sK + F5_NST * 2 * F5_TILE;       // V ring: (stage, tile)
+  uint8_t *sP = sV + F5_NST * 2 * F5_TILE;       // P: tile t at sP + t*TILE
+  __shared__ __align__(8) uint64_t bar_q, k_full[F5_NST], k_empty[F5_NST], v_full[F5_NST],
+      v_empty[F5_NST], s_full[2], s_empty[2], p_full, o_done;
   __shared__ uint32_t tmem_base_sh;
-  __shared__ int s_item[2][kMaxKK];  // (kb << 3) | kind of the j-th live slot
-  __shared__ int s_islot[2][kMaxKK];
+  __shared__ int s_item[2][F5_MAXN];  // (kb << 3) | kind of the j-th live slot
+  __shared__ int s_islot[2][F5_MAXN];
   __shared__ int s_n[2];
 
   // ---- CTA coordinates: (b, kv head, query-block pair, head in group)
@@ -73,6 +107,12 @@ __global__ void __launch_bounds__(192, 1)
   const int qb0 = 2 * pair;
   const bool validB = qb0 + 1 < p.nblk;
 
+#ifdef BSA_TRACE
+  if (p.trace && tid == 0) {
+    p.trace[1024 + 3 * blockIdx.x] = f5_smid();
+    p.trace[1024 + 3 * blockIdx.x + 1] = f5_gtime();
+  }
+#endif
   // ---- live-slot lists of both tiles (one thread per tile)
   if (tid == 0 || tid == 32) {
     const int t = tid >> 5;
@@ -87,7 +127,7 @@ __global__ void __launch_bounds__(192, 1)
           for (int i = 0; i < slot && !dup; ++i) dup = __ldg(selrow + i) == kb;
         const int kind = slot_kind(kb, slot, dup, qblk, p.nblk, p.bs, p.L, p.mask_mode, p.causal,
                                    p.status);
-        if (kind != KIND_SKIP) {
+        if (kind != KIND_SKIP && n < F5_MAXN) {
           s_item[t][n] = (kb << 3) | kind;
           s_islot[t][n] = slot;
           ++n;
@@ -99,15 +139,17 @@ __global__ void __launch_bounds__(192, 1)
   if (tid == 0) {
     mbar_init(&bar_q, 1);
     for (int s = 0; s < F5_NST; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
       mbar_init(&s_empty[s], 128);
     }
     mbar_init(&p_full, 128);
-    mbar_init(&o_full, 1);
+    mbar_init(&o_done, 1);
     fence_mbar_init();
   }
   if (warp == 5) {
@@ -122,41 +164,89 @@ __global__ void __launch_bounds__(192, 1)
   const int nsteps = nA > nB ? nA : nB;
 
   if (warp == 4) {
-    // ================= TMA producer
+    // ================= TMA producers (lane 0: Q and K, lane 1: V)
     if (lane == 0) {
       mbar_expect_tx(&bar_q, (validB ? 2 : 1) * F5_TILE);
       tma_load_rhb(sQ, &tq, &bar_q, perm_q, 0, qb0 * p.bs, h, b);
       if (validB) tma_load_rhb(sQ + F5_TILE, &tq, &bar_q, perm_q, 0, (qb0 + 1) * p.bs, h, b);
-      for (int j = 0; j < nsteps; ++j) {
+    }
+    if (lane == 0) {
+      int jk = 0, jv = 0;
+      uint32_t idle = 0;
+      auto issue = [&](bool isv, int j) {
         const int st = j % F5_NST;
-        if (j >= F5_NST && !mbar_wait(&kv_empty[st], ((j / F5_NST) - 1) & 1))
-          report(p.status, BSA_DEVERR_TIMEOUT);
+        uint64_t *full = isv ? &v_full[st] : &k_full[st];
+        uint8_t *ring = isv ? sV : sK;
         const int act = (j < nA ? 1 : 0) + (j < nB ? 1 : 0);
-        mbar_expect_tx(&kv_full[st], act * 2 * F5_TILE);
+        mbar_expect_tx(full, act * F5_TILE);
         for (int t = 0; t < 2; ++t) {
           if (j >= (t ? nB : nA)) continue;
           const int kb = s_item[t][j] >> 3;
-          uint8_t *dk = sKV + (st * 4 + t * 2) * F5_TILE;
-          tma_load_rhb(dk, &tk, &kv_full[st], perm_k, 0, kb * p.bs, hk, b);
-          tma_load_rhb(dk + F5_TILE, &tv, &kv_full[st], perm_v, 0, kb * p.bs, hk, b);
+          tma_load_rhb(ring + (st * 2 + t) * F5_TILE, isv ? &tv : &tk, full, isv ? perm_v : perm_k,
+                       0, kb * p.bs, hk, b);
+        }
+      };
+      while (jk < nsteps || jv < nsteps) {
+        bool progress = false;
+        if (jk < nsteps &&
+            (jk < F5_NST || mbar_test(&k_empty[jk % F5_NST], ((jk / F5_NST) - 1) & 1))) {
+          F5_TRACE(0, jk);
+          issue(false, jk++);
+          progress = true;
+        }
+        if (jv < nsteps &&
+            (jv < F5_NST || mbar_test(&v_empty[jv % F5_NST], ((jv / F5_NST) - 1) & 1))) {
+          issue(true, jv++);
+          progress = true;
+        }
+        if (progress) {
+          idle = 0;
+        } else {
+          if (++idle > kSpinLimit) {
+            report(p.status, BSA_DEVERR_TIMEOUT);
+            break;
+          }
+          __nanosleep(32);
         }
       }
     }
   } else if (warp == 5) {
-    // ================= MMA issuer
+    // ================= MMA issuer (S and PV queues, polled)
     if (lane == 0) {
       if (!mbar_wait(&bar_q, 0)) report(p.status, BSA_DEVERR_TIMEOUT);
       const uint32_t q_addr = smem_u32(sQ), p_addr = smem_u32(sP);
-      for (int j = 0; j <= nsteps; ++j) {
-        if (j < nsteps) {
-          const int st = j % F5_NST, bb = j & 1;
-          if (!mbar_wait(&kv_full[st], (j / F5_NST) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
-          if (j >= 2 && !mbar_wait(&s_empty[bb], ((j >> 1) - 1) & 1))
-            report(p.status, BSA_DEVERR_TIMEOUT);
+      int js = 0, jp = 0;
+      uint32_t idle = 0;
+      while (js < nsteps || jp < nsteps) {
+        bool progress = false;
+        if (jp < js && mbar_test(&p_full, jp & 1) &&
+            mbar_test(&v_full[jp % F5_NST], (jp / F5_NST) & 1)) {
+          const int st = jp % F5_NST;
+          F5_TRACE(3, jp);
           tc05::fence_after();
           for (int t = 0; t < 2; ++t) {
-            if (j >= (t ? nB : nA)) continue;
-            const uint32_t k_addr = smem_u32(sKV + (st * 4 + t * 2) * F5_TILE);
+            if (jp >= (t ? nB : nA)) continue;
+            const uint32_t v_addr = smem_u32(sV + (st * 2 + t) * F5_TILE);
+            const uint32_t d = tc05::taddr(tmem, 16 * t, F5_OCOL);
+#pragma unroll
+            for (int ks = 0; ks < F5_BS / 16; ++ks)
+              tc05::mma_f16(d, tc05::sdesc(p_addr + t * F5_TILE + ks * 32, 16, 1024),
+                            tc05::sdesc(v_addr + ks * 2048, F5_BS * 128, 1024), IDESC_PV,
+                            (jp > 0 || ks > 0) ? 1u : 0u);
+          }
+          tc05::commit(&v_empty[st]);
+          tc05::commit(&o_done);
+          ++jp;
+          progress = true;
+        }
+        if (js < nsteps && mbar_test(&k_full[js % F5_NST], (js / F5_NST) & 1) &&
+            (js < 2 || mbar_test(&s_empty[js & 1], ((js >> 1) - 1) & 1))) {
+          const int st = js % F5_NST, bb = js & 1;
+          F5_TRACE(2, js);
+          tc05::fence_after();
+          for (int t = 0; t < 2; ++t) {
+            if (js >= (t ? nB : nA)) continue;
+            const uint32_t k_addr = smem_u32(sK + (st * 2 + t) * F5_TILE);
             const uint32_t d = tc05::taddr(tmem, 16 * t, F5_SCOL0 + 64 * bb);
 #pragma unroll
             for (int ks = 0; ks < F5_D / 16; ++ks)
@@ -164,23 +254,18 @@ __global__ void __launch_bounds__(192, 1)
                             tc05::sdesc(k_addr + ks * 32, 16, 1024), IDESC_S, ks > 0);
           }
           tc05::commit(&s_full[bb]);
+          tc05::commit(&k_empty[st]);
+          ++js;
+          progress = true;
         }
-        if (j >= 1) {
-          const int jj = j - 1, st = jj % F5_NST;
-          if (!mbar_wait(&p_full, jj & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
-          tc05::fence_after();
-          for (int t = 0; t < 2; ++t) {
-            if (jj >= (t ? nB : nA)) continue;
-            const uint32_t v_addr = smem_u32(sKV + (st * 4 + t * 2 + 1) * F5_TILE);
-            const uint32_t d = tc05::taddr(tmem, 16 * t, F5_OCOL);
-#pragma unroll
-            for (int ks = 0; ks < F5_BS / 16; ++ks)
-              tc05::mma_f16(d, tc05::sdesc(p_addr + t * F5_TILE + ks * 32, 16, 1024),
-                            tc05::sdesc(v_addr + ks * 2048, F5_BS * 128, 1024), IDESC_PV,
-                            (jj > 0 || ks > 0) ? 1u : 0u);
+        if (progress) {
+          idle = 0;
+        } else {
+          if (++idle > kSpinLimit) {
+            report(p.status, BSA_DEVERR_TIMEOUT);
+            break;
           }
-          tc05::commit(&o_full);
-          tc05::commit(&kv_empty[st]);
+          __nanosleep(20);
         }
       }
     }
@@ -200,6 +285,7 @@ __global__ void __launch_bounds__(192, 1)
     for (int j = 0; j < nsteps; ++j) {
       const int bb = j & 1;
       if (!mbar_wait(&s_full[bb], (j >> 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
+      if (lane == 0) F5_TRACE(4 + warp, j);
       tc05::fence_after();
       tc05::ld32(tmem + lane_base + F5_SCOL0 + 64 * bb, s);
       tc05::ld32(tmem + lane_base + F5_SCOL0 + 64 * bb + 32, s + 32);
@@ -207,33 +293,57 @@ __global__ void __launch_bounds__(192, 1)
       tc05::fence_before();
       tc05::mbar_arrive(&s_empty[bb]);
       const bool active = j < nmine;
-      float mx = -INFINITY;
-      int kind = 0, kb = 0;
+      float mx = -INFINITY, g2 = 0.f;
       if (active) {
         const int item = s_item[t][j];
-        kind = item & 7;
-        kb = item >> 3;
-        const float g2 = gaterow ? __ldg(gaterow + s_islot[t][j]) * kLog2e : 0.f;
+        const int kind = item & 7, kb = item >> 3;
+        g2 = gaterow ? __ldg(gaterow + s_islot[t][j]) * kLog2e : 0.f;
+        if (kind & (KIND_TRIU | KIND_PAD)) {  // diagonal / padded block only
 #pragma unroll
-        for (int c = 0; c < 64; ++c) {
-          float x = fmaf(s[c], p.scale2, g2);
-          if ((kind & KIND_TRIU) && c > r) x = -INFINITY;
-          if ((kind & KIND_PAD) && kb * p.bs + c >= p.L) x = -INFINITY;
-          s[c] = x;
-          mx = fmaxf(mx, x);
+          for (int c = 0; c < 64; ++c)
+            if (((kind & KIND_TRIU) && c > r) || ((kind & KIND_PAD) && kb * p.bs + c >= p.L))
+              s[c] = -INFINITY;
         }
+        // row max of the raw scores (scale2 > 0), 8-way tree
+        float m8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) m8[i] = fmaxf(s[i], s[i + 8]);
+#pragma unroll
+        for (int c = 16; c < 64; c += 8)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) m8[i] = fmaxf(m8[i], s[c + i]);
+        const float mr = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                               fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+        mx = mr == -INFINITY ? -INFINITY : fmaf(mr, p.scale2, g2);
       }
       const bool need = active && mx > -INFINITY && (m_used == -INFINITY || mx > m_used + F5_RESCALE);
-      // P buffer / O accumulator are free once PV_{j-1} has completed
-      if (j >= 1) {
-        if (!mbar_wait(&o_full, (j - 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
-        tc05::fence_after();
-      }
       float alpha = 1.f;
       if (need) {
         alpha = m_used == -INFINITY ? 0.f : ex2(m_used - mx);
         m_used = mx;
         l *= alpha;
+      }
+      // p = 2^(s*scale2 + g2 - m_used): one fma + one ex2 per element, packed to T
+      uint32_t w[32];
+      if (active) {
+        const float off = g2 - (m_used == -INFINITY ? 0.f : m_used);
+        float sum8[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) sum8[i] = 0.f;
+#pragma unroll
+        for (int c = 0; c < 64; c += 2) {
+          const float p0 = ex2(fmaf(s[c], p.scale2, off));
+          const float p1 = ex2(fmaf(s[c + 1], p.scale2, off));
+          sum8[c & 7] += p0;
+          sum8[(c & 7) + 1] += p1;
+          w[c >> 1] = Mma<T>::pack(p0, p1);
+        }
+        l += ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
+      }
+      // PV_{j-1} must be complete: it reads the P buffer and accumulates into O
+      if (j >= 1) {
+        if (!mbar_wait(&o_done, (j - 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
+        tc05::fence_after();
       }
       if (__any_sync(0xffffffffu, need) && j >= 1) {
         float o[32];
@@ -249,32 +359,21 @@ __global__ void __launch_bounds__(192, 1)
         tc05::wait_st();
       }
       if (active) {
-        const float base = m_used == -INFINITY ? 0.f : m_used;
-        float sum = 0.f;
         const uint32_t prow = smem_u32(sP + t * F5_TILE);
 #pragma unroll
-        for (int c8 = 0; c8 < 8; ++c8) {
-          uint32_t w[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float p0 = ex2(s[c8 * 8 + 2 * e] - base);
-            const float p1 = ex2(s[c8 * 8 + 2 * e + 1] - base);
-            sum += p0 + p1;
-            w[e] = Mma<T>::pack(p0, p1);
-          }
+        for (int c8 = 0; c8 < 8; ++c8)
           asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(swz(prow, F5_BS, r, c8 * 8)),
-                       "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3])
+                       "r"(w[4 * c8]), "r"(w[4 * c8 + 1]), "r"(w[4 * c8 + 2]), "r"(w[4 * c8 + 3])
                        : "memory");
-        }
-        l += sum;
       }
       fence_proxy_async_smem();
       tc05::fence_before();
+      if (lane == 0) F5_TRACE(8 + warp, j);
       tc05::mbar_arrive(&p_full);
     }
     // ---- epilogue: O / l
     if (nsteps > 0) {
-      if (!mbar_wait(&o_full, (nsteps - 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
+      if (!mbar_wait(&o_done, (nsteps - 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
       tc05::fence_after();
     }
     float o[64];
@@ -306,6 +405,9 @@ __global__ void __launch_bounds__(192, 1)
   }
   tc05::fence_before();
   __syncthreads();
+#ifdef BSA_TRACE
+  if (p.trace && tid == 0) p.trace[1024 + 3 * blockIdx.x + 2] = f5_gtime();
+#endif
   if (warp == 5) {
     tc05::fence_after();
     tc05::dealloc(tmem, F5_TMEM_COLS);
@@ -314,7 +416,7 @@ __global__ void __launch_bounds__(192, 1)
 
 // ------------------------------------------------------------------ launcher
 bool fwd_sm100_applicable(const bsa_attn_args *a) {
-  return a->dtype != BSA_F32 && a->bs == 64 && a->D == 64 && a->sel && a->kk <= kMaxKK &&
+  return a->dtype != BSA_F32 && a->bs == 64 && a->D == 64 && a->sel && a->kk <= F5_MAXN &&
          !a->out_gate.ptr && !getenv("BSA_FWD_LEGACY");
 }
 
@@ -329,15 +431,29 @@ bsa_status launch_fwd_sm100(const bsa_attn_args *a, const AttnParams &p, cudaStr
     return s;
   auto pk = [](const TensorMap4 &m) { return m.perm[0] | (m.perm[1] << 2) | (m.perm[2] << 4); };
   const long long grid = (long long)a->B * a->Hq * ((a->nblk + 1) / 2);
-  if (a->dtype == BSA_BF16) {
-    auto kern = attn_fwd_sm100_kernel<__nv_bfloat16>;
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, F5_SMEM);
-    kern<<<(unsigned)grid, 192, F5_SMEM, st>>>(mq.map, mk.map, mv.map, pk(mq), pk(mk), pk(mv), p);
-  } else {
-    auto kern = attn_fwd_sm100_kernel<__half>;
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, F5_SMEM);
-    kern<<<(unsigned)grid, 192, F5_SMEM, st>>>(mq.map, mk.map, mv.map, pk(mq), pk(mk), pk(mv), p);
+#ifdef BSA_TRACE
+  AttnParams pt = p;
+  if (const char *tp = getenv("BSA_TRACE_PTR")) pt.trace = (unsigned long long *)strtoull(tp, nullptr, 0);
+#define p pt
+#endif
+  const char *env = getenv("BSA_FWD_STAGES");
+  const bool three = env && env[0] == '3';
+#define BSA_F5_LAUNCH(T_, N_)                                                                   \
+  {                                                                                             \
+    auto kern = attn_fwd_sm100_kernel<T_, N_>;                                                  \
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, f5_smem<N_>());      \
+    kern<<<(unsigned)grid, 192, f5_smem<N_>(), st>>>(mq.map, mk.map, mv.map, pk(mq), pk(mk),    \
+                                                      pk(mv), p);                               \
   }
+  if (a->dtype == BSA_BF16) {
+    if (three) BSA_F5_LAUNCH(__nv_bfloat16, 3) else BSA_F5_LAUNCH(__nv_bfloat16, 2)
+  } else {
+    if (three) BSA_F5_LAUNCH(__half, 3) else BSA_F5_LAUNCH(__half, 2)
+  }
+#undef BSA_F5_LAUNCH
+#ifdef BSA_TRACE
+#undef p
+#endif
   return check_launch("attn_fwd_sm100");
 }
 
