@@ -994,6 +994,11 @@ size_t attn_bwd_workspace(const bsa_attn_args *a) {
 }
 
 bsa_status fill_attn_params(const bsa_attn_args *a, AttnParams *p, bool bwd);
+bool dkdv_sm100_applicable(int dtype, int bs, int D);
+bsa_status launch_dkdv_sm100(int dtype, const CUtensorMap &mq, const CUtensorMap &mdo,
+                             const CUtensorMap &mk, const CUtensorMap &mv, int pq, int pdo, int pk,
+                             int pv, const AttnParams &p, const BwdPlan &pl, long long dkv_grid,
+                             cudaStream_t st);
 
 template <typename T, int BS, int D>
 static bsa_status launch_bwd_tc(const bsa_attn_args *a, const AttnParams &p, const BwdPlan &pl,
@@ -1034,12 +1039,18 @@ static bsa_status launch_bwd_tc(const bsa_attn_args *a, const AttnParams &p, con
   kq<<<(unsigned)grid, Q::NT, Q::SMEM, st>>>(mq.map, mdo.map, mkc.map, mvc.map, pk(mq), pk(mdo),
                                               pk(mkc), pk(mvc), p);
   if ((s = check_launch("attn_dq"))) return s;
-  auto kk = attn_dkdv_kernel<T, BS, D>;
-  cudaFuncSetAttribute(kk, cudaFuncAttributeMaxDynamicSharedMemorySize, K::SMEM);
-  kk<<<dim3((unsigned)dkv_grid, pl.Y), K::NT, K::SMEM, st>>>(mqc.map, mdoc.map, mk.map, mv.map,
-                                                             pk(mqc), pk(mdoc), pk(mk), pk(mv), p,
-                                                             pl);
-  if ((s = check_launch("attn_dkdv"))) return s;
+  if (dkdv_sm100_applicable(a->dtype, BS, D)) {
+    if ((s = launch_dkdv_sm100(a->dtype, mqc.map, mdoc.map, mk.map, mv.map, pk(mqc), pk(mdoc),
+                               pk(mk), pk(mv), p, pl, dkv_grid, st)))
+      return s;
+  } else {
+    auto kk = attn_dkdv_kernel<T, BS, D>;
+    cudaFuncSetAttribute(kk, cudaFuncAttributeMaxDynamicSharedMemorySize, K::SMEM);
+    kk<<<dim3((unsigned)dkv_grid, pl.Y), K::NT, K::SMEM, st>>>(mqc.map, mdoc.map, mk.map, mv.map,
+                                                               pk(mqc), pk(mdoc), pk(mk), pk(mv), p,
+                                                               pl);
+    if ((s = check_launch("attn_dkdv"))) return s;
+  }
   dkdv_reduce_kernel<T><<<dim3(pl.nbins, pl.Y), 256, 0, st>>>(p, pl, BS, D);
   return check_launch("dkdv_reduce");
 }
@@ -1097,6 +1108,8 @@ bsa_status run_attn_bwd(const bsa_attn_args *a, void *ws, size_t ws_bytes, cudaS
   pl.plan = w.plan;
   pl.part = w.part;
   const long long E = (long long)nbins * a->kk;
+  pl.npart = 2 * ((E + kChunkEntries - 1) / kChunkEntries) + 1;
+  pl.ncol = (int)E;
   const long long dkv_grid = nbins + (E + kChunkEntries - 1) / kChunkEntries;
 
   if (a->dtype == BSA_F32) {

@@ -1,0 +1,503 @@
+// Block-sparse attention backward, dK/dV part, on tcgen05 for block 64,
+// head dim 64.
+//
+// One CTA processes two dK/dV work items (tiles A and B): consecutive chunks of
+// the key-block CSR plan, each a key block of one KV head with up to 32 listed
+// (query block, slot) entries.  The key block's K and V stay in shared memory
+// as the stationary A operands; the listed query blocks stream through a
+// 3-stage ring (Q, dO by TMA, lse and Dvec rows by bulk copy).
+//
+// Per step j (one entry and query head of each tile):
+//   S^T  = K  Q_j^T    dP^T = V dO_j^T         (tcgen05, fp32 in TMEM, 2 buffers)
+//   P^T  = 2^(S^T*scale*log2e + gate - lse_j)  dS^T = P^T (dP^T - Dvec_j)
+//   dV  += P^T dO_j    dK  += dS^T Q_j          (tcgen05, accumulators in TMEM)
+// The elementwise step has no cross-column dependency, so every row (key) is
+// split over two warps of the same TMEM quadrant (32 columns each): 8 warps.
+//
+// Warp roles (320 threads, one CTA per SM):
+//   warps 0-7  elementwise: TMEM -> registers, P^T / dS^T (bf16) -> shared
+//              memory in the 128B-swizzled K-major layout, final dK / dV.
+//   warp 8     TMA producer (one thread, polls the ring).
+//   warp 9     TMEM allocation (512 columns) and the MMA-issuing thread, which
+//              polls two queues: dV/dK of step j as soon as P/dS are written,
+//              S/dP of the next step as soon as its ring stage has landed.
+// TMEM columns: S^T [0,64) [64,128), dP^T [128,192) [192,256), dV [256,320),
+// dK [320,384); tile B at lane offset 16.
+#include <algorithm>
+#include <type_traits>
+
+#include "bsa_attn.cuh"
+#include "bsa_host.h"
+#include "bsa_tc05.cuh"
+
+namespace bsa {
+
+#ifdef BSA_TRACE
+#define B5_TRACE(ev, j)                                                                  \
+  do {                                                                                   \
+    if (p.trace && blockIdx.x == p.trace[1023] && (j) < 128) p.trace[(ev) * 128 + (j)] = clock64(); \
+  } while (0)
+#else
+#define B5_TRACE(ev, j) \
+  do {                  \
+  } while (0)
+#endif
+
+namespace {
+constexpr int B5_BS = 64, B5_D = 64, B5_NST = 3;
+constexpr int B5_TILE = B5_BS * B5_D * 2;            // 8 KB
+constexpr int B5_ROWB = B5_BS * 4;                   // one lse / Dvec row chunk
+constexpr int B5_SMEM = 1024 + 4 * B5_TILE           // K, V of both tiles
+                        + B5_NST * 4 * B5_TILE       // ring: (stage, tile) Q, dO
+                        + 8 * B5_TILE                // P^T, dS^T of both tiles, 2 buffers
+                        + B5_NST * 2 * 2 * B5_ROWB;  // ring: (stage, tile) lse, Dvec
+constexpr uint32_t B5_TMEM_COLS = 512;
+constexpr int B5_SCOL = 0, B5_DPCOL = 128, B5_DVCOL = 256, B5_DKCOL = 320;  // +128: 2nd acc buffer
+}  // namespace
+
+__device__ __forceinline__ int b5_find_bin(const unsigned long long *plan, int nbins, unsigned x) {
+  int lo = 0, hi = nbins - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if ((unsigned)(plan[mid] >> 32) <= x)
+      lo = mid;
+    else
+      hi = mid - 1;
+  }
+  return lo;
+}
+
+// Work unit u -> (two chunks of the plan, KV head within the bin group).
+struct B5Unit {
+  int n[2], kb[2], b[2], hk[2], ebeg[2], nch[2], cidx[2], poff[2];
+  bool valid[2];
+};
+
+__device__ __forceinline__ void b5_unit(const BwdPlan &pl, const AttnParams &p, unsigned total,
+                                        int u, B5Unit &w) {
+  const unsigned x0 = 2u * (unsigned)(u / pl.Y);
+  const int y = u % pl.Y;
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const unsigned x = x0 + t;
+    w.valid[t] = x < total;
+    w.n[t] = 0;
+    w.kb[t] = w.b[t] = w.hk[t] = w.ebeg[t] = w.cidx[t] = w.poff[t] = 0;
+    w.nch[t] = 1;
+    if (!w.valid[t]) continue;
+    const int bin = b5_find_bin(pl.plan, pl.nbins, x);
+    const unsigned coff = (unsigned)(pl.plan[bin] >> 32);
+    w.poff[t] = (int)(pl.plan[bin] & 0xffffffffu);
+    w.nch[t] = (int)((unsigned)(pl.plan[bin + 1] >> 32) - coff);
+    w.cidx[t] = (int)(x - coff);
+    w.ebeg[t] = pl.row_ptr[bin] + w.cidx[t] * pl.C;
+    const int ee = min(pl.row_ptr[bin + 1], w.ebeg[t] + pl.C);
+    w.n[t] = (ee - w.ebeg[t]) * p.grp;
+    w.kb[t] = bin % p.nblk;
+    w.b[t] = bin / (p.nblk * pl.Hs);
+    w.hk[t] = ((bin / p.nblk) % pl.Hs) * pl.Y + y;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(320, 1)
+    attn_dkdv_sm100_kernel(const __grid_constant__ CUtensorMap tq,
+                           const __grid_constant__ CUtensorMap tdo,
+                           const __grid_constant__ CUtensorMap tk,
+                           const __grid_constant__ CUtensorMap tv, const int perm_q,
+                           const int perm_do, const int perm_k, const int perm_v,
+                           const AttnParams p, const BwdPlan pl) {
+  constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr uint32_t IDESC_KK = tc05::idesc_f16(kBF16, 64, 64, false);  // both K-major
+  constexpr uint32_t IDESC_KM = tc05::idesc_f16(kBF16, 64, B5_D, true);  // B MN-major
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                              ~uintptr_t(1023));
+  uint8_t *sKV = smem;                       // tile t: K, V
+  uint8_t *sR = sKV + 4 * B5_TILE;           // (stage, tile): Q, dO
+  uint8_t *sPD = sR + B5_NST * 4 * B5_TILE;  // (buffer, tile): P^T, dS^T
+  float *sRow = reinterpret_cast<float *>(sPD + 8 * B5_TILE);  // (stage, tile): lse[64], Dvec[64]
+  // p_full[b] / g_done[b]: P/dS of a step with parity b written / consumed by
+  // its dV/dK MMAs.  One barrier per buffer: with two buffers the elementwise
+  // warps may run one step ahead of the MMA issuer, and a single barrier would
+  // then be two phases ahead of its waiter (ambiguous parity).
+  __shared__ __align__(8) uint64_t kv_full, kv_empty, r_full[B5_NST], r_empty[B5_NST],
+      s_full[2], s_empty[2], p_full[2], g_done[2], acc_empty[2];
+  __shared__ uint32_t tmem_base_sh;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const unsigned total = (unsigned)(pl.plan[pl.nbins] >> 32);
+  const int nunits = (int)((total + 1) / 2) * pl.Y;
+
+  if (tid == 0) {
+    mbar_init(&kv_full, 1);
+    mbar_init(&kv_empty, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_empty[s], 256);
+      mbar_init(&acc_empty[s], 256);
+      mbar_init(&g_done[s], 1);
+      mbar_init(&p_full[s], 256);
+    }
+    for (int s = 0; s < B5_NST; ++s) {
+      mbar_init(&r_full[s], 1);
+      mbar_init(&r_empty[s], 1);
+    }
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tc05::alloc(&tmem_base_sh, B5_TMEM_COLS);
+    tc05::relinquish();
+  }
+  tc05::fence_before();
+  __syncthreads();
+  tc05::fence_after();
+  const uint32_t tmem = tmem_base_sh;
+
+  auto item = [&](const B5Unit &w, int t, int j, int &qblk, int &slot, int &h) {
+    int ci = w.ebeg[t] + j / p.grp;
+    if (ci < 0 || ci >= pl.ncol) {  // self-check: never read outside the CSR list
+      report(p.status, BSA_DEVERR_INDEX);
+      ci = 0;
+    }
+    const int e = pl.col[ci];
+    qblk = e / p.kk;
+    slot = e - qblk * p.kk;
+    h = w.hk[t] * p.grp + (j % p.grp);
+  };
+
+  if (warp == 8) {
+    // ================= producer: K/V per unit (2 buffers), Q/dO/lse/Dvec per step (ring)
+    if (lane == 0) {
+      int gs = 0, ne = 0;
+      uint32_t idle = 0;
+      for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
+        B5Unit w;
+        b5_unit(pl, p, total, u, w);
+        const int ns = max(w.n[0], w.n[1]);
+        if (ns == 0) continue;
+        // single K/V buffer: the previous unit's last S/dP MMAs must be done
+        if (ne >= 1 && !mbar_wait(&kv_empty, (ne - 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
+        mbar_expect_tx(&kv_full, ((w.n[0] > 0) + (w.n[1] > 0)) * 2 * B5_TILE);
+        for (int t = 0; t < 2; ++t) {
+          if (w.n[t] == 0) continue;
+          uint8_t *dst = sKV + t * 2 * B5_TILE;
+          tma_load_rhb(dst, &tk, &kv_full, perm_k, 0, w.kb[t] * p.bs, w.hk[t], w.b[t]);
+          tma_load_rhb(dst + B5_TILE, &tv, &kv_full, perm_v, 0, w.kb[t] * p.bs, w.hk[t], w.b[t]);
+        }
+        ++ne;
+        for (int j = 0; j < ns; ++j, ++gs) {
+          const int st = gs % B5_NST;
+          while (gs >= B5_NST && !mbar_test(&r_empty[st], ((gs / B5_NST) - 1) & 1)) {
+            if (++idle > kSpinLimit) {
+              report(p.status, BSA_DEVERR_TIMEOUT);
+              break;
+            }
+            __nanosleep(32);
+          }
+          idle = 0;
+          B5_TRACE(0, gs);
+          const int act = (j < w.n[0]) + (j < w.n[1]);
+          mbar_expect_tx(&r_full[st], act * (2 * B5_TILE + 2 * B5_ROWB));
+          for (int t = 0; t < 2; ++t) {
+            if (j >= w.n[t]) continue;
+            int qblk, slot, h;
+            item(w, t, j, qblk, slot, h);
+            if (qblk < 0 || qblk >= p.nblk || h < 0 || h >= p.Hq || w.b[t] < 0 || w.b[t] >= p.B) {
+              report(p.status, BSA_DEVERR_INDEX);  // self-check: keep every address in range
+              qblk = 0;
+              h = 0;
+              w.b[t] = 0;
+            }
+            const int row = qblk * p.bs;
+            uint8_t *dst = sR + (st * 2 + t) * 2 * B5_TILE;
+            tma_load_rhb(dst, &tq, &r_full[st], perm_q, 0, row, h, w.b[t]);
+            tma_load_rhb(dst + B5_TILE, &tdo, &r_full[st], perm_do, 0, row, h, w.b[t]);
+            const long long rb = ((long long)w.b[t] * p.Hq + h) * p.Lp + row;
+            float *rw = sRow + (st * 2 + t) * 2 * B5_BS;
+            bulk_load(rw, p.lse + rb, B5_ROWB, &r_full[st]);
+            bulk_load(rw + B5_BS, p.dvec + rb, B5_ROWB, &r_full[st]);
+          }
+        }
+      }
+    }
+  } else if (warp == 9) {
+    // ================= MMA issuer: S/dP queue and dV/dK queue, polled
+    if (lane == 0) {
+      // S queue state
+      int us = blockIdx.x, js = 0, gss = 0, nes = -1;
+      B5Unit ws;
+      bool have_s = false;
+      // G queue state
+      int ug = blockIdx.x, jg = 0, gsg = 0, neg = -1;
+      B5Unit wg;
+      bool have_g = false;
+      uint32_t idle = 0;
+      auto next_unit = [&](int &u, B5Unit &w, int &ne) -> bool {
+        for (; u < nunits; u += gridDim.x) {
+          b5_unit(pl, p, total, u, w);
+          if (max(w.n[0], w.n[1]) > 0) {
+            ++ne;
+            return true;
+          }
+        }
+        return false;
+      };
+      have_s = next_unit(us, ws, nes);
+      have_g = next_unit(ug, wg, neg);
+      while (have_g) {
+        bool progress = false;
+        // ---- dV += P^T dO, dK += dS^T Q for step (ug, jg)
+        if (gsg < gss && mbar_test(&p_full[gsg & 1], (gsg >> 1) & 1) &&
+            (jg > 0 || neg < 2 || mbar_test(&acc_empty[neg & 1], ((neg >> 1) - 1) & 1))) {
+          const int st = gsg % B5_NST, ab = neg & 1;
+          B5_TRACE(2, gsg);
+          tc05::fence_after();
+          for (int t = 0; t < 2; ++t) {
+            if (jg >= wg.n[t]) continue;
+            const uint32_t q_addr = smem_u32(sR + (st * 2 + t) * 2 * B5_TILE);
+            const uint32_t do_addr = q_addr + B5_TILE;
+            const uint32_t p_addr = smem_u32(sPD + ((gsg & 1) * 2 + t) * 2 * B5_TILE);
+            const uint32_t ds_addr = p_addr + B5_TILE;
+            const uint32_t dv = tc05::taddr(tmem, 16 * t, B5_DVCOL + 128 * ab);
+            const uint32_t dk = tc05::taddr(tmem, 16 * t, B5_DKCOL + 128 * ab);
+#pragma unroll
+            for (int ks = 0; ks < B5_BS / 16; ++ks) {
+              const uint32_t acc = (jg > 0 || ks > 0) ? 1u : 0u;
+              tc05::mma_f16(dv, tc05::sdesc(p_addr + ks * 32, 16, 1024),
+                            tc05::sdesc(do_addr + ks * 2048, B5_BS * 128, 1024), IDESC_KM, acc);
+              tc05::mma_f16(dk, tc05::sdesc(ds_addr + ks * 32, 16, 1024),
+                            tc05::sdesc(q_addr + ks * 2048, B5_BS * 128, 1024), IDESC_KM, acc);
+            }
+          }
+          tc05::commit(&r_empty[st]);
+          tc05::commit(&g_done[gsg & 1]);
+          ++gsg;
+          if (++jg == max(wg.n[0], wg.n[1])) {
+            jg = 0;
+            ug += gridDim.x;
+            have_g = next_unit(ug, wg, neg);
+          }
+          progress = true;
+        }
+        // ---- S^T = K Q^T, dP^T = V dO^T for step (us, js)
+        if (have_s && mbar_test(&r_full[gss % B5_NST], (gss / B5_NST) & 1) &&
+            (gss < 2 || mbar_test(&s_empty[gss & 1], ((gss >> 1) - 1) & 1)) &&
+            (js > 0 || mbar_test(&kv_full, nes & 1))) {
+          const int st = gss % B5_NST, bb = gss & 1;
+          B5_TRACE(1, gss);
+          tc05::fence_after();
+          for (int t = 0; t < 2; ++t) {
+            if (js >= ws.n[t]) continue;
+            const uint32_t q_addr = smem_u32(sR + (st * 2 + t) * 2 * B5_TILE);
+            const uint32_t do_addr = q_addr + B5_TILE;
+            const uint32_t k_addr = smem_u32(sKV + t * 2 * B5_TILE);
+            const uint32_t v_addr = k_addr + B5_TILE;
+            const uint32_t ds = tc05::taddr(tmem, 16 * t, B5_SCOL + 64 * bb);
+            const uint32_t ddp = tc05::taddr(tmem, 16 * t, B5_DPCOL + 64 * bb);
+#pragma unroll
+            for (int ks = 0; ks < B5_D / 16; ++ks) {
+              tc05::mma_f16(ds, tc05::sdesc(k_addr + ks * 32, 16, 1024),
+                            tc05::sdesc(q_addr + ks * 32, 16, 1024), IDESC_KK, ks > 0);
+              tc05::mma_f16(ddp, tc05::sdesc(v_addr + ks * 32, 16, 1024),
+                            tc05::sdesc(do_addr + ks * 32, 16, 1024), IDESC_KK, ks > 0);
+            }
+          }
+          tc05::commit(&s_full[bb]);
+          ++gss;
+          if (++js == max(ws.n[0], ws.n[1])) {
+            tc05::commit(&kv_empty);  // last reader of this unit's K/V
+            js = 0;
+            us += gridDim.x;
+            have_s = next_unit(us, ws, nes);
+          }
+          progress = true;
+        }
+        if (progress) {
+          idle = 0;
+        } else {
+          if (++idle > kSpinLimit) {
+            report(p.status, BSA_DEVERR_TIMEOUT);
+            break;
+          }
+          __nanosleep(20);
+        }
+      }
+    }
+  } else {
+    // ================= elementwise warps 0-7
+    const int quad = warp & 3, hf = warp >> 2;
+    const int t = lane >> 4;
+    const int kr = quad * 16 + (lane & 15);  // key row within the block
+    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
+    int gs = 0, ne = 0;
+    for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
+      B5Unit w;
+      b5_unit(pl, p, total, u, w);
+      const int ns = max(w.n[0], w.n[1]);
+      const int nmine = w.n[t], kb = w.kb[t], b = w.b[t], hk = w.hk[t];
+      const float *gbase = p.gate ? p.gate + b * p.gate_sb + hk * p.gate_sh : nullptr;
+      const bool key_ok = (long long)kb * p.bs + kr < p.L;
+      for (int j = 0; j < ns; ++j, ++gs) {
+        const int bb = gs & 1, st = gs % B5_NST;
+        if (!mbar_wait(&s_full[bb], (gs >> 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
+        if (tid == 0) B5_TRACE(3, gs);
+        tc05::fence_after();
+        float sv[32], dp[32];
+        tc05::ld32(tmem + lane_base + B5_SCOL + 64 * bb + 32 * hf, sv);
+        tc05::ld32(tmem + lane_base + B5_DPCOL + 64 * bb + 32 * hf, dp);
+        tc05::wait_ld();
+        tc05::fence_before();
+        tc05::mbar_arrive(&s_empty[bb]);
+        uint32_t wp[16], wd[16];
+        const bool active = j < nmine;
+        if (active) {
+          int qblk, slot, h;
+          item(w, t, j, qblk, slot, h);
+          const bool triu = p.causal && ((p.mask_mode == BSA_MASK_SLOT) ? slot == 0 : kb == qblk);
+          const float g2 = gbase ? __ldg(gbase + (long long)qblk * p.gate_sn + slot) * kLog2e : 0.f;
+          const float *lsep = sRow + (st * 2 + t) * 2 * B5_BS + 32 * hf;
+          const long long q0 = (long long)qblk * p.bs + 32 * hf;
+          if (triu || !key_ok || q0 + 32 > p.L) {  // diagonal / padded steps: explicit masks
+#pragma unroll
+            for (int c = 0; c < 32; ++c) {
+              const int qc = 32 * hf + c;
+              if (!key_ok || (triu && kr > qc) || q0 + c >= p.L) sv[c] = -INFINITY;
+            }
+          }
+#pragma unroll
+          for (int c = 0; c < 32; c += 4) {
+            const float4 a4 = *reinterpret_cast<const float4 *>(lsep + c);
+            const float4 d4 = *reinterpret_cast<const float4 *>(lsep + B5_BS + c);
+            const float p0 = ex2(fmaf(sv[c], p.scale2, g2 - a4.x));
+            const float p1 = ex2(fmaf(sv[c + 1], p.scale2, g2 - a4.y));
+            const float p2 = ex2(fmaf(sv[c + 2], p.scale2, g2 - a4.z));
+            const float p3 = ex2(fmaf(sv[c + 3], p.scale2, g2 - a4.w));
+            wp[c >> 1] = Mma<T>::pack(p0, p1);
+            wp[(c >> 1) + 1] = Mma<T>::pack(p2, p3);
+            wd[c >> 1] = Mma<T>::pack(p0 * (dp[c] - d4.x), p1 * (dp[c + 1] - d4.y));
+            wd[(c >> 1) + 1] = Mma<T>::pack(p2 * (dp[c + 2] - d4.z), p3 * (dp[c + 3] - d4.w));
+          }
+        }
+        if (gs >= 2) {  // dV/dK of step gs-2 read P / dS buffer gs & 1
+          if (!mbar_wait(&g_done[gs & 1], ((gs >> 1) - 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
+          tc05::fence_after();
+        }
+        if (active) {
+          const uint32_t pa = smem_u32(sPD + ((gs & 1) * 2 + t) * 2 * B5_TILE);
+#pragma unroll
+          for (int c8 = 0; c8 < 4; ++c8) {
+            const int col = 32 * hf + 8 * c8;
+            asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(swz(pa, B5_BS, kr, col)),
+                         "r"(wp[4 * c8]), "r"(wp[4 * c8 + 1]), "r"(wp[4 * c8 + 2]), "r"(wp[4 * c8 + 3])
+                         : "memory");
+            asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(swz(pa + B5_TILE, B5_BS, kr, col)),
+                         "r"(wd[4 * c8]), "r"(wd[4 * c8 + 1]), "r"(wd[4 * c8 + 2]), "r"(wd[4 * c8 + 3])
+                         : "memory");
+          }
+        }
+        fence_proxy_async_smem();
+        tc05::fence_before();
+        if (lane == 0 && (warp == 0 || warp == 7)) B5_TRACE(warp == 0 ? 4 : 5, gs);
+        tc05::mbar_arrive(&p_full[gs & 1]);
+      }
+      // ---- dK (scaled) and dV of this unit: this thread's row, columns [32*hf, +32)
+      float dkv[32], dvv[32];
+      if (ns > 0) {
+        const int gl = gs - 1;  // last step of this unit
+        if (!mbar_wait(&g_done[gl & 1], (gl >> 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
+        tc05::fence_after();
+        const int ab = ne & 1;
+        tc05::ld32(tmem + lane_base + B5_DKCOL + 128 * ab + 32 * hf, dkv);
+        tc05::ld32(tmem + lane_base + B5_DVCOL + 128 * ab + 32 * hf, dvv);
+        tc05::wait_ld();
+        tc05::fence_before();
+        tc05::mbar_arrive(&acc_empty[ab]);
+        ++ne;
+      }
+      if (!w.valid[t]) continue;
+      if (nmine == 0) {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) dkv[c] = dvv[c] = 0.f;
+      }
+      if (w.nch[t] == 1) {
+        const long long g = (long long)kb * p.bs + kr;
+        if (g < p.L) {
+          T *dkp = reinterpret_cast<T *>(p.dk) + b * p.dk_sb + hk * p.dk_sh + g * p.dk_sl + 32 * hf;
+          T *dvp = reinterpret_cast<T *>(p.dv) + b * p.dv_sb + hk * p.dv_sh + g * p.dv_sl + 32 * hf;
+#pragma unroll
+          for (int c = 0; c < 32; c += 8) {
+            uint4 a4, v4;
+            a4.x = Mma<T>::pack(dkv[c] * p.scale, dkv[c + 1] * p.scale);
+            a4.y = Mma<T>::pack(dkv[c + 2] * p.scale, dkv[c + 3] * p.scale);
+            a4.z = Mma<T>::pack(dkv[c + 4] * p.scale, dkv[c + 5] * p.scale);
+            a4.w = Mma<T>::pack(dkv[c + 6] * p.scale, dkv[c + 7] * p.scale);
+            v4.x = Mma<T>::pack(dvv[c], dvv[c + 1]);
+            v4.y = Mma<T>::pack(dvv[c + 2], dvv[c + 3]);
+            v4.z = Mma<T>::pack(dvv[c + 4], dvv[c + 5]);
+            v4.w = Mma<T>::pack(dvv[c + 6], dvv[c + 7]);
+            *reinterpret_cast<uint4 *>(dkp + c) = a4;
+            *reinterpret_cast<uint4 *>(dvp + c) = v4;
+          }
+        }
+      } else {
+        const long long pidx = (long long)(w.poff[t] + w.cidx[t]) * pl.Y + (u % pl.Y);
+        if (pidx < 0 || pidx >= pl.npart * pl.Y) {  // self-check: partial tile in range
+          report(p.status, BSA_DEVERR_INDEX);
+          continue;
+        }
+        float *part = pl.part + pidx * (2LL * B5_BS * B5_D);
+#pragma unroll
+        for (int c = 0; c < 32; c += 4) {
+          *reinterpret_cast<float4 *>(part + kr * B5_D + 32 * hf + c) =
+              make_float4(dkv[c], dkv[c + 1], dkv[c + 2], dkv[c + 3]);
+          *reinterpret_cast<float4 *>(part + B5_BS * B5_D + kr * B5_D + 32 * hf + c) =
+              make_float4(dvv[c], dvv[c + 1], dvv[c + 2], dvv[c + 3]);
+        }
+      }
+    }
+  }
+  tc05::fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    tc05::fence_after();
+    tc05::dealloc(tmem, B5_TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ launcher
+bool dkdv_sm100_applicable(int dtype, int bs, int D) {
+  return dtype != BSA_F32 && bs == 64 && D == 64 && !getenv("BSA_BWD_LEGACY");
+}
+
+bsa_status launch_dkdv_sm100(int dtype, const CUtensorMap &mq, const CUtensorMap &mdo,
+                             const CUtensorMap &mk, const CUtensorMap &mv, int pq, int pdo, int pk,
+                             int pv, const AttnParams &p, const BwdPlan &pl, long long dkv_grid,
+                             cudaStream_t st) {
+  // persistent: one CTA per SM (the unit count is only known on the device)
+  int dev = 0, nsm = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  const long long units_max = ((dkv_grid + 1) / 2) * pl.Y;
+  const unsigned grid = (unsigned)std::max<long long>(1, std::min<long long>(nsm, units_max));
+#ifdef BSA_TRACE
+  AttnParams pt = p;
+  if (const char *tp = getenv("BSA_TRACE_PTR")) pt.trace = (unsigned long long *)strtoull(tp, nullptr, 0);
+#define p pt
+#endif
+  if (dtype == BSA_BF16) {
+    auto kern = attn_dkdv_sm100_kernel<__nv_bfloat16>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, B5_SMEM);
+    kern<<<grid, 320, B5_SMEM, st>>>(mq, mdo, mk, mv, pq, pdo, pk, pv, p, pl);
+  } else {
+    auto kern = attn_dkdv_sm100_kernel<__half>;
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, B5_SMEM);
+    kern<<<grid, 320, B5_SMEM, st>>>(mq, mdo, mk, mv, pq, pdo, pk, pv, p, pl);
+  }
+#ifdef BSA_TRACE
+#undef p
+#endif
+  return check_launch("attn_dkdv_sm100");
+}
+
+}  // namespace bsa

@@ -199,3 +199,32 @@ def test_tcgen05_forward_matches_mma_sync_path(cuda, monkeypatch, B, H, L, kk, c
     _cmp(o5, ref, torch.bfloat16, "o tcgen05")
     _cmp(o1, ref, torch.bfloat16, "o mma.sync")
     assert (l5 - l1).abs().max().item() < 1e-4
+
+
+@pytest.mark.parametrize("Hq,Hkv,shared,hub", [(2, 2, False, False), (4, 4, True, True), (4, 2, False, False)])
+def test_tcgen05_backward_matches_mma_sync_path(cuda, monkeypatch, Hq, Hkv, shared, hub):
+    """dK/dV run on tcgen05 for block 64 / D 64; the mma.sync kernels (BSA_BWD_LEGACY)
+    must agree bitwise-closely and both match the oracle (incl. GQA and hub blocks)."""
+    import _bsa
+    B, L, D, bs, kk = 1, 4096, 64, 64, 9
+    gen = torch.Generator().manual_seed(Hq * 10 + Hkv + hub)
+    nblk = L // bs
+    q, do = (torch.randn(B, Hq, L, D, generator=gen).to(torch.bfloat16) for _ in range(2))
+    k, v = (torch.randn(B, Hkv, L, D, generator=gen).to(torch.bfloat16) for _ in range(2))
+    shape = (B, nblk, kk) if shared else (B, Hkv, nblk, kk)
+    sel = torch.randint(0, nblk, shape, generator=gen)
+    sel[..., 0] = torch.arange(nblk).view(*([1] * (len(shape) - 2)), nblk)
+    if hub:
+        sel[..., 1] = 0
+        sel[..., 2] = 3
+    gate = torch.randn(shape, generator=gen) * 0.3
+    dev = [t.to(cuda) for t in (q, k, v, do)]
+    sd, gd = sel.to(cuda, torch.int32), gate.to(cuda)
+    o, lse = _bsa.attn_fwd(dev[0], dev[1], dev[2], sd, gd, bs=bs, causal=True)
+    r5 = _bsa.attn_bwd(dev[0], dev[1], dev[2], o, dev[3], sd, lse, gd, bs=bs, causal=True)
+    monkeypatch.setenv("BSA_BWD_LEGACY", "1")
+    r1 = _bsa.attn_bwd(dev[0], dev[1], dev[2], o, dev[3], sd, lse, gd, bs=bs, causal=True)
+    rq, rk, rv, _ = O.attention_grads(q, k, v, sel, do, gate, bs=bs, causal=True)
+    for i, (ref, name) in enumerate(((rq, "dq"), (rk, "dk"), (rv, "dv"))):
+        _cmp(r5[i], ref, torch.bfloat16, name + " tcgen05")
+        _cmp(r1[i], ref, torch.bfloat16, name + " mma.sync")
