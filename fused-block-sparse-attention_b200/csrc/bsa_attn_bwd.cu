@@ -995,6 +995,11 @@ size_t attn_bwd_workspace(const bsa_attn_args *a) {
 
 bsa_status fill_attn_params(const bsa_attn_args *a, AttnParams *p, bool bwd);
 bool dkdv_sm100_applicable(int dtype, int bs, int D);
+bool dq_sm100_applicable(const AttnParams &p, int dtype, int D);
+bsa_status launch_dvec(int dtype, const AttnParams &p, int D, cudaStream_t st);
+bsa_status launch_dq_sm100(int dtype, const CUtensorMap &mq, const CUtensorMap &mdo,
+                           const CUtensorMap &mk, const CUtensorMap &mv, int pq, int pdo, int pk,
+                           int pv, const AttnParams &p, cudaStream_t st);
 bsa_status launch_dkdv_sm100(int dtype, const CUtensorMap &mq, const CUtensorMap &mdo,
                              const CUtensorMap &mk, const CUtensorMap &mv, int pq, int pdo, int pk,
                              int pv, const AttnParams &p, const BwdPlan &pl, long long dkv_grid,
@@ -1033,12 +1038,19 @@ static bsa_status launch_bwd_tc(const bsa_attn_args *a, const AttnParams &p, con
                      "v")))
     return s;
   auto pk = [](const TensorMap4 &m) { return m.perm[0] | (m.perm[1] << 2) | (m.perm[2] << 4); };
-  auto kq = attn_dq_kernel<T, BS, D>;
-  cudaFuncSetAttribute(kq, cudaFuncAttributeMaxDynamicSharedMemorySize, Q::SMEM);
-  const long long grid = (long long)a->B * a->Hq * a->nblk;
-  kq<<<(unsigned)grid, Q::NT, Q::SMEM, st>>>(mq.map, mdo.map, mkc.map, mvc.map, pk(mq), pk(mdo),
-                                              pk(mkc), pk(mvc), p);
-  if ((s = check_launch("attn_dq"))) return s;
+  if (dq_sm100_applicable(p, a->dtype, D) && a->sel) {
+    if ((s = launch_dvec(a->dtype, p, D, st))) return s;
+    if ((s = launch_dq_sm100(a->dtype, mq.map, mdo.map, mkc.map, mvc.map, pk(mq), pk(mdo), pk(mkc),
+                             pk(mvc), p, st)))
+      return s;
+  } else {
+    auto kq = attn_dq_kernel<T, BS, D>;
+    cudaFuncSetAttribute(kq, cudaFuncAttributeMaxDynamicSharedMemorySize, Q::SMEM);
+    const long long grid = (long long)a->B * a->Hq * a->nblk;
+    kq<<<(unsigned)grid, Q::NT, Q::SMEM, st>>>(mq.map, mdo.map, mkc.map, mvc.map, pk(mq), pk(mdo),
+                                                pk(mkc), pk(mvc), p);
+    if ((s = check_launch("attn_dq"))) return s;
+  }
   if (dkdv_sm100_applicable(a->dtype, BS, D)) {
     if ((s = launch_dkdv_sm100(a->dtype, mqc.map, mdoc.map, mk.map, mv.map, pk(mqc), pk(mdoc),
                                pk(mk), pk(mv), p, pl, dkv_grid, st)))

@@ -100,6 +100,21 @@ __device__ __forceinline__ void tma_load_rhb(void *dst, const CUtensorMap *map, 
   tma_load_4d(dst, map, bar, col, c1, c2, c3);
 }
 
+// L2 prefetch of the same box tma_load_rhb would copy (no shared memory, no
+// barrier): lets a producer run several ring stages ahead of its loads.
+__device__ __forceinline__ void tma_prefetch_rhb(const CUtensorMap *map, int perm, int col, int row,
+                                                 int head, int batch) {
+  const int pr = perm & 3, ph = (perm >> 2) & 3;
+  const int c1 = pr == 1 ? row : (ph == 1 ? head : batch);
+  const int c2 = pr == 2 ? row : (ph == 2 ? head : batch);
+  const int c3 = pr == 3 ? row : (ph == 3 ? head : batch);
+  asm volatile(
+      "cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(col), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
 // 1-D bulk copy global -> shared (both 16-byte aligned, bytes % 16 == 0).
 __device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes,
                                           uint64_t *bar) {
@@ -178,6 +193,11 @@ struct Mma<__half> {
   __device__ __forceinline__ static float to_f(__half x) { return __half2float(x); }
   __device__ __forceinline__ static __half from_f(float x) { return __float2half_rn(x); }
 };
+
+// Barrier `id` (1..15) among `count` threads (a multiple of 32).
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
 
 // Hardware base-2 exponential (the MUFU ex2 instruction, flush-to-zero).
 __device__ __forceinline__ float ex2(float x) {

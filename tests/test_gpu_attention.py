@@ -203,8 +203,9 @@ def test_tcgen05_forward_matches_mma_sync_path(cuda, monkeypatch, B, H, L, kk, c
 
 @pytest.mark.parametrize("Hq,Hkv,shared,hub", [(2, 2, False, False), (4, 4, True, True), (4, 2, False, False)])
 def test_tcgen05_backward_matches_mma_sync_path(cuda, monkeypatch, Hq, Hkv, shared, hub):
-    """dK/dV run on tcgen05 for block 64 / D 64; the mma.sync kernels (BSA_BWD_LEGACY)
-    must agree bitwise-closely and both match the oracle (incl. GQA and hub blocks)."""
+    """dK/dV run on tcgen05 for block 64 / D 64 (dQ too with BSA_DQ_TC05=1); the
+    mma.sync kernels (BSA_BWD_LEGACY) must agree closely and both match the oracle
+    (incl. GQA and hub blocks)."""
     import _bsa
     B, L, D, bs, kk = 1, 4096, 64, 64, 9
     gen = torch.Generator().manual_seed(Hq * 10 + Hkv + hub)
@@ -221,9 +222,14 @@ def test_tcgen05_backward_matches_mma_sync_path(cuda, monkeypatch, Hq, Hkv, shar
     dev = [t.to(cuda) for t in (q, k, v, do)]
     sd, gd = sel.to(cuda, torch.int32), gate.to(cuda)
     o, lse = _bsa.attn_fwd(dev[0], dev[1], dev[2], sd, gd, bs=bs, causal=True)
-    r5 = _bsa.attn_bwd(dev[0], dev[1], dev[2], o, dev[3], sd, lse, gd, bs=bs, causal=True)
+    monkeypatch.setenv("BSA_DQ_TC05", "1")
+    r5 = _bsa.attn_bwd(dev[0], dev[1], dev[2], o, dev[3], sd, lse, gd, bs=bs, causal=True,
+                       want_dgate=True)
     monkeypatch.setenv("BSA_BWD_LEGACY", "1")
-    r1 = _bsa.attn_bwd(dev[0], dev[1], dev[2], o, dev[3], sd, lse, gd, bs=bs, causal=True)
+    r1 = _bsa.attn_bwd(dev[0], dev[1], dev[2], o, dev[3], sd, lse, gd, bs=bs, causal=True,
+                       want_dgate=True)
+    dg5, dg1 = r5[3], r1[3]
+    assert torch.allclose(dg5, dg1, atol=2e-2, rtol=2e-2), (dg5 - dg1).abs().max().item()
     rq, rk, rv, _ = O.attention_grads(q, k, v, sel, do, gate, bs=bs, causal=True)
     for i, (ref, name) in enumerate(((rq, "dq"), (rk, "dk"), (rv, "dv"))):
         _cmp(r5[i], ref, torch.bfloat16, name + " tcgen05")
