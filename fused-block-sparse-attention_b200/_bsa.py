@@ -20,6 +20,7 @@ BF16, F16, F32 = 0, 1, 2
 MASK_SLOT, MASK_TOKEN = 0, 1
 SCORE_DOT, SCORE_MAXDOT2, SCORE_QUEST = 0, 1, 2
 SEL_SSA, SEL_FINISH = 0, 1
+HASH_ARGMAX, HASH_SIGN = 0, 1
 
 _STATUS_NAMES = {ERR_SHAPE: "shape", ERR_DTYPE: "dtype", ERR_STRIDE: "stride",
                  ERR_UNSUPPORTED: "unsupported", ERR_INDEX: "index", ERR_LAUNCH: "launch",
@@ -72,6 +73,14 @@ class SelectArgs(ctypes.Structure):
         ("status", ctypes.c_void_p)]
 
 
+class LshArgs(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in
+                ("G", "nblk", "dim", "hash_kind", "n_rounds", "n_planes", "cap", "causal", "topk")] + [
+        ("scale", ctypes.c_float), ("a", ctypes.c_void_p), ("b", ctypes.c_void_p),
+        ("planes", ctypes.c_void_p), ("sel", ctypes.c_void_p), ("score_out", ctypes.c_void_p),
+        ("gate_out", ctypes.c_void_p), ("status", ctypes.c_void_p)]
+
+
 class CsrArgs(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int32) for n in
                 ("B", "Hs", "nblk", "kk", "bs", "L", "mask_mode", "causal")] + [
@@ -95,6 +104,10 @@ SYMBOLS = {
     "bsa_pool": (ctypes.c_int, [ctypes.POINTER(PoolArgs), ctypes.c_void_p]),
     "bsa_select_width": (ctypes.c_int32, [ctypes.POINTER(SelectArgs)]),
     "bsa_select": (ctypes.c_int, [ctypes.POINTER(SelectArgs), ctypes.c_void_p]),
+    "bsa_select_lsh_width": (ctypes.c_int32, [ctypes.POINTER(LshArgs)]),
+    "bsa_select_lsh_workspace": (ctypes.c_size_t, [ctypes.POINTER(LshArgs)]),
+    "bsa_select_lsh": (ctypes.c_int, [ctypes.POINTER(LshArgs), ctypes.c_void_p, ctypes.c_size_t,
+                                      ctypes.c_void_p]),
     "bsa_csr_workspace": (ctypes.c_size_t, [ctypes.POINTER(CsrArgs)]),
     "bsa_sel_csr": (ctypes.c_int, [ctypes.POINTER(CsrArgs), ctypes.c_void_p, ctypes.c_size_t,
                                    ctypes.c_void_p]),
@@ -349,6 +362,44 @@ def select(a_sum, b1, b2=None, *, kind=SCORE_DOT, layout=SEL_SSA, causal=True, t
     s.sel = sel.data_ptr()
     s.status = status_tensor(a_sum.device).data_ptr()
     _check(L.bsa_select(ctypes.byref(s), _stream()))
+    return sel, score, gate
+
+
+def select_lsh(a_sum, b_sum, planes, *, hash_kind=HASH_SIGN, cap=16, causal=True, topk=16,
+               scale=1.0, want_score=False, want_gate=False):
+    """LSH candidate selection (bsa_select_lsh).  a_sum, b_sum: fp32 (..., nblk, dim) raw
+    block summaries (normalised inside); planes: (dim, n_rounds, n_planes).  Returns
+    (sel int32 (..., nblk, W), score, gate) in the SSA layout (own block first)."""
+    _need_cuda(a_sum, b_sum, planes)
+    lead = a_sum.shape[:-2]
+    nblk, dim = a_sum.shape[-2:]
+    A = a_sum.reshape(-1, nblk, dim).float().contiguous()
+    Bk = b_sum.reshape(-1, nblk, dim).float().contiguous()
+    R = planes.float().contiguous()
+    if R.dim() != 3 or R.shape[0] != dim:
+        raise BsaShapeError(ERR_SHAPE, "select_lsh: planes must be (dim, n_rounds, n_planes)")
+    s = LshArgs()
+    s.G, s.nblk, s.dim = A.shape[0], nblk, dim
+    s.hash_kind, s.n_rounds, s.n_planes, s.cap = hash_kind, R.shape[1], R.shape[2], cap
+    s.causal, s.topk, s.scale = 1 if causal else 0, topk, float(scale)
+    s.a, s.b, s.planes = A.data_ptr(), Bk.data_ptr(), R.data_ptr()
+    L = lib()
+    W = L.bsa_select_lsh_width(ctypes.byref(s))
+    nws = L.bsa_select_lsh_workspace(ctypes.byref(s))
+    if nws == 0:
+        _check(L.bsa_select_lsh(ctypes.byref(s), None, 0, _stream()))
+    ws = torch.empty(nws, dtype=torch.uint8, device=a_sum.device)
+    sel = torch.empty(*lead, nblk, W, dtype=torch.int32, device=a_sum.device)
+    score = gate = None
+    if want_score:
+        score = torch.empty(*lead, nblk, W, dtype=torch.float32, device=a_sum.device)
+        s.score_out = score.data_ptr()
+    if want_gate:
+        gate = torch.empty(*lead, nblk, W, dtype=torch.float32, device=a_sum.device)
+        s.gate_out = gate.data_ptr()
+    s.sel = sel.data_ptr()
+    s.status = status_tensor(a_sum.device).data_ptr()
+    _check(L.bsa_select_lsh(ctypes.byref(s), ctypes.c_void_p(ws.data_ptr()), nws, _stream()))
     return sel, score, gate
 
 

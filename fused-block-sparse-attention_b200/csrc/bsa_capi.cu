@@ -15,6 +15,9 @@ size_t sel_csr_workspace(const bsa_csr_args *a);
 bsa_status run_pool(const bsa_pool_args *a, cudaStream_t st);
 bsa_status run_select(const bsa_select_args *a, cudaStream_t st);
 int32_t select_width(const bsa_select_args *a);
+int32_t lsh_width(const bsa_lsh_args *a);
+size_t lsh_workspace(const bsa_lsh_args *a);
+bsa_status run_lsh(const bsa_lsh_args *a, void *ws, size_t ws_bytes, cudaStream_t st);
 bsa_status run_rope(const bsa_rope_args *a, cudaStream_t st);
 
 static bsa_status check_view(const bsa_view &v, int dtype, const char *name, bool vec16) {
@@ -63,8 +66,6 @@ bsa_status fill_attn_params(const bsa_attn_args *a, AttnParams *p, bool bwd) {
                reinterpret_cast<uintptr_t>(a->dv.ptr) % 4))
       return fail(BSA_ERR_STRIDE, "attn_bwd: dk/dv rows must be 4-byte aligned");
     if (!a->lse) return fail(BSA_ERR_ARG, "attn_bwd: lse is NULL");
-    if (a->mask_mode == BSA_MASK_TOKEN && a->dgate)
-      return fail(BSA_ERR_ARG, "attn_bwd: dgate is SLOT-mode only");
   }
   AttnParams &P = *p;
   P = AttnParams{};
@@ -178,6 +179,16 @@ int32_t bsa_select_width(const bsa_select_args *a) { return a ? select_width(a) 
 bsa_status bsa_select(const bsa_select_args *a, bsa_stream_t stream) {
   if (!a) return fail(BSA_ERR_ARG, "select: args is NULL");
   return run_select(a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int32_t bsa_select_lsh_width(const bsa_lsh_args *a) { return a ? lsh_width(a) : 0; }
+
+size_t bsa_select_lsh_workspace(const bsa_lsh_args *a) { return a ? lsh_workspace(a) : 0; }
+
+bsa_status bsa_select_lsh(const bsa_lsh_args *a, void *workspace, size_t workspace_bytes,
+                          bsa_stream_t stream) {
+  if (!a) return fail(BSA_ERR_ARG, "select_lsh: args is NULL");
+  return run_lsh(a, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
 }
 
 size_t bsa_csr_workspace(const bsa_csr_args *a) {

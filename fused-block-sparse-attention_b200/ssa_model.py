@@ -3,6 +3,9 @@ on sm_100a.
 
 BlockSparseSSA(d, h, block=64, topk=8, sel_dim=32, gate=False, causal=False,
                use_triton=False).forward(x, needle_pos=None)
+LSHBucketSSA(d, h, block=32, topk=4, sel_dim=32, n_rounds=4, n_buckets=8, cap=8,
+             gate=False, causal=False, scale=None, ...).forward(x, needle_pos=None)
+                                                        (src/ssa_model.py:336-513)
 
 Same parameters (qkv, o, sel_q, sel_k MLP selectors) and outputs.  Selection
 runs on device: the selector features are block-pooled (mean for queries,
@@ -21,7 +24,7 @@ import torch.nn.functional as F
 import _bsa
 from triton_kernel import bsattn
 
-__all__ = ["BlockSparseSSA"]
+__all__ = ["BlockSparseSSA", "LSHBucketSSA"]
 
 
 def _mlp_sel(d, sel_dim):
@@ -102,6 +105,101 @@ class BlockSparseSSA(nn.Module):
                 gate_bias = gate_bias.detach()
         out = bsattn(q, k, v, sel, gate_bias, causal=self.causal,
                      gate_grad=(self.gate and not self.use_triton))
+        out = out.reshape(B, H, Lp, dh).transpose(1, 2).reshape(B, Lp, D)[:, :L]
+        if needle_pos is not None:
+            chosen_last = sel[:, nblk - 1, :].long()
+            self.last_hit = (chosen_last == (needle_pos // Bs).unsqueeze(-1)).any(-1).float().mean().item()
+        return self.o(out)
+
+
+class LSHBucketSSA(nn.Module):
+    """LSH-bucketed selection + block-sparse attention (reference
+    src/ssa_model.py:336-513).  Same parameters (qkv, o, sel_q, sel_k, R).
+
+    Inference branch (dense_select False, the default): the selector features are
+    block-pooled on device (mean for queries; max(mean, max) for keys), then
+    bsa_select_lsh normalises them, hashes them by the argmax over R's n_buckets
+    projections per round, keeps the first `cap` key blocks of every bucket, and
+    re-scores the candidates by scale * cosine (top-k, own block first).  Missing
+    picks repeat the own block and are dropped by the attention's masks (causal:
+    content blocks must precede the query block; non-causal: repeated ids are
+    skipped), which is the reference's -inf mask on invalid slots (:480-482).
+    dense_select True: all-pairs cosine top-k (:404-414) with the fused
+    scoring/top-k kernel.  The learned-hash loss of the training branch
+    (learn_hash, :415-435) is not built; last_hash_loss stays None.
+    """
+
+    def __init__(self, d, h, block=32, topk=4, sel_dim=32, n_rounds=4, n_buckets=8, cap=8,
+                 gate=False, causal=False, scale=None, learn_hash=False, hash_tau=1.0,
+                 hash_detach_reps=False):
+        super().__init__()
+        self.h, self.dh = h, d // h
+        self.block, self.topk = block, topk
+        self.qkv = nn.Linear(d, 3 * d)
+        self.o = nn.Linear(d, d)
+        self.sel_q = _mlp_sel(d, sel_dim)
+        self.sel_k = _mlp_sel(d, sel_dim)
+        self.sel_dim = sel_dim
+        self.scale = float(sel_dim ** 0.5) if scale is None else float(scale)
+        self.n_rounds, self.n_buckets, self.cap = n_rounds, n_buckets, cap
+        self.gate, self.causal = gate, causal
+        self.dense_select = False
+        self.learn_hash, self.hash_tau = learn_hash, hash_tau
+        self.hash_detach_reps = hash_detach_reps
+        R0 = torch.randn(sel_dim, n_rounds, n_buckets)
+        if learn_hash:
+            self.R = nn.Parameter(R0)
+        else:
+            self.register_buffer("R", R0)
+        self.last_hit = None
+        self.last_block_logits = None
+        self.last_hash_loss = None
+
+    def forward(self, x, needle_pos=None):
+        B, L, D = x.shape
+        Bs = self.block
+        pad = (Bs - L % Bs) % Bs
+        if pad:
+            x = F.pad(x, (0, 0, 0, pad))
+        Lp = L + pad
+        nblk = Lp // Bs
+        H, dh = self.h, self.dh
+        q, k, v = self.qkv(x).chunk(3, -1)
+        q = q.view(B, Lp, H, dh).transpose(1, 2)
+        k = k.view(B, Lp, H, dh).transpose(1, 2)
+        v = v.view(B, Lp, H, dh).transpose(1, 2)
+
+        sqf, skf = self.sel_q(x), self.sel_k(x)
+        with torch.no_grad():
+            (sqp,) = _bsa.pool(sqf.detach().float().unsqueeze(1), Bs)
+            skm, skx = _bsa.pool(skf.detach().float().unsqueeze(1), Bs, mean=True, vmax=True)
+            skp = torch.maximum(skm, skx)
+            if self.dense_select:
+                qn, kn = F.normalize(sqp, dim=-1), F.normalize(skp, dim=-1)
+                sel, _, _ = _bsa.select(qn, kn, kind=_bsa.SCORE_DOT, layout=_bsa.SEL_SSA,
+                                        causal=self.causal, topk=self.topk)
+            else:
+                sel, _, _ = _bsa.select_lsh(sqp, skp, self.R.detach(), hash_kind=_bsa.HASH_ARGMAX,
+                                            cap=min(self.cap, nblk), causal=self.causal,
+                                            topk=self.topk, scale=self.scale)
+        sel = sel[:, 0]                                         # (B, nblk, kk) int32
+
+        # differentiable normalised reps for the gate and the logged logits
+        sq = F.normalize(sqf.view(B, nblk, Bs, self.sel_dim).mean(2), dim=-1)
+        skv = skf.view(B, nblk, Bs, self.sel_dim)
+        sk = F.normalize(torch.maximum(skv.mean(2), skv.max(2).values), dim=-1)
+        self.last_block_logits = self.scale * torch.bmm(sk, sq[:, nblk - 1:nblk].transpose(-1, -2)).squeeze(-1)
+
+        gate_bias = None
+        if self.gate:
+            idx = sel.long()
+            kk = idx.shape[-1]
+            flat = idx.view(B, nblk * kk, 1).expand(-1, -1, self.sel_dim)
+            gk = torch.gather(sk, 1, flat).view(B, nblk, kk, self.sel_dim)
+            gate_bias = F.logsigmoid(self.scale * (sq.unsqueeze(2) * gk).sum(-1).float())
+        mode = _bsa.MASK_SLOT if self.causal else _bsa.MASK_TOKEN
+        out = bsattn(q, k, v, sel, gate_bias, causal=self.causal, gate_grad=self.gate,
+                     mask_mode=mode)
         out = out.reshape(B, H, Lp, dh).transpose(1, 2).reshape(B, Lp, D)[:, :L]
         if needle_pos is not None:
             chosen_last = sel[:, nblk - 1, :].long()

@@ -59,12 +59,15 @@ class BSAttnFunction(torch.autograd.Function):
     """Autograd wrapper; gradients for q, k, v (and gate_bias when gate_grad)."""
 
     @staticmethod
-    def forward(ctx, q, k, v, sel, gate_bias, causal, gate_grad=False):
-        o, lse = _forward_lse(q, k, v, sel, gate_bias, causal)
+    def forward(ctx, q, k, v, sel, gate_bias, causal, gate_grad=False, mask_mode=_bsa.MASK_SLOT):
+        bs = _geometry(q, sel)
+        o, lse = _bsa.attn_fwd(q, k, v, sel, gate_bias, bs=bs, causal=causal, mask_mode=mask_mode,
+                               want_lse=True)
         ctx.save_for_backward(q, k, v, o, sel, lse,
                               gate_bias if gate_bias is not None else torch.empty(0, device=q.device))
         ctx.has_gate = gate_bias is not None
         ctx.causal = causal
+        ctx.mask_mode = mask_mode
         ctx.gate_grad = bool(gate_grad) and gate_bias is not None
         return o
 
@@ -74,7 +77,7 @@ class BSAttnFunction(torch.autograd.Function):
         gate = gate if ctx.has_gate else None
         bs = _geometry(q, sel)
         dq, dk, dv, dg = _bsa.attn_bwd(q, k, v, o, do, sel, lse, gate, bs=bs, causal=ctx.causal,
-                                       want_dgate=ctx.gate_grad)
+                                       mask_mode=ctx.mask_mode, want_dgate=ctx.gate_grad)
         dgate = None
         if ctx.gate_grad:
             # per-query-head sums -> the gate's own layout
@@ -83,9 +86,10 @@ class BSAttnFunction(torch.autograd.Function):
             else:
                 dgate = dg.view(dg.shape[0], gate.shape[1], -1, *dg.shape[2:]).sum(2)
             dgate = dgate.to(gate.dtype)
-        return dq, dk, dv, None, dgate, None, None
+        return dq, dk, dv, None, dgate, None, None, None
 
 
-def bsattn(q, k, v, sel, gate_bias=None, causal=False, gate_grad=False):
-    """Autograd-aware block-sparse attention. Use this for training."""
-    return BSAttnFunction.apply(q, k, v, sel, gate_bias, causal, gate_grad)
+def bsattn(q, k, v, sel, gate_bias=None, causal=False, gate_grad=False, mask_mode=_bsa.MASK_SLOT):
+    """Autograd-aware block-sparse attention. Use this for training.  mask_mode
+    MASK_TOKEN (an extension) also drops repeated block ids within a row."""
+    return BSAttnFunction.apply(q, k, v, sel, gate_bias, causal, gate_grad, mask_mode)

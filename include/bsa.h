@@ -164,6 +164,38 @@ typedef struct {
 int32_t bsa_select_width(const bsa_select_args *a);
 bsa_status bsa_select(const bsa_select_args *a, bsa_stream_t stream);
 
+/* LSH candidate selection in the SSA layout (row i = [i, picks...]).
+ * Replaces the inference branch of LSHBucketSSA (reference
+ * src/ssa_model.py:438-470).  Per group g: query summaries a[g,i,:] and key
+ * summaries b[g,j,:] (fp32, contiguous, dim wide) are L2-normalised
+ * (y = x / max(|x|, 1e-12), src/ssa_model.py:397-399) and hashed once per round:
+ *   ARGMAX: bucket = argmax_c <y, planes[:, r, c]>, n_planes buckets (:438-439);
+ *   SIGN:   bucket = bits [<y, planes[:, r, c]> > 0], 2^n_planes buckets.
+ * Each (round, bucket) keeps its first `cap` key blocks by index (:441-450).
+ * Candidates of query block i = the key blocks in its bucket of every round,
+ * deduplicated, excluding i (and j > i when causal) (:451-462); like the
+ * reference, which dedups ids clamped at 0, block 0 is also dropped when an
+ * earlier round's list had an empty slot (:452-457); score =
+ * scale * <yq_i, yk_j>; the top min(topk, max(1, nblk-1), n_rounds*cap) by
+ * (score desc, block asc) follow i in the row; missing picks are filled with i
+ * (their score_out is 0, as the reference's gscore, :472-476).  planes:
+ * (dim, n_rounds, n_planes) fp32.  Dots are fp32 fma chains over d from 0. */
+typedef enum { BSA_HASH_ARGMAX = 0, BSA_HASH_SIGN = 1 } bsa_hash_kind;
+typedef struct {
+  int32_t G, nblk, dim;
+  int32_t hash_kind, n_rounds, n_planes, cap, causal, topk;
+  float scale;
+  const float *a, *b, *planes;
+  int32_t *sel;      /* (G, nblk, width) */
+  float *score_out;  /* optional (G, nblk, width) */
+  float *gate_out;   /* optional (G, nblk, width): logsigmoid(score_out) */
+  int32_t *status;
+} bsa_lsh_args;
+int32_t bsa_select_lsh_width(const bsa_lsh_args *a);
+size_t bsa_select_lsh_workspace(const bsa_lsh_args *a);
+bsa_status bsa_select_lsh(const bsa_lsh_args *a, void *workspace, size_t workspace_bytes,
+                          bsa_stream_t stream);
+
 /* CSR transpose of a selection: for every (b, sel head, key block) the list of
  * entries e = qblk*kk + slot whose slot is active under the mask rules of
  * bsa_attn_args, in ascending e.  row_ptr: int32 (B*Hs*nblk + 1);

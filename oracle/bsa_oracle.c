@@ -19,6 +19,15 @@
  *                    scores        DOT   q.k of mean-pooled blocks
  *                                  MAXDOT2 src/ssa_model.py:118-119
  *                                  QUEST src/qwen_blocksparse.py:117-120
+ *   oracle_select_lsh — LSH candidate selection, the inference branch of LSHBucketSSA
+ *                    src/ssa_model.py:438-470: per-round buckets (argmax of the
+ *                    projections, :438-439, or the sign bits of n_planes hyperplanes),
+ *                    the first `cap` key blocks of each bucket by index (:441-450),
+ *                    candidates = the query block's buckets over all rounds,
+ *                    deduplicated, own / future excluded (:451-462; block 0 is also
+ *                    dropped after an empty slot of an earlier round, because the
+ *                    reference dedups ids clamped at 0, :452-457), re-scored by
+ *                    scale * cosine, top-k, own block first (:470-476).
  *   oracle_csr     — key-block transpose of the active (qblk, slot) entries under the
  *                    masks of src/triton_kernel.py:57-61 (SLOT) or
  *                    src/qwen_blocksparse.py:67-72 (TOKEN).
@@ -202,4 +211,110 @@ void oracle_csr(const int32_t *sel, int64_t sb, int64_t sh, int64_t sn, int B, i
           }
       }
   free(fill);
+}
+
+/* LSH selection (see header).  a, b: (G, nblk, dim) raw summaries; planes:
+ * (dim, rounds, nplanes).  sel/score/gate: (G, nblk, W), W = oracle_lsh_width. */
+int oracle_lsh_width(int nblk, int topk, int rounds, int cap) {
+  int T = topk < (nblk - 1 > 1 ? nblk - 1 : 1) ? topk : (nblk - 1 > 1 ? nblk - 1 : 1);
+  int P = rounds * cap;
+  return 1 + (T < P ? T : P);
+}
+
+static void lsh_normalise(const float *x, float *y, int dim) {
+  float ss = 0.f;
+  for (int d = 0; d < dim; ++d) ss = fmaf(x[d], x[d], ss);
+  float nrm = sqrtf(ss);
+  if (nrm < 1e-12f) nrm = 1e-12f;
+  for (int d = 0; d < dim; ++d) y[d] = x[d] / nrm;
+}
+
+static int lsh_code(const float *y, const float *planes, int dim, int rounds, int nplanes, int r,
+                    int sign_hash) {
+  int best = 0, bits = 0;
+  float bv = 0.f;
+  for (int c = 0; c < nplanes; ++c) {
+    float v = 0.f;
+    for (int d = 0; d < dim; ++d) v = fmaf(y[d], planes[(int64_t)d * rounds * nplanes + r * nplanes + c], v);
+    if (c == 0 || v > bv) {
+      best = c;
+      bv = v;
+    }
+    if (v > 0.f) bits |= 1 << c;
+  }
+  return sign_hash ? bits : best;
+}
+
+void oracle_select_lsh(const float *a, const float *b, const float *planes, int G, int nblk, int dim,
+                       int sign_hash, int rounds, int nplanes, int cap, int causal, int topk,
+                       float scale, int32_t *sel, float *score, float *gate) {
+  const int NB = sign_hash ? (1 << nplanes) : nplanes;
+  const int W = oracle_lsh_width(nblk, topk, rounds, cap);
+  const int rk = W - 1, P = rounds * cap;
+  float *yq = malloc(sizeof(float) * (size_t)nblk * dim);
+  float *yk = malloc(sizeof(float) * (size_t)nblk * dim);
+  int *qc = malloc(sizeof(int) * (size_t)nblk * rounds), *kc = malloc(sizeof(int) * (size_t)nblk * rounds);
+  int *list = malloc(sizeof(int) * (size_t)rounds * NB * cap), *cnt = malloc(sizeof(int) * (size_t)rounds * NB);
+  int *cid = malloc(sizeof(int) * P);
+  float *csc = malloc(sizeof(float) * P);
+  for (int g = 0; g < G; ++g) {
+    const float *ag = a + (int64_t)g * nblk * dim, *bg = b + (int64_t)g * nblk * dim;
+    for (int i = 0; i < nblk; ++i) {
+      lsh_normalise(ag + (int64_t)i * dim, yq + (int64_t)i * dim, dim);
+      lsh_normalise(bg + (int64_t)i * dim, yk + (int64_t)i * dim, dim);
+      for (int r = 0; r < rounds; ++r) {
+        qc[i * rounds + r] = lsh_code(yq + (int64_t)i * dim, planes, dim, rounds, nplanes, r, sign_hash);
+        kc[i * rounds + r] = lsh_code(yk + (int64_t)i * dim, planes, dim, rounds, nplanes, r, sign_hash);
+      }
+    }
+    /* first `cap` key blocks of every (round, bucket), in block order */
+    memset(cnt, 0, sizeof(int) * (size_t)rounds * NB);
+    for (int r = 0; r < rounds; ++r)
+      for (int j = 0; j < nblk; ++j) {
+        int c = kc[j * rounds + r], *n = &cnt[r * NB + c];
+        if (*n < cap) list[(r * NB + c) * cap + *n] = j;
+        ++*n;
+      }
+    for (int i = 0; i < nblk; ++i) {
+      const float *y = yq + (int64_t)i * dim;
+      int np = 0, empty_before = 0;
+      for (int r = 0; r < rounds; ++r) {
+        int c = qc[i * rounds + r], n = cnt[r * NB + c] < cap ? cnt[r * NB + c] : cap;
+        for (int p = 0; p < n; ++p) {
+          int j = list[(r * NB + c) * cap + p], dup = 0;
+          if (j == i || (causal && j > i)) continue;
+          /* the reference dedups on ids clamped at 0, so an empty slot of an
+           * earlier round (id -1 -> 0) removes block 0 (src/ssa_model.py:452-457) */
+          if (j == 0 && empty_before) continue;
+          for (int e = 0; e < np && !dup; ++e) dup = cid[e] == j;
+          if (dup) continue;
+          float s = 0.f;
+          for (int d = 0; d < dim; ++d) s = fmaf(y[d], yk[(int64_t)j * dim + d], s);
+          cid[np] = j;
+          csc[np] = s * scale;
+          ++np;
+        }
+        if (n < cap) empty_before = 1;
+      }
+      float own = 0.f;
+      for (int d = 0; d < dim; ++d) own = fmaf(y[d], yk[(int64_t)i * dim + d], own);
+      own *= scale;
+      int64_t ob = ((int64_t)g * nblk + i) * W;
+      sel[ob] = i;
+      if (score) score[ob] = own;
+      if (gate) gate[ob] = logsigmoidf_(own);
+      for (int t = 0; t < rk; ++t) {
+        int bi = -1;
+        for (int e = 0; e < np; ++e)
+          if (cid[e] >= 0 && (bi < 0 || better(csc[e], cid[e], csc[bi], cid[bi]))) bi = e;
+        int pick = bi >= 0 ? cid[bi] : i;
+        float ps = bi >= 0 ? csc[bi] : 0.f;
+        if (bi >= 0) cid[bi] = -1;
+        sel[ob + 1 + t] = pick;
+        if (score) score[ob + 1 + t] = ps;
+        if (gate) gate[ob + 1 + t] = logsigmoidf_(ps);
+      }
+    }
+  }
+  free(yq); free(yk); free(qc); free(kc); free(list); free(cnt); free(cid); free(csc);
 }

@@ -15,6 +15,11 @@ Fixtures (npz, fp32 / int32):
                       causal and non-causal (duplicates in sel).
   qwen_*.npz          qwen_blocksparse.blocksparse_forward with SelectMax / SelectAll / the
                       all-blocks fast path (src/qwen_blocksparse.py:29-121), GQA, padded L.
+  lsh_*.npz           LSHBucketSSA's inference selection (src/ssa_model.py:438-470): the raw
+                      block summaries it hashes (mean of sel_q, max(mean, max) of sel_k),
+                      its planes R, and the selection it attends with, decoded from the
+                      gathered keys (key rows carry their block id) and the -inf mask it
+                      hands to _sdpa (invalid picks).
   rope.npz            transformers' apply_rotary_pos_emb (qwen3_5_moe) on bf16 inputs, and
                       the cos/sin of Qwen3_5MoeTextRotaryEmbedding for text positions.
 """
@@ -138,25 +143,76 @@ def rope_case(name):
          ke=ke.float(), meta=np.array([B, Hq, Hkv, L, D, rot], np.int32), theta=np.array([theta]))
 
 
+def lsh_case(name, B, L, d, h, bs, topk, n_rounds, n_buckets, cap, causal, seed):
+    import ssa_model
+    torch.manual_seed(seed)
+    nblk = L // bs
+    m = ssa_model.LSHBucketSSA(d, h, block=bs, topk=topk, n_rounds=n_rounds, n_buckets=n_buckets,
+                               cap=cap, causal=causal)
+    m.eval()
+    x = torch.randn(B, L, d)
+    dh = d // h
+    # keys carry their block id in dim 0, so the gathered keys reveal the selection
+    kid = (torch.arange(L) // bs).float().view(1, L, 1, 1).expand(B, L, h, dh).clone()
+    qkv = torch.cat([torch.zeros(B, L, d), kid.reshape(B, L, d), torch.zeros(B, L, d)], -1)
+    del m.qkv
+    m.qkv = lambda x_: qkv
+    cap_ = {}
+
+    def spy(q, k, v, mask):
+        cap_["k"], cap_["mask"] = k.detach().clone(), mask.detach().clone()
+        return torch.zeros_like(q)
+
+    orig = ssa_model._sdpa
+    ssa_model._sdpa = spy
+    try:
+        with torch.no_grad():
+            m(x)
+    finally:
+        ssa_model._sdpa = orig
+    kk = cap_["k"].shape[1] // bs
+    ksel = cap_["k"].view(B, h, nblk, kk, bs, dh)[:, 0, :, :, 0, 0].round().to(torch.int32)
+    # last query row of each block: under the causal triangle it still sees the whole
+    # own block, so a slot is invalid exactly when its additive mask is -inf there
+    mlast = cap_["mask"].reshape(B, h, nblk, -1, kk * bs)[:, 0, :, -1, :]
+    valid = torch.isfinite(mlast.reshape(B, nblk, kk, bs)[..., 0])
+    with torch.no_grad():
+        s = m.sel_dim
+        a_raw = m.sel_q(x).view(B, nblk, bs, s).mean(2)
+        skv = m.sel_k(x).view(B, nblk, bs, s)
+        b_raw = torch.maximum(skv.mean(2), skv.max(2).values)
+    save(name, a=a_raw, b=b_raw, planes=m.R, scale=torch.tensor(m.scale), sel=ksel,
+         valid=valid.to(torch.int32), cap=torch.tensor(cap), topk=torch.tensor(topk),
+         causal=torch.tensor(int(causal)))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("BSA_REFERENCE", ""))
+    ap.add_argument("--only", default="", help="generate only fixtures whose name starts with this")
     a = ap.parse_args()
     src = os.path.join(a.ref, "src")
     if not os.path.isdir(src):
         sys.exit("reference src/ not found; pass --ref")
     sys.path.insert(0, src)
     torch.set_num_threads(min(8, os.cpu_count() or 1))
-    ssa_gather_case("ssa_gather_causal_gate.npz", 1, 2, 512, 64, 64, 3, True, True, 1)
-    ssa_gather_case("ssa_gather_causal.npz", 2, 1, 256, 64, 32, 4, True, False, 2)
-    ssa_gather_case("ssa_gather_noncausal_gate.npz", 1, 2, 256, 64, 64, 2, False, True, 3)
-    triton_interp_case("triton_interp_causal.npz", 1, 2, 256, 64, 64, 4, True, 4)
-    triton_interp_case("triton_interp_noncausal.npz", 1, 2, 256, 64, 64, 4, False, 5)
-    qwen_case("qwen_selectmax.npz", 1, 4, 2, 448, 64, 64, 3, 6, "max")
-    qwen_case("qwen_selectall.npz", 1, 4, 2, 200, 64, 32, 0, 8, "all")
-    qwen_case("qwen_fastpath.npz", 1, 4, 2, 256, 64, 64, 0, 9, "fast")
-    rope_case("rope.npz")
-
+    cases = [
+        ("ssa_gather_causal_gate.npz", ssa_gather_case, (1, 2, 512, 64, 64, 3, True, True, 1)),
+        ("ssa_gather_causal.npz", ssa_gather_case, (2, 1, 256, 64, 32, 4, True, False, 2)),
+        ("ssa_gather_noncausal_gate.npz", ssa_gather_case, (1, 2, 256, 64, 64, 2, False, True, 3)),
+        ("triton_interp_causal.npz", triton_interp_case, (1, 2, 256, 64, 64, 4, True, 4)),
+        ("triton_interp_noncausal.npz", triton_interp_case, (1, 2, 256, 64, 64, 4, False, 5)),
+        ("qwen_selectmax.npz", qwen_case, (1, 4, 2, 448, 64, 64, 3, 6, "max")),
+        ("qwen_selectall.npz", qwen_case, (1, 4, 2, 200, 64, 32, 0, 8, "all")),
+        ("qwen_fastpath.npz", qwen_case, (1, 4, 2, 256, 64, 64, 0, 9, "fast")),
+        ("lsh_causal.npz", lsh_case, (2, 2048, 64, 2, 16, 6, 4, 8, 8, True, 10)),
+        ("lsh_noncausal.npz", lsh_case, (1, 1024, 64, 2, 16, 4, 3, 6, 5, False, 11)),
+    ]
+    for name, fn, args in cases:
+        if name.startswith(a.only):
+            fn(name, *args)
+    if "rope.npz".startswith(a.only):
+        rope_case("rope.npz")
 
 if __name__ == "__main__":
     main()

@@ -111,15 +111,19 @@ def test_bf16_shapes_vs_oracle(cuda, bs, D, shared):
     _cmp(v.grad, rv, torch.bfloat16, "dv")
 
 
-def test_gate_gradient_vs_oracle(cuda):
+@pytest.mark.parametrize("mode,causal", [(0, True), (1, True), (1, False)])
+def test_gate_gradient_vs_oracle(cuda, mode, causal):
+    """dgate per slot; under TOKEN masks a repeated block id gets no gradient."""
     import triton_kernel as tk
     B, H, L, D, bs, kk = 1, 2, 512, 64, 64, 4
     q, k, v, do, sel, gate = _random_case(B, H, L, D, bs, kk, torch.float32, cuda, 11, shared=True)
+    if mode == 1:
+        sel[:, 5:, 2] = sel[:, 5:, 1]    # repeated ids
     gate.requires_grad_(True)
-    o = tk.bsattn(q, k, v, sel, gate, causal=True, gate_grad=True)
+    o = tk.bsattn(q, k, v, sel, gate, causal=causal, gate_grad=True, mask_mode=mode)
     (o * do).sum().backward()
     _, _, _, rg = O.attention_grads(q.cpu(), k.cpu(), v.cpu(), sel.cpu(), do.cpu(), gate.detach().cpu(),
-                                    bs=bs, causal=True, want_dgate=True)
+                                    bs=bs, causal=causal, mask_mode=mode, want_dgate=True)
     _cmp(gate.grad, rg, torch.float32, "dgate", 1e-4)
 
 

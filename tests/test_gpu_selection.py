@@ -146,3 +146,100 @@ def test_qwen_variant_bf16_vs_oracle(cuda):
     ref = ref.transpose(1, 2).reshape(B, L, Hq * D) * torch.sigmoid(gate.double())
     diff = (out.double().cpu() - ref).abs()
     assert (diff <= 2e-2 + 1e-2 * ref.abs()).all(), diff.max().item()
+
+
+@pytest.mark.parametrize("name", ["lsh_causal.npz", "lsh_noncausal.npz"])
+def test_lsh_golden(cuda, name):
+    """bsa_select_lsh on the reference LSHBucketSSA's own summaries and planes gives
+    its selection exactly (invalid slots -> own block)."""
+    import _bsa
+    g = golden(name)
+    dev = lambda x: torch.from_numpy(np.ascontiguousarray(x)).to(cuda)
+    sel, _, _ = _bsa.select_lsh(dev(g["a"]), dev(g["b"]), dev(g["planes"]),
+                                hash_kind=_bsa.HASH_ARGMAX, cap=int(g["cap"]),
+                                causal=bool(g["causal"]), topk=int(g["topk"]),
+                                scale=float(g["scale"]))
+    own = np.arange(g["sel"].shape[1]).reshape(1, -1, 1)
+    exp = np.where(g["valid"].astype(bool), g["sel"], own)
+    assert np.array_equal(sel.cpu().numpy(), exp)
+
+
+@pytest.mark.parametrize("hash_kind,causal,cap,topk,planes,rounds,nblk", [
+    (1, True, 16, 16, 4, 4, 700),
+    (1, False, 8, 12, 3, 2, 257),
+    (0, True, 5, 16, 8, 3, 300),
+    (0, True, 64, 32, 6, 4, 1000),
+    (1, True, 16, 64, 4, 4, 100),
+])
+def test_lsh_bit_exact_vs_oracle(cuda, hash_kind, causal, cap, topk, planes, rounds, nblk):
+    import _bsa
+    gen = torch.Generator().manual_seed(nblk + cap)
+    G, dim = 3, 64
+    a = torch.randn(G, nblk, dim, generator=gen)
+    b = a + 0.7 * torch.randn(G, nblk, dim, generator=gen)
+    R = torch.randn(dim, rounds, planes, generator=gen)
+    sel, sc, gt = _bsa.select_lsh(a.to(cuda), b.to(cuda), R.to(cuda), hash_kind=hash_kind, cap=cap,
+                                  causal=causal, topk=topk, scale=2.0, want_score=True,
+                                  want_gate=True)
+    osel, osc, ogt = O.select_lsh(a, b, R, hash_kind=hash_kind, cap=cap, causal=causal, topk=topk,
+                                  scale=2.0, want_score=True, want_gate=True)
+    assert np.array_equal(sel.cpu().numpy(), osel)
+    assert np.array_equal(sc.cpu().numpy(), osc)
+    assert np.allclose(gt.cpu().numpy(), ogt, atol=1e-6)
+
+
+def test_lsh_config5_full_size(cuda):
+    """BASELINE configuration 5 selection (B1 H8 N131072 D64 block 64, 4 sign planes x 4
+    rounds, cap 16, top-16): bit-exact against the oracle on the pooled summaries."""
+    import _bsa
+    import selection
+    gen = torch.Generator(device=cuda).manual_seed(5)
+    q, k = (torch.randn(1, 8, 131072, 64, device=cuda, generator=gen).to(torch.bfloat16)
+            for _ in range(2))
+    sel, _, _ = selection.select_lsh(q, k, bs=64, topk=16, n_rounds=4, n_planes=4, cap=16, seed=0)
+    assert sel.shape == (1, 8, 2048, 17)
+    (qp,) = _bsa.pool(q, 64)
+    (kp,) = _bsa.pool(k, 64)
+    R = selection.lsh_planes(64, 4, 4, 0)
+    osel, _, _ = O.select_lsh(qp.cpu(), kp.cpu(), R, hash_kind=O.HASH_SIGN, cap=16, causal=True,
+                              topk=16)
+    assert np.array_equal(sel.cpu().numpy(), osel)
+
+
+def test_lsh_module_matches_oracle_attention(cuda, monkeypatch):
+    """ssa_model.LSHBucketSSA: its selection equals the oracle's on the same pooled
+    features, and its attention (invalid picks masked: causal by position,
+    non-causal as repeated ids) equals the oracle attention over that selection."""
+    import _bsa
+    import ssa_model
+    real = ssa_model.bsattn
+    for causal in (True, False):
+        torch.manual_seed(7)
+        m = ssa_model.LSHBucketSSA(128, 2, block=32, topk=4, n_rounds=3, n_buckets=6, cap=4,
+                                   gate=True, causal=causal).to(cuda)
+        x = torch.randn(2, 1000, 128, device=cuda)
+        seen = {}
+
+        def spy(q, k, v, sel, gate, causal=False, gate_grad=False, mask_mode=0):
+            out = real(q, k, v, sel, gate, causal=causal, gate_grad=gate_grad, mask_mode=mask_mode)
+            seen.update(q=q, k=k, v=v, sel=sel, gate=gate, mode=mask_mode, out=out)
+            return out
+
+        monkeypatch.setattr(ssa_model, "bsattn", spy)
+        out = m(x)
+        out.float().sum().backward()
+        assert torch.isfinite(out).all()
+        assert m.sel_q[0].weight.grad is not None and torch.isfinite(m.sel_q[0].weight.grad).all()
+        xp = torch.nn.functional.pad(x, (0, 0, 0, 24))
+        (sqp,) = _bsa.pool(m.sel_q(xp).detach().float().unsqueeze(1), 32)
+        skm, skx = _bsa.pool(m.sel_k(xp).detach().float().unsqueeze(1), 32, mean=True, vmax=True)
+        osel, _, _ = O.select_lsh(sqp.cpu()[:, 0], torch.maximum(skm, skx).cpu()[:, 0], m.R.cpu(),
+                                  hash_kind=O.HASH_ARGMAX, cap=4, causal=causal, topk=4,
+                                  scale=m.scale)
+        assert np.array_equal(seen["sel"].cpu().numpy(), osel)
+        ref = O.attention(seen["q"].detach().float().cpu(), seen["k"].detach().float().cpu(),
+                          seen["v"].detach().float().cpu(), seen["sel"].cpu().long(),
+                          seen["gate"].detach().float().cpu(), bs=32, causal=causal,
+                          mask_mode=seen["mode"])
+        err = (seen["out"].detach().float().cpu() - ref).abs().max().item()
+        assert err < 1e-4, err

@@ -132,3 +132,60 @@ def test_csr_oracle_is_a_transpose():
             exp_rp[bin_ + 1] += 1
         assert np.array_equal(rp, np.cumsum(exp_rp))
         assert np.array_equal(col, np.array([e for _, e in seen], np.int32))
+
+
+def _lsh_expected(g):
+    """The reference's LSH selection with its invalid slots (-inf mask) replaced by
+    the own block, which is how the build marks a missing pick."""
+    own = np.arange(g["sel"].shape[1]).reshape(1, -1, 1)
+    return np.where(g["valid"].astype(bool), g["sel"], own)
+
+
+def test_lsh_selection_matches_reference():
+    """LSHBucketSSA's inference selection (argmax hashing, index-ordered bucket caps,
+    cross-round dedup incl. the block-0 quirk, cosine re-score, top-k)."""
+    for name in ("lsh_causal.npz", "lsh_noncausal.npz"):
+        g = golden(name)
+        sel, score, gate = O.select_lsh(g["a"], g["b"], g["planes"], hash_kind=O.HASH_ARGMAX,
+                                        cap=int(g["cap"]), causal=bool(g["causal"]),
+                                        topk=int(g["topk"]), scale=float(g["scale"]),
+                                        want_score=True, want_gate=True)
+        assert np.array_equal(sel, _lsh_expected(g)), name
+        # own score = scale * cosine of the normalised summaries
+        qa = g["a"] / np.maximum(np.linalg.norm(g["a"], axis=-1, keepdims=True), 1e-12)
+        kb = g["b"] / np.maximum(np.linalg.norm(g["b"], axis=-1, keepdims=True), 1e-12)
+        own = float(g["scale"]) * (qa * kb).sum(-1)
+        assert np.allclose(score[..., 0], own, atol=1e-5)
+        assert np.allclose(gate, np.log(1 / (1 + np.exp(-score.astype(np.float64)))), atol=1e-5)
+
+
+def test_lsh_sign_hash_structure():
+    """Sign hashing: every pick shares a bucket with its
+    query block in some round, precedes it (causal), appears once, and is ranked by
+    descending score; a cap of nblk with one round and zero planes' worth of buckets
+    degenerates to the dense causal top-k."""
+    rng = np.random.default_rng(3)
+    G, nblk, dim, rounds, planes, cap, topk = 3, 200, 64, 4, 4, 16, 16
+    a = rng.standard_normal((G, nblk, dim)).astype(np.float32)
+    b = (a + 0.5 * rng.standard_normal((G, nblk, dim))).astype(np.float32)
+    R = rng.standard_normal((dim, rounds, planes)).astype(np.float32)
+    sel, score, _ = O.select_lsh(a, b, R, hash_kind=O.HASH_SIGN, cap=cap, causal=True, topk=topk,
+                                 want_score=True)
+    qn = a / np.linalg.norm(a, axis=-1, keepdims=True)
+    kn = b / np.linalg.norm(b, axis=-1, keepdims=True)
+    qcode = ((np.einsum("gnd,drc->gnrc", qn, R) > 0) * (1 << np.arange(planes))).sum(-1)
+    kcode = ((np.einsum("gnd,drc->gnrc", kn, R) > 0) * (1 << np.arange(planes))).sum(-1)
+    for g in range(G):
+        for i in range(nblk):
+            picks = [j for j in sel[g, i, 1:] if j != i]
+            assert len(picks) == len(set(picks))
+            for j in picks:
+                assert j < i and (qcode[g, i] == kcode[g, j]).any()
+            sc = score[g, i, 1:1 + len(picks)]
+            assert (np.diff(sc) <= 0).all()
+    # one round whose single plane is zero: every block lands in bucket 0, the cap
+    # covers all blocks -> dense causal top-k by cosine (ties to the lower block)
+    Z = np.zeros((dim, 1, 1), np.float32)
+    sel1, _, _ = O.select_lsh(a, b, Z, hash_kind=O.HASH_SIGN, cap=nblk, causal=True, topk=8)
+    dense, _, _ = O.select(qn, kn, kind=O.SCORE_DOT, layout=O.SEL_SSA, causal=True, topk=8)
+    assert np.array_equal(sel1, dense)
