@@ -56,7 +56,8 @@ class AttnArgs(ctypes.Structure):
         ("sel_sn", ctypes.c_int64),
         ("gate", ctypes.c_void_p), ("gate_sb", ctypes.c_int64), ("gate_sh", ctypes.c_int64),
         ("gate_sn", ctypes.c_int64),
-        ("lse", ctypes.c_void_p), ("dgate", ctypes.c_void_p), ("status", ctypes.c_void_p)]
+        ("lse", ctypes.c_void_p), ("dgate", ctypes.c_void_p), ("status", ctypes.c_void_p),
+        ("q_blk0", ctypes.c_int32), ("Lq", ctypes.c_int32)]
 
 
 class PoolArgs(ctypes.Structure):
@@ -70,7 +71,7 @@ class SelectArgs(ctypes.Structure):
                 ("G", "nblk", "dim", "score_kind", "layout", "causal", "topk", "sink")] + [
         ("a", ctypes.c_void_p), ("b1", ctypes.c_void_p), ("b2", ctypes.c_void_p),
         ("sel", ctypes.c_void_p), ("score_out", ctypes.c_void_p), ("gate_out", ctypes.c_void_p),
-        ("status", ctypes.c_void_p)]
+        ("status", ctypes.c_void_p), ("q_blk0", ctypes.c_int32), ("nq", ctypes.c_int32)]
 
 
 class LshArgs(ctypes.Structure):
@@ -86,7 +87,7 @@ class CsrArgs(ctypes.Structure):
                 ("B", "Hs", "nblk", "kk", "bs", "L", "mask_mode", "causal")] + [
         ("sel", ctypes.c_void_p), ("sel_sb", ctypes.c_int64), ("sel_sh", ctypes.c_int64),
         ("sel_sn", ctypes.c_int64), ("row_ptr", ctypes.c_void_p), ("col", ctypes.c_void_p),
-        ("status", ctypes.c_void_p)]
+        ("status", ctypes.c_void_p), ("q_blk0", ctypes.c_int32), ("nq", ctypes.c_int32)]
 
 
 class RopeArgs(ctypes.Structure):
@@ -241,23 +242,31 @@ def _gate_fields(a, gate, sel):
     return gate
 
 
-def _base_args(q, k, v, bs, mask_mode, causal, scale, sel, gate):
+def _base_args(q, k, v, bs, mask_mode, causal, scale, sel, gate, q_blk0=None):
+    """q_blk0 (query-block sharding): q holds the query rows starting at block
+    q_blk0 of the sequence whose keys k, v hold; sel/gate rows cover q's blocks."""
     _need_cuda(q, k, v, sel, gate)
     if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
         raise BsaShapeError(ERR_SHAPE, "q, k, v must be (B, H, L, D)")
     if not (q.dtype == k.dtype == v.dtype):
         raise BsaError(ERR_DTYPE, "q, k, v must share a dtype")
-    B, Hq, L, D = q.shape
-    Hkv = k.shape[1]
+    B, Hq, Lq, D = q.shape
+    Hkv, L = k.shape[1], k.shape[2]
+    if q_blk0 is None and Lq != L:
+        raise BsaShapeError(ERR_SHAPE, "q and k lengths differ; pass q_blk0 for a query shard")
     nblk = (L + bs - 1) // bs
+    nq = (Lq + bs - 1) // bs
     a = AttnArgs()
     a.dtype = _dtype(q)
     a.B, a.Hq, a.Hkv, a.L, a.D, a.bs, a.nblk = B, Hq, Hkv, L, D, bs, nblk
+    if q_blk0 is not None:
+        a.q_blk0, a.Lq = int(q_blk0), Lq
+    a.nq = nq
     a.mask_mode = mask_mode
     a.causal = 1 if causal else 0
     a.scale = float(D ** -0.5 if scale is None else scale)
     keep = []
-    s, a.kk = _sel_fields(a, sel, B, Hkv, nblk)
+    s, a.kk = _sel_fields(a, sel, B, Hkv, nq)
     keep.append(s)
     if gate is not None:
         keep.append(_gate_fields(a, gate, s))
@@ -266,11 +275,12 @@ def _base_args(q, k, v, bs, mask_mode, causal, scale, sel, gate):
 
 
 def attn_fwd(q, k, v, sel, gate=None, *, bs, causal, mask_mode=MASK_SLOT, scale=None,
-             out=None, out_gate=None, want_lse=True):
+             out=None, out_gate=None, want_lse=True, q_blk0=None):
     """Block-sparse attention forward (bsa_attn_fwd).  Returns (o, lse or None).
-    `out` may be a strided (B,Hq,L,D) view (e.g. a transpose of (B,L,Hq,D))."""
+    `out` may be a strided (B,Hq,L,D) view (e.g. a transpose of (B,L,Hq,D)).
+    q_blk0: q is the query shard starting at that block (k, v: the whole sequence)."""
     q, k, v = _prep(q), _prep(k), _prep(v)
-    a, keep = _base_args(q, k, v, bs, mask_mode, causal, scale, sel, gate)
+    a, keep = _base_args(q, k, v, bs, mask_mode, causal, scale, sel, gate, q_blk0)
     a.q, a.k, a.v = _view4(q), _view4(k), _view4(v)
     o = torch.empty_like(q, memory_format=torch.contiguous_format) if out is None else out
     a.o = _view4(o)
@@ -279,18 +289,19 @@ def attn_fwd(q, k, v, sel, gate=None, *, bs, causal, mask_mode=MASK_SLOT, scale=
         a.out_gate = _view4(out_gate)
     lse = None
     if want_lse:
-        lse = torch.empty(a.B, a.Hq, a.nblk * a.bs, dtype=torch.float32, device=q.device)
+        lse = torch.empty(a.B, a.Hq, a.nq * a.bs, dtype=torch.float32, device=q.device)
         a.lse = lse.data_ptr()
     _check(lib().bsa_attn_fwd(ctypes.byref(a), _stream()))
     return o, lse
 
 
 def attn_bwd(q, k, v, o, do, sel, lse, gate=None, *, bs, causal, mask_mode=MASK_SLOT,
-             scale=None, want_dgate=False):
+             scale=None, want_dgate=False, q_blk0=None):
     """Block-sparse attention backward (bsa_attn_bwd).  Returns (dq, dk, dv, dgate or None);
-    dgate is per query head, (B, Hq, nblk, kk) fp32."""
+    dgate is per query head, (B, Hq, nq, kk) fp32.  With q_blk0 (a query shard) dk, dv
+    are this shard's contributions over the whole sequence."""
     q, k, v, o, do = _prep(q), _prep(k), _prep(v), _prep(o), _prep(do)
-    a, keep = _base_args(q, k, v, bs, mask_mode, causal, scale, sel, gate)
+    a, keep = _base_args(q, k, v, bs, mask_mode, causal, scale, sel, gate, q_blk0)
     a.q, a.k, a.v, a.o, a.dout = _view4(q), _view4(k), _view4(v), _view4(o), _view4(do)
     cf = torch.contiguous_format
     dq = torch.empty_like(q, memory_format=cf)
@@ -300,7 +311,7 @@ def attn_bwd(q, k, v, o, do, sel, lse, gate=None, *, bs, causal, mask_mode=MASK_
     a.lse = lse.data_ptr()
     dgate = None
     if want_dgate:
-        dgate = torch.empty(a.B, a.Hq, a.nblk, a.kk, dtype=torch.float32, device=q.device)
+        dgate = torch.empty(a.B, a.Hq, a.nq, a.kk, dtype=torch.float32, device=q.device)
         a.dgate = dgate.data_ptr()
     L = lib()
     nbytes = L.bsa_attn_bwd_workspace(ctypes.byref(a))
@@ -334,30 +345,36 @@ def pool(x, bs, *, grp=1, mean=True, vmin=False, vmax=False):
 
 
 def select(a_sum, b1, b2=None, *, kind=SCORE_DOT, layout=SEL_SSA, causal=True, topk=8,
-           sink=False, want_score=False, want_gate=False):
+           sink=False, want_score=False, want_gate=False, q_blk0=None):
     """Fused scoring + top-k (bsa_select).  a_sum, b1, b2: fp32 (..., nblk, dim); leading
-    dims are flattened into G groups.  Returns (sel int32 (..., nblk, W), score, gate)."""
+    dims are flattened into G groups.  Returns (sel int32 (..., nq, W), score, gate).
+    q_blk0: a_sum holds the nq query blocks starting there (a query shard)."""
     _need_cuda(a_sum, b1, b2)
     lead = a_sum.shape[:-2]
-    nblk, dim = a_sum.shape[-2:]
-    A = a_sum.reshape(-1, nblk, dim).float().contiguous()
+    nq, dim = a_sum.shape[-2:]
+    nblk = b1.shape[-2]
+    if q_blk0 is None and nq != nblk:
+        raise BsaShapeError(ERR_SHAPE, "select: query and key block counts differ; pass q_blk0")
+    A = a_sum.reshape(-1, nq, dim).float().contiguous()
     B1 = b1.reshape(-1, nblk, dim).float().contiguous()
     B2 = b2.reshape(-1, nblk, dim).float().contiguous() if b2 is not None else None
     s = SelectArgs()
     s.G, s.nblk, s.dim = A.shape[0], nblk, dim
+    if q_blk0 is not None:
+        s.q_blk0, s.nq = int(q_blk0), nq
     s.score_kind, s.layout, s.causal, s.topk, s.sink = kind, layout, 1 if causal else 0, topk, \
         1 if sink else 0
     s.a, s.b1 = A.data_ptr(), B1.data_ptr()
     s.b2 = B2.data_ptr() if B2 is not None else None
     L = lib()
     W = L.bsa_select_width(ctypes.byref(s))
-    sel = torch.empty(*lead, nblk, W, dtype=torch.int32, device=a_sum.device)
+    sel = torch.empty(*lead, nq, W, dtype=torch.int32, device=a_sum.device)
     score = gate = None
     if want_score:
-        score = torch.empty(*lead, nblk, W, dtype=torch.float32, device=a_sum.device)
+        score = torch.empty(*lead, nq, W, dtype=torch.float32, device=a_sum.device)
         s.score_out = score.data_ptr()
     if want_gate:
-        gate = torch.empty(*lead, nblk, W, dtype=torch.float32, device=a_sum.device)
+        gate = torch.empty(*lead, nq, W, dtype=torch.float32, device=a_sum.device)
         s.gate_out = gate.data_ptr()
     s.sel = sel.data_ptr()
     s.status = status_tensor(a_sum.device).data_ptr()

@@ -7,7 +7,8 @@ namespace bsa {
 
 struct AttnParams {
   int B, Hq, Hkv, grp, L, nblk, kk, bs, mask_mode, causal;
-  int Lp;        // nblk * bs (row count of lse / Dvec)
+  int q0, nq, Lq;  // local query blocks [q0, q0 + nq) of Lq rows (q0 = 0, nq = nblk, Lq = L unsharded)
+  int Lp;        // nq * bs (row count of lse / Dvec)
   float scale;   // softmax scale
   float scale2;  // scale * log2(e)
   const int32_t *sel;

@@ -1,6 +1,6 @@
 // Block-sparse attention backward for sm_100a.
 //
-//  1. CSR transpose of the selection (bsa_sel_csr): an entry e = qblk*kk + slot
+//  1. CSR transpose of the selection (bsa_sel_csr): an entry e = qi*kk + slot
 //     is "active" under the same mask rules as the forward; its key block is
 //     its bin.  Counts -> exclusive scan -> stable radix sort of (bin, e), so
 //     every bin lists its entries in ascending e (deterministic).
@@ -24,19 +24,21 @@
 namespace bsa {
 
 // ------------------------------------------------------------------ CSR build
-__global__ void csr_count_kernel(bsa_csr_args a, int32_t *cnt, uint32_t *keys, int32_t *vals,
-                                 int nbins) {
-  // one thread per (b, hs, qblk, slot)
-  const long long n = (long long)a.B * a.Hs * a.nblk * a.kk;
+static inline int csr_nq(const bsa_csr_args *a) { return a->nq > 0 ? a->nq : a->nblk; }
+
+__global__ void csr_count_kernel(bsa_csr_args a, int nq, int32_t *cnt, uint32_t *keys,
+                                 int32_t *vals, int nbins) {
+  // one thread per (b, hs, local query block, slot); bins are global key blocks
+  const long long n = (long long)a.B * a.Hs * nq * a.kk;
   for (long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x; t < n;
        t += (long long)gridDim.x * blockDim.x) {
     const int slot = (int)(t % a.kk);
     long long r = t / a.kk;
-    const int qblk = (int)(r % a.nblk);
-    r /= a.nblk;
+    const int qi = (int)(r % nq), qblk = a.q_blk0 + qi;
+    r /= nq;
     const int hs = (int)(r % a.Hs);
     const int b = (int)(r / a.Hs);
-    const int32_t *selrow = a.sel + b * a.sel_sb + hs * a.sel_sh + (long long)qblk * a.sel_sn;
+    const int32_t *selrow = a.sel + b * a.sel_sb + hs * a.sel_sh + (long long)qi * a.sel_sn;
     const int kb = selrow[slot];
     bool dup = false;
     if (a.mask_mode == BSA_MASK_TOKEN)
@@ -50,7 +52,7 @@ __global__ void csr_count_kernel(bsa_csr_args a, int32_t *cnt, uint32_t *keys, i
     } else {
       keys[t] = (uint32_t)nbins;  // sorts after every real bin
     }
-    vals[t] = qblk * a.kk + slot;
+    vals[t] = qi * a.kk + slot;
   }
 }
 
@@ -71,7 +73,7 @@ static int bits_for(long long v) {
 
 static size_t csr_layout(const bsa_csr_args *a, CsrWs *w, uint8_t *base) {
   const long long nbins = (long long)a->B * a->Hs * a->nblk;
-  const long long n = nbins * a->kk;
+  const long long n = (long long)a->B * a->Hs * csr_nq(a) * a->kk;
   size_t sort_bytes = 0, scan_bytes = 0;
   cub::DeviceRadixSort::SortPairs(nullptr, sort_bytes, (uint32_t *)nullptr, (uint32_t *)nullptr,
                                   (int32_t *)nullptr, (int32_t *)nullptr, (int)n, 0,
@@ -100,12 +102,12 @@ bsa_status run_sel_csr(const bsa_csr_args *a, void *ws, size_t ws_bytes, cudaStr
   if (!ws || ws_bytes < need) return fail(BSA_ERR_WORKSPACE, "sel_csr: workspace too small");
   csr_layout(a, &w, reinterpret_cast<uint8_t *>(ws));
   const long long nbins = (long long)a->B * a->Hs * a->nblk;
-  const long long n = nbins * a->kk;
+  const long long n = (long long)a->B * a->Hs * csr_nq(a) * a->kk;
   cudaMemsetAsync(w.cnt, 0, (nbins + 1) * 4, st);
   const int threads = 256;
   const long long blocks = std::min<long long>((n + threads - 1) / threads, 148LL * 64);
   csr_count_kernel<<<(unsigned)std::max<long long>(blocks, 1), threads, 0, st>>>(
-      *a, w.cnt, w.keys_in, w.vals_in, (int)nbins);
+      *a, csr_nq(a), w.cnt, w.keys_in, w.vals_in, (int)nbins);
   if (bsa_status s = check_launch("csr_count")) return s;
   size_t tb = w.cub_bytes;
   if (cub::DeviceRadixSort::SortPairs(w.cub_tmp, tb, w.keys_in, w.keys_out, w.vals_in, a->col,
@@ -183,8 +185,9 @@ __global__ void __launch_bounds__(TileCfg<BS, D>::NT)
   long long id = blockIdx.x;
   const int gi = (int)(id % p.grp);
   id /= p.grp;
-  const int qblk = (int)(id % p.nblk);
-  id /= p.nblk;
+  const int qi = (int)(id % p.nq);  // local query block; qblk is its global index
+  id /= p.nq;
+  const int qblk = p.q0 + qi;
   const int hk = (int)(id % p.Hkv);
   const int b = (int)(id / p.Hkv);
   const int h = hk * p.grp + gi;
@@ -192,9 +195,9 @@ __global__ void __launch_bounds__(TileCfg<BS, D>::NT)
   const long long bh = (long long)b * p.Hq + h;
 
   const int32_t *selrow =
-      p.sel ? p.sel + b * p.sel_sb + hk * p.sel_sh + (long long)qblk * p.sel_sn : nullptr;
+      p.sel ? p.sel + b * p.sel_sb + hk * p.sel_sh + (long long)qi * p.sel_sn : nullptr;
   const float *gaterow =
-      p.gate ? p.gate + b * p.gate_sb + hk * p.gate_sh + (long long)qblk * p.gate_sn : nullptr;
+      p.gate ? p.gate + b * p.gate_sb + hk * p.gate_sh + (long long)qi * p.gate_sn : nullptr;
   if (selrow)
     build_slot_table(s_slot, selrow, p.kk, qblk, p.nblk, p.bs, p.L, p.mask_mode, p.causal,
                      p.status);
@@ -206,9 +209,9 @@ __global__ void __launch_bounds__(TileCfg<BS, D>::NT)
   // Dvec = rowsum(dO * O) for this block's rows: two threads per row.
   {
     const int row = tid >> 1, half = tid & 1;
-    const long long grow = (long long)qblk * p.bs + row;
+    const long long grow = (long long)qi * p.bs + row;
     float acc = 0.f;
-    if (grow < p.L) {
+    if (grow < p.Lq) {
       const T *po = reinterpret_cast<const T *>(p.oin) + b * p.oi_sb + h * p.oi_sh + grow * p.oi_sl +
                     half * (D / 2);
       const T *pd = reinterpret_cast<const T *>(p.dout) + b * p.do_sb + h * p.do_sh +
@@ -276,8 +279,8 @@ __global__ void __launch_bounds__(TileCfg<BS, D>::NT)
     mbar_expect_tx(&bar[NST], 2 * Cfg::TILE);
 #pragma unroll
     for (int r = 0; r < D / 64; ++r) {
-      tma_load_rhb(sQ + r * BS * 128, &tq, &bar[NST], perm_q, r * 64, qblk * p.bs, h, b);
-      tma_load_rhb(sdO + r * BS * 128, &tdo, &bar[NST], perm_do, r * 64, qblk * p.bs, h, b);
+      tma_load_rhb(sQ + r * BS * 128, &tq, &bar[NST], perm_q, r * 64, qi * p.bs, h, b);
+      tma_load_rhb(sdO + r * BS * 128, &tdo, &bar[NST], perm_do, r * 64, qi * p.bs, h, b);
     }
     for (int s = 0; s < NST; ++s) {
       int kb = 0;
@@ -391,7 +394,7 @@ __global__ void __launch_bounds__(TileCfg<BS, D>::NT)
   }
   __syncthreads();
   if (p.dgate) {
-    float *dg = p.dgate + (bh * p.nblk + qblk) * (long long)p.kk;
+    float *dg = p.dgate + (bh * p.nq + qi) * (long long)p.kk;
     for (int j = tid; j < p.kk; j += NT) dg[j] = j < kMaxKK ? s_dg[j] : 0.f;
   }
   // stage dQ * scale (rounded to T) in the Q region, then 16-byte stores
@@ -407,8 +410,8 @@ __global__ void __launch_bounds__(TileCfg<BS, D>::NT)
   T *dqb = reinterpret_cast<T *>(p.dq) + b * p.dq_sb + h * p.dq_sh;
   for (int idx = tid; idx < BS * (D / 8); idx += NT) {
     const int row = idx / (D / 8), c8 = idx % (D / 8);
-    const long long grow = (long long)qblk * p.bs + row;
-    if (grow >= p.L) continue;
+    const long long grow = (long long)qi * p.bs + row;
+    if (grow >= p.Lq) continue;
     uint4 val;
     asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
                  : "=r"(val.x), "=r"(val.y), "=r"(val.z), "=r"(val.w)
@@ -446,7 +449,6 @@ __global__ void __launch_bounds__(TileCfg<BS, D>::NT)
   uint8_t *sST = sV + Cfg::TILE;  // stages: Q chunk, dO chunk, lse chunk, Dvec chunk
   __shared__ __align__(8) uint64_t bar[NST + 1];
   __shared__ int s_item[NST];  // entry index into col (relative), -1 end
-  __shared__ int s_meta[NST];  // (qblk << 12) | (slot << 3)... packed below
 
   const unsigned x = blockIdx.x;
   const unsigned total = (unsigned)(pl.plan[pl.nbins] >> 32);
@@ -477,11 +479,11 @@ __global__ void __launch_bounds__(TileCfg<BS, D>::NT)
     const int c = it % NCH;
     const int g = (it / NCH) % p.grp;
     const int e = pl.col[e_beg + it / (NCH * p.grp)];
-    const int qblk = e / p.kk;
+    const int qi = e / p.kk;  // local query block
     const int h = hk * p.grp + g;
     uint8_t *base = sST + st * Cfg::STAGE;
     mbar_expect_tx(&bar[st], 2 * Cfg::CH + 2 * Cfg::ROWB);
-    const int row = qblk * p.bs + c * KC;
+    const int row = qi * p.bs + c * KC;
 #pragma unroll
     for (int r = 0; r < D / 64; ++r) {
       tma_load_rhb(base + r * KC * 128, &tq, &bar[st], perm_q, r * 64, row, h, b);
@@ -524,7 +526,7 @@ __global__ void __launch_bounds__(TileCfg<BS, D>::NT)
     if (!mbar_wait(&bar[st], (it / NST) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
     const int c = it % NCH;
     const int e = pl.col[e_beg + it / (NCH * p.grp)];
-    const int qblk = e / p.kk, slot = e % p.kk;
+    const int qi = e / p.kk, slot = e % p.kk, qblk = p.q0 + qi;
     // the slot kind as recorded by the CSR build: TRIU only for causal slot 0
     // (SLOT mode) or the own block (TOKEN mode)
     const bool triu = p.causal && ((p.mask_mode == BSA_MASK_SLOT) ? slot == 0 : kb == qblk);
@@ -534,7 +536,7 @@ __global__ void __launch_bounds__(TileCfg<BS, D>::NT)
       const uint32_t qc = smem_u32(base), dc = qc + Cfg::CH;
       const float *slse = reinterpret_cast<const float *>(base + 2 * Cfg::CH);
       const float *sdv = slse + KC;
-      const float g2 = gbase ? __ldg(gbase + (long long)qblk * p.gate_sn + slot) * kLog2e : 0.f;
+      const float g2 = gbase ? __ldg(gbase + (long long)qi * p.gate_sn + slot) * kLog2e : 0.f;
       float s[NT8][4], dp[NT8][4];
 #pragma unroll
       for (int n = 0; n < NT8; ++n)
@@ -577,7 +579,7 @@ __global__ void __launch_bounds__(TileCfg<BS, D>::NT)
           const int qrow = c * KC + qc_;
           const int krow = e2 < 2 ? kr0 : kr1;
           const bool masked = (triu && krow > qrow) ||
-                              ((long long)qblk * p.bs + qrow >= p.L) ||
+                              ((long long)qi * p.bs + qrow >= p.Lq) ||
                               ((long long)kb * p.bs + krow >= p.L);
           const float pr = masked ? 0.f : ex2(fmaf(s[n][e2], p.scale2, g2) - slse[qc_]);
           s[n][e2] = pr;
@@ -712,17 +714,18 @@ __global__ void __launch_bounds__(256) attn_dq_f32_kernel(const AttnParams p) {
   long long id = blockIdx.x;
   const int gi = (int)(id % p.grp);
   id /= p.grp;
-  const int qblk = (int)(id % p.nblk);
-  id /= p.nblk;
+  const int qi = (int)(id % p.nq);  // local query block; qblk is its global index
+  id /= p.nq;
+  const int qblk = p.q0 + qi;
   const int hk = (int)(id % p.Hkv);
   const int b = (int)(id / p.Hkv);
   const int h = hk * p.grp + gi;
   const int tid = threadIdx.x;
   const long long bh = (long long)b * p.Hq + h;
   const int32_t *selrow =
-      p.sel ? p.sel + b * p.sel_sb + hk * p.sel_sh + (long long)qblk * p.sel_sn : nullptr;
+      p.sel ? p.sel + b * p.sel_sb + hk * p.sel_sh + (long long)qi * p.sel_sn : nullptr;
   const float *gaterow =
-      p.gate ? p.gate + b * p.gate_sb + hk * p.gate_sh + (long long)qblk * p.gate_sn : nullptr;
+      p.gate ? p.gate + b * p.gate_sb + hk * p.gate_sh + (long long)qi * p.gate_sn : nullptr;
   if (selrow)
     build_slot_table(s_slot, selrow, p.kk, qblk, p.nblk, p.bs, p.L, p.mask_mode, p.causal,
                      p.status);
@@ -734,17 +737,17 @@ __global__ void __launch_bounds__(256) attn_dq_f32_kernel(const AttnParams p) {
   const float *v = reinterpret_cast<const float *>(p.v) + b * p.v_sb + hk * p.v_sh;
   for (int i = tid; i < BS * D; i += 256) {
     const int r = i / D, d = i % D;
-    const long long gr = (long long)qblk * p.bs + r;
-    const bool ok = gr < p.L;
+    const long long gr = (long long)qi * p.bs + r;
+    const bool ok = gr < p.Lq;
     sq[r * LD + d] = ok ? q[gr * p.q_sl + d] : 0.f;
     sdo[r * LD + d] = ok ? dO[gr * p.do_sl + d] : 0.f;
     sdq[r * LD + d] = 0.f;
   }
   __syncthreads();
   for (int r = tid; r < BS; r += 256) {
-    const long long gr = (long long)qblk * p.bs + r;
+    const long long gr = (long long)qi * p.bs + r;
     float acc = 0.f;
-    if (gr < p.L)
+    if (gr < p.Lq)
       for (int d = 0; d < D; ++d) acc = fmaf(o[gr * p.oi_sl + d], sdo[r * LD + d], acc);
     sD[r] = acc;
     p.dvec[bh * p.Lp + gr] = acc;
@@ -800,14 +803,14 @@ __global__ void __launch_bounds__(256) attn_dq_f32_kernel(const AttnParams p) {
     }
   }
   if (p.dgate) {
-    float *dg = p.dgate + (bh * p.nblk + qblk) * (long long)p.kk;
+    float *dg = p.dgate + (bh * p.nq + qi) * (long long)p.kk;
     for (int j = tid; j < p.kk; j += 256) dg[j] = j < kMaxKK ? s_dg[j] : 0.f;
   }
   float *dq = reinterpret_cast<float *>(p.dq) + b * p.dq_sb + h * p.dq_sh;
   for (int i = tid; i < BS * D; i += 256) {
     const int r = i / D, d = i % D;
-    const long long gr = (long long)qblk * p.bs + r;
-    if (gr < p.L) dq[gr * p.dq_sl + d] = sdq[r * LD + d] * p.scale;
+    const long long gr = (long long)qi * p.bs + r;
+    if (gr < p.Lq) dq[gr * p.dq_sl + d] = sdq[r * LD + d] * p.scale;
   }
 }
 
@@ -855,27 +858,27 @@ __global__ void __launch_bounds__(256) attn_dkdv_f32_kernel(const AttnParams p, 
   }
   for (int ei = e_beg; ei < e_end; ++ei) {
     const int e = pl.col[ei];
-    const int qblk = e / p.kk, slot = e % p.kk;
+    const int qi = e / p.kk, slot = e % p.kk, qblk = p.q0 + qi;
     const bool triu = p.causal && ((p.mask_mode == BSA_MASK_SLOT) ? slot == 0 : kb == qblk);
     for (int g = 0; g < p.grp; ++g) {
       const int h = hk * p.grp + g;
       const long long bh = (long long)b * p.Hq + h;
       const float gv = p.gate ? p.gate[b * p.gate_sb + hk * p.gate_sh +
-                                       (long long)qblk * p.gate_sn + slot]
+                                       (long long)qi * p.gate_sn + slot]
                               : 0.f;
       const float *q = reinterpret_cast<const float *>(p.q) + b * p.q_sb + h * p.q_sh;
       const float *dO = reinterpret_cast<const float *>(p.dout) + b * p.do_sb + h * p.do_sh;
       __syncthreads();
       for (int i = tid; i < BS * D; i += 256) {
         const int r = i / D, d = i % D;
-        const long long gr = (long long)qblk * p.bs + r;
-        const bool ok = gr < p.L;
+        const long long gr = (long long)qi * p.bs + r;
+        const bool ok = gr < p.Lq;
         sq[r * LD + d] = ok ? q[gr * p.q_sl + d] : 0.f;
         sdo[r * LD + d] = ok ? dO[gr * p.do_sl + d] : 0.f;
       }
       for (int r = tid; r < BS; r += 256) {
-        slse[r] = p.lse[bh * p.Lp + (long long)qblk * p.bs + r] / kLog2e;
-        sD[r] = p.dvec[bh * p.Lp + (long long)qblk * p.bs + r];
+        slse[r] = p.lse[bh * p.Lp + (long long)qi * p.bs + r] / kLog2e;
+        sD[r] = p.dvec[bh * p.Lp + (long long)qi * p.bs + r];
       }
       __syncthreads();
       for (int i = tid; i < BS * BS; i += 256) {
@@ -885,7 +888,7 @@ __global__ void __launch_bounds__(256) attn_dkdv_f32_kernel(const AttnParams p, 
           s = fmaf(sq[r * LD + d], sk[c * LD + d], s);
           dp = fmaf(sdo[r * LD + d], sv[c * LD + d], dp);
         }
-        const bool masked = (triu && c > r) || ((long long)qblk * p.bs + r >= p.L) ||
+        const bool masked = (triu && c > r) || ((long long)qi * p.bs + r >= p.Lq) ||
                             ((long long)kb * p.bs + c >= p.L);
         const float pr = masked ? 0.f : expf(s * p.scale + gv - slse[r]);
         sP[r * LP + c] = pr;
@@ -941,7 +944,14 @@ struct BwdWs {
   size_t total;
 };
 
+// local query blocks of an attention call (its query range; all blocks unsharded)
+static int attn_nq(const bsa_attn_args *a) {
+  const int Lq = a->Lq > 0 ? a->Lq : a->L;
+  return (Lq + a->bs - 1) / a->bs;
+}
+
 static void csr_args_from(const bsa_attn_args *a, bsa_csr_args *c) {
+  *c = bsa_csr_args{};
   c->B = a->B;
   c->Hs = a->sel_sh == 0 ? 1 : a->Hkv;
   c->nblk = a->nblk;
@@ -955,14 +965,16 @@ static void csr_args_from(const bsa_attn_args *a, bsa_csr_args *c) {
   c->sel_sh = a->sel_sh;
   c->sel_sn = a->sel_sn;
   c->status = a->status;
+  c->q_blk0 = a->q_blk0;
+  c->nq = attn_nq(a);
 }
 
 static size_t bwd_layout(const bsa_attn_args *a, BwdWs *w, uint8_t *base) {
   bsa_csr_args c;
   csr_args_from(a, &c);
-  const long long Lp = (long long)a->nblk * a->bs;
+  const long long Lp = (long long)attn_nq(a) * a->bs;
   const long long nbins = (long long)a->B * c.Hs * a->nblk;
-  const long long E = nbins * a->kk;
+  const long long E = (long long)a->B * c.Hs * attn_nq(a) * a->kk;
   const int Y = a->Hkv / c.Hs;
   const long long pmax = 2 * ((E + kChunkEntries - 1) / kChunkEntries) + 1;
   size_t scan_bytes = 0;
@@ -1012,15 +1024,15 @@ static bsa_status launch_bwd_tc(const bsa_attn_args *a, const AttnParams &p, con
   using K = DkvCfg<BS, D>;
   TensorMap4 mq, mdo, mk, mv, mqc, mdoc;
   bsa_status s;
-  if ((s = make_tmap(&mq, a->q.ptr, a->dtype, a->B, a->Hq, a->L, D, a->q.sb, a->q.sh, a->q.sl, BS, "q")))
+  if ((s = make_tmap(&mq, a->q.ptr, a->dtype, a->B, a->Hq, p.Lq, D, a->q.sb, a->q.sh, a->q.sl, BS, "q")))
     return s;
-  if ((s = make_tmap(&mdo, a->dout.ptr, a->dtype, a->B, a->Hq, a->L, D, a->dout.sb, a->dout.sh,
+  if ((s = make_tmap(&mdo, a->dout.ptr, a->dtype, a->B, a->Hq, p.Lq, D, a->dout.sb, a->dout.sh,
                      a->dout.sl, BS, "dout")))
     return s;
-  if ((s = make_tmap(&mqc, a->q.ptr, a->dtype, a->B, a->Hq, a->L, D, a->q.sb, a->q.sh, a->q.sl,
+  if ((s = make_tmap(&mqc, a->q.ptr, a->dtype, a->B, a->Hq, p.Lq, D, a->q.sb, a->q.sh, a->q.sl,
                      Q::KC, "q")))
     return s;
-  if ((s = make_tmap(&mdoc, a->dout.ptr, a->dtype, a->B, a->Hq, a->L, D, a->dout.sb, a->dout.sh,
+  if ((s = make_tmap(&mdoc, a->dout.ptr, a->dtype, a->B, a->Hq, p.Lq, D, a->dout.sb, a->dout.sh,
                      a->dout.sl, Q::KC, "dout")))
     return s;
   // K/V: chunk boxes for dQ, full-block boxes for dK/dV
@@ -1046,7 +1058,7 @@ static bsa_status launch_bwd_tc(const bsa_attn_args *a, const AttnParams &p, con
   } else {
     auto kq = attn_dq_kernel<T, BS, D>;
     cudaFuncSetAttribute(kq, cudaFuncAttributeMaxDynamicSharedMemorySize, Q::SMEM);
-    const long long grid = (long long)a->B * a->Hq * a->nblk;
+    const long long grid = (long long)a->B * a->Hq * p.nq;
     kq<<<(unsigned)grid, Q::NT, Q::SMEM, st>>>(mq.map, mdo.map, mkc.map, mvc.map, pk(mq), pk(mdo),
                                                 pk(mkc), pk(mvc), p);
     if ((s = check_launch("attn_dq"))) return s;
@@ -1073,7 +1085,7 @@ static bsa_status launch_bwd_f32(const AttnParams &p, const BwdPlan &pl, long lo
   using C = F32BwdCfg<BS, D>;
   auto kq = attn_dq_f32_kernel<BS, D>;
   cudaFuncSetAttribute(kq, cudaFuncAttributeMaxDynamicSharedMemorySize, C::DQ_SMEM);
-  const long long grid = (long long)p.B * p.Hq * p.nblk;
+  const long long grid = (long long)p.B * p.Hq * p.nq;
   kq<<<(unsigned)grid, 256, C::DQ_SMEM, st>>>(p);
   if (bsa_status s = check_launch("attn_dq_f32")) return s;
   auto kk = attn_dkdv_f32_kernel<BS, D>;
@@ -1119,7 +1131,7 @@ bsa_status run_attn_bwd(const bsa_attn_args *a, void *ws, size_t ws_bytes, cudaS
   pl.col = w.col;
   pl.plan = w.plan;
   pl.part = w.part;
-  const long long E = (long long)nbins * a->kk;
+  const long long E = (long long)a->B * c.Hs * attn_nq(a) * a->kk;
   pl.npart = 2 * ((E + kChunkEntries - 1) / kChunkEntries) + 1;
   pl.ncol = (int)E;
   const long long dkv_grid = nbins + (E + kChunkEntries - 1) / kChunkEntries;

@@ -203,7 +203,7 @@ __global__ void __launch_bounds__(320, 1)
             if (j >= w.n[t]) continue;
             int qblk, slot, h;
             item(w, t, j, qblk, slot, h);
-            if (qblk < 0 || qblk >= p.nblk || h < 0 || h >= p.Hq || w.b[t] < 0 || w.b[t] >= p.B) {
+            if (qblk < 0 || qblk >= p.nq || h < 0 || h >= p.Hq || w.b[t] < 0 || w.b[t] >= p.B) {
               report(p.status, BSA_DEVERR_INDEX);  // self-check: keep every address in range
               qblk = 0;
               h = 0;
@@ -354,15 +354,16 @@ __global__ void __launch_bounds__(320, 1)
         if (active) {
           int qblk, slot, h;
           item(w, t, j, qblk, slot, h);
-          const bool triu = p.causal && ((p.mask_mode == BSA_MASK_SLOT) ? slot == 0 : kb == qblk);
+          // qblk is the local query block; kb is global
+          const bool triu = p.causal && ((p.mask_mode == BSA_MASK_SLOT) ? slot == 0 : kb == p.q0 + qblk);
           const float g2 = gbase ? __ldg(gbase + (long long)qblk * p.gate_sn + slot) * kLog2e : 0.f;
           const float *lsep = sRow + (st * 2 + t) * 2 * B5_BS + 32 * hf;
           const long long q0 = (long long)qblk * p.bs + 32 * hf;
-          if (triu || !key_ok || q0 + 32 > p.L) {  // diagonal / padded steps: explicit masks
+          if (triu || !key_ok || q0 + 32 > p.Lq) {  // diagonal / padded steps: explicit masks
 #pragma unroll
             for (int c = 0; c < 32; ++c) {
               const int qc = 32 * hf + c;
-              if (!key_ok || (triu && kr > qc) || q0 + c >= p.L) sv[c] = -INFINITY;
+              if (!key_ok || (triu && kr > qc) || q0 + c >= p.Lq) sv[c] = -INFINITY;
             }
           }
 #pragma unroll

@@ -43,7 +43,7 @@ __global__ void dvec_kernel(const AttnParams p, int D) {
     const long long bh = r / p.Lp;
     const int h = (int)(bh % p.Hq), b = (int)(bh / p.Hq);
     float acc = 0.f;
-    if (row < p.L) {
+    if (row < p.Lq) {
       const T *po = reinterpret_cast<const T *>(p.oin) + b * p.oi_sb + h * p.oi_sh + (long long)row * p.oi_sl;
       const T *pd = reinterpret_cast<const T *>(p.dout) + b * p.do_sb + h * p.do_sh + (long long)row * p.do_sl;
       for (int c = lane * 8; c < D; c += 64) {
@@ -99,7 +99,7 @@ struct Q5Unit {
 };
 
 __device__ __forceinline__ void q5_unit(const AttnParams &p, int u, Q5Unit &w) {
-  const int npairs = (p.nblk + 1) >> 1;
+  const int npairs = (p.nq + 1) >> 1;
   const int pair = u % npairs;
   const int bh = u / npairs;
   w.h = bh % p.Hq;
@@ -108,10 +108,10 @@ __device__ __forceinline__ void q5_unit(const AttnParams &p, int u, Q5Unit &w) {
   w.qb0 = 2 * pair;
 #pragma unroll
   for (int t = 0; t < 2; ++t) {
-    const int qblk = w.qb0 + t;
-    w.valid[t] = qblk < p.nblk;
+    const int qi = w.qb0 + t, qblk = p.q0 + qi;  // local / global query block
+    w.valid[t] = qi < p.nq;
     w.n[t] = 0;
-    w.selrow[t] = p.sel + w.b * p.sel_sb + w.hk * p.sel_sh + (long long)(w.valid[t] ? qblk : 0) * p.sel_sn;
+    w.selrow[t] = p.sel + w.b * p.sel_sb + w.hk * p.sel_sh + (long long)(w.valid[t] ? qi : 0) * p.sel_sn;
     if (!w.valid[t]) continue;
     int n = 0;
     for (int s = 0; s < p.kk; ++s) {
@@ -147,7 +147,7 @@ __global__ void __launch_bounds__(320, 1)
   __shared__ float s_dg[Q5_MAXN][2][8];  // per (step, tile, warp) sums of dS
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int npairs = (p.nblk + 1) >> 1;
+  const int npairs = (p.nq + 1) >> 1;
   const int nunits = p.B * p.Hq * npairs;
   if (tid == 0) {
     mbar_init(&qd_full, 1);
@@ -208,7 +208,7 @@ __global__ void __launch_bounds__(320, 1)
           for (int t = 0; t < 2; ++t) {
             if (j >= w.n[t]) continue;
             int slot;
-            const int it = q5_next(p, cur[t], w.qb0 + t, slot);
+            const int it = q5_next(p, cur[t], p.q0 + w.qb0 + t, slot);
             const int kb = it >> 3;
             uint8_t *dst = sR + (st * 2 + t) * 2 * Q5_TILE;
             tma_load_rhb(dst, &tk, &r_full[st], perm_k, 0, kb * p.bs, w.hk, w.b);
@@ -318,16 +318,16 @@ __global__ void __launch_bounds__(320, 1)
       Q5Unit w;
       q5_unit(p, u, w);
       const int ns = max(w.n[0], w.n[1]);
-      const int qblk = w.qb0 + t, nmine = w.n[t];
+      const int qi = w.qb0 + t, qblk = p.q0 + qi, nmine = w.n[t];
       const long long bh = (long long)w.b * p.Hq + w.h;
-      const long long grow = (long long)qblk * p.bs + r;
+      const long long grow = (long long)qi * p.bs + r;
       float lse2 = 0.f, dv = 0.f;
       if (w.valid[t]) {
         lse2 = p.lse[bh * p.Lp + grow];
         dv = p.dvec[bh * p.Lp + grow];
       }
       const float *gaterow =
-          (p.gate && w.valid[t]) ? p.gate + w.b * p.gate_sb + w.hk * p.gate_sh + (long long)qblk * p.gate_sn
+          (p.gate && w.valid[t]) ? p.gate + w.b * p.gate_sb + w.hk * p.gate_sh + (long long)qi * p.gate_sn
                                  : nullptr;
       Q5Cursor cur = {w.selrow[t], 0};
       for (int j = 0; j < ns; ++j, ++gs) {
@@ -364,7 +364,7 @@ __global__ void __launch_bounds__(320, 1)
             dgs += d0 + d1;
             wd[c >> 1] = Mma<T>::pack(d0, d1);
           }
-          if (grow >= p.L) dgs = 0.f;
+          if (grow >= p.Lq) dgs = 0.f;
         }
         if (p.dgate) {  // per-warp, per-tile partial of sum(dS) for this step
 #pragma unroll
@@ -405,25 +405,25 @@ __global__ void __launch_bounds__(320, 1)
         // thread i < 2*kk writes slot (i % kk) of tile (i / kk)
         for (int i = warp * 32 + lane; i < 2 * p.kk; i += 256) {
           const int tt = i / p.kk, slot = i % p.kk;
-          const int qb = w.qb0 + tt;
-          if (qb >= p.nblk) continue;
+          const int qb = w.qb0 + tt;  // local
+          if (qb >= p.nq) continue;
           // live slots of tile tt in order: its j-th live slot is `slot`?
           Q5Cursor c2 = {w.selrow[tt], 0};
           float v = 0.f;
           for (int jj = 0; jj < Q5_MAXN; ++jj) {
             int sl;
-            if (q5_next(p, c2, qb, sl) < 0) break;
+            if (q5_next(p, c2, p.q0 + qb, sl) < 0) break;
             if (sl == slot) {
 #pragma unroll
               for (int wv = 0; wv < 8; ++wv) v += s_dg[jj][tt][wv];
               break;
             }
           }
-          p.dgate[(((long long)w.b * p.Hq + w.h) * p.nblk + qb) * p.kk + slot] = v;
+          p.dgate[(((long long)w.b * p.Hq + w.h) * p.nq + qb) * p.kk + slot] = v;
         }
         asm volatile("bar.sync 1, 256;" ::: "memory");
       }
-      if (!w.valid[t] || grow >= p.L) continue;
+      if (!w.valid[t] || grow >= p.Lq) continue;
       if (nmine == 0) {
 #pragma unroll
         for (int c = 0; c < 32; ++c) dq[c] = 0.f;
@@ -474,7 +474,7 @@ bsa_status launch_dq_sm100(int dtype, const CUtensorMap &mq, const CUtensorMap &
   int dev = 0, nsm = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-  const long long units = (long long)p.B * p.Hq * ((p.nblk + 1) / 2);
+  const long long units = (long long)p.B * p.Hq * ((p.nq + 1) / 2);
   const unsigned grid = (unsigned)std::max<long long>(1, std::min<long long>(nsm, units));
   if (dtype == BSA_BF16) {
     auto kern = attn_dq_sm100_kernel<__nv_bfloat16>;

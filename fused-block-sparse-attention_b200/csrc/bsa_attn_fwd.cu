@@ -51,17 +51,18 @@ __global__ void __launch_bounds__(TileCfg<BS, D>::NT)
   long long id = blockIdx.x;
   const int gi = (int)(id % p.grp);
   id /= p.grp;
-  const int qblk = (int)(id % p.nblk);
-  id /= p.nblk;
+  const int qi = (int)(id % p.nq);  // local query block; qblk is its global index
+  id /= p.nq;
+  const int qblk = p.q0 + qi;
   const int hk = (int)(id % p.Hkv);
   const int b = (int)(id / p.Hkv);
   const int h = hk * p.grp + gi;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   const int32_t *selrow =
-      p.sel ? p.sel + b * p.sel_sb + hk * p.sel_sh + (long long)qblk * p.sel_sn : nullptr;
+      p.sel ? p.sel + b * p.sel_sb + hk * p.sel_sh + (long long)qi * p.sel_sn : nullptr;
   const float *gaterow =
-      p.gate ? p.gate + b * p.gate_sb + hk * p.gate_sh + (long long)qblk * p.gate_sn : nullptr;
+      p.gate ? p.gate + b * p.gate_sb + hk * p.gate_sh + (long long)qi * p.gate_sn : nullptr;
 
   if (selrow)
     build_slot_table(s_slot, selrow, p.kk, qblk, p.nblk, p.bs, p.L, p.mask_mode, p.causal,
@@ -121,7 +122,7 @@ __global__ void __launch_bounds__(TileCfg<BS, D>::NT)
     mbar_expect_tx(&bar[NST], Cfg::TILE);
 #pragma unroll
     for (int r = 0; r < D / 64; ++r)
-      tma_load_rhb(sQ + r * BS * 128, &tq, &bar[NST], perm_q, r * 64, qblk * p.bs, h, b);
+      tma_load_rhb(sQ + r * BS * 128, &tq, &bar[NST], perm_q, r * 64, qi * p.bs, h, b);
     for (int s = 0; s < NST; ++s) {
       int kb = 0;
       const int item = next_item(kb);
@@ -274,8 +275,8 @@ __global__ void __launch_bounds__(TileCfg<BS, D>::NT)
   const float inv1 = l1 > 0.f ? 1.f / l1 : 0.f;
   const long long bh = (long long)b * p.Hq + h;
   if (p.lse && (lane & 3) == 0) {
-    p.lse[bh * p.Lp + (long long)qblk * p.bs + r0] = l0 > 0.f ? m0 + __log2f(l0) : INFINITY;
-    p.lse[bh * p.Lp + (long long)qblk * p.bs + r1] = l1 > 0.f ? m1 + __log2f(l1) : INFINITY;
+    p.lse[bh * p.Lp + (long long)qi * p.bs + r0] = l0 > 0.f ? m0 + __log2f(l0) : INFINITY;
+    p.lse[bh * p.Lp + (long long)qi * p.bs + r1] = l1 > 0.f ? m1 + __log2f(l1) : INFINITY;
   }
   // stage O (rounded to T) in the Q region, then 16-byte coalesced stores
 #pragma unroll
@@ -291,8 +292,8 @@ __global__ void __launch_bounds__(TileCfg<BS, D>::NT)
   const T *gbase = p.og ? reinterpret_cast<const T *>(p.og) + b * p.og_sb + h * p.og_sh : nullptr;
   for (int idx = tid; idx < BS * (D / 8); idx += NT) {
     const int row = idx / (D / 8), c8 = idx % (D / 8);
-    const long long grow = (long long)qblk * p.bs + row;
-    if (grow >= p.L) continue;
+    const long long grow = (long long)qi * p.bs + row;
+    if (grow >= p.Lq) continue;
     uint4 val;
     asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
                  : "=r"(val.x), "=r"(val.y), "=r"(val.z), "=r"(val.w)
@@ -342,16 +343,17 @@ __global__ void __launch_bounds__(256) attn_fwd_f32_kernel(const AttnParams p) {
   long long id = blockIdx.x;
   const int gi = (int)(id % p.grp);
   id /= p.grp;
-  const int qblk = (int)(id % p.nblk);
-  id /= p.nblk;
+  const int qi = (int)(id % p.nq);  // local query block; qblk is its global index
+  id /= p.nq;
+  const int qblk = p.q0 + qi;
   const int hk = (int)(id % p.Hkv);
   const int b = (int)(id / p.Hkv);
   const int h = hk * p.grp + gi;
   const int tid = threadIdx.x;
   const int32_t *selrow =
-      p.sel ? p.sel + b * p.sel_sb + hk * p.sel_sh + (long long)qblk * p.sel_sn : nullptr;
+      p.sel ? p.sel + b * p.sel_sb + hk * p.sel_sh + (long long)qi * p.sel_sn : nullptr;
   const float *gaterow =
-      p.gate ? p.gate + b * p.gate_sb + hk * p.gate_sh + (long long)qblk * p.gate_sn : nullptr;
+      p.gate ? p.gate + b * p.gate_sb + hk * p.gate_sh + (long long)qi * p.gate_sn : nullptr;
   if (selrow)
     build_slot_table(s_slot, selrow, p.kk, qblk, p.nblk, p.bs, p.L, p.mask_mode, p.causal,
                      p.status);
@@ -360,8 +362,8 @@ __global__ void __launch_bounds__(256) attn_fwd_f32_kernel(const AttnParams p) {
   const float *v = reinterpret_cast<const float *>(p.v) + b * p.v_sb + hk * p.v_sh;
   for (int i = tid; i < BS * D; i += 256) {
     const int r = i / D, d = i % D;
-    const long long gr = (long long)qblk * p.bs + r;
-    sq[r * LD + d] = gr < p.L ? q[gr * p.q_sl + d] : 0.f;
+    const long long gr = (long long)qi * p.bs + r;
+    sq[r * LD + d] = gr < p.Lq ? q[gr * p.q_sl + d] : 0.f;
     sacc[r * LD + d] = 0.f;
   }
   for (int r = tid; r < BS; r += 256) {
@@ -431,8 +433,8 @@ __global__ void __launch_bounds__(256) attn_fwd_f32_kernel(const AttnParams p) {
   const float *og = p.og ? reinterpret_cast<const float *>(p.og) + b * p.og_sb + h * p.og_sh : nullptr;
   for (int i = tid; i < BS * D; i += 256) {
     const int r = i / D, d = i % D;
-    const long long gr = (long long)qblk * p.bs + r;
-    if (gr >= p.L) continue;
+    const long long gr = (long long)qi * p.bs + r;
+    if (gr >= p.Lq) continue;
     float val = sl[r] > 0.f ? sacc[r * LD + d] / sl[r] : 0.f;
     if (og) val = val * (1.f / (1.f + expf(-og[gr * p.og_sl + d])));
     o[gr * p.o_sl + d] = val;
@@ -440,7 +442,7 @@ __global__ void __launch_bounds__(256) attn_fwd_f32_kernel(const AttnParams p) {
   if (p.lse) {
     const long long bh = (long long)b * p.Hq + h;
     for (int r = tid; r < BS; r += 256)
-      p.lse[bh * p.Lp + (long long)qblk * p.bs + r] =
+      p.lse[bh * p.Lp + (long long)qi * p.bs + r] =
           sl[r] > 0.f ? (sm[r] + logf(sl[r])) * kLog2e : INFINITY;
   }
 }
@@ -451,7 +453,7 @@ static bsa_status launch_fwd_tc(const bsa_attn_args *a, const AttnParams &p, cud
   using Cfg = FwdCfg<BS, D>;
   TensorMap4 mq, mk, mv;
   bsa_status s;
-  if ((s = make_tmap(&mq, a->q.ptr, a->dtype, a->B, a->Hq, a->L, D, a->q.sb, a->q.sh, a->q.sl, BS,
+  if ((s = make_tmap(&mq, a->q.ptr, a->dtype, a->B, a->Hq, p.Lq, D, a->q.sb, a->q.sh, a->q.sl, BS,
                      "q")))
     return s;
   if ((s = make_tmap(&mk, a->k.ptr, a->dtype, a->B, a->Hkv, a->L, D, a->k.sb, a->k.sh, a->k.sl,
@@ -463,7 +465,7 @@ static bsa_status launch_fwd_tc(const bsa_attn_args *a, const AttnParams &p, cud
   auto pk = [](const TensorMap4 &m) { return m.perm[0] | (m.perm[1] << 2) | (m.perm[2] << 4); };
   auto kern = attn_fwd_kernel<T, BS, D>;
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
-  const long long grid = (long long)a->B * a->Hq * a->nblk;
+  const long long grid = (long long)a->B * a->Hq * p.nq;
   kern<<<(unsigned)grid, Cfg::NT, Cfg::SMEM, st>>>(mq.map, mk.map, mv.map, pk(mq), pk(mk), pk(mv),
                                                     p);
   return check_launch("attn_fwd");
@@ -504,7 +506,7 @@ bsa_status run_attn_fwd(const bsa_attn_args *a, cudaStream_t st) {
   bsa_status s = fill_attn_params(a, &p, false);
   if (s) return s;
   if (a->dtype == BSA_F32) {
-    const long long grid = (long long)a->B * a->Hq * a->nblk;
+    const long long grid = (long long)a->B * a->Hq * p.nq;
 #define BSA_F32_CASE(BS_, D_) \
   if (a->bs == BS_ && a->D == D_) return launch_fwd_f32<BS_, D_>(p, grid, st);
     BSA_F32_CASE(16, 64)

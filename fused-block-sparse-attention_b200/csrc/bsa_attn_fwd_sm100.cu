@@ -94,7 +94,7 @@ __global__ void __launch_bounds__(192, 1)
   __shared__ int s_n[2];
 
   // ---- CTA coordinates: (b, kv head, query-block pair, head in group)
-  const int npairs = (p.nblk + 1) >> 1;
+  const int npairs = (p.nq + 1) >> 1;
   long long id = blockIdx.x;
   const int gi = (int)(id % p.grp);
   id /= p.grp;
@@ -104,8 +104,8 @@ __global__ void __launch_bounds__(192, 1)
   const int b = (int)(id / p.Hkv);
   const int h = hk * p.grp + gi;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int qb0 = 2 * pair;
-  const bool validB = qb0 + 1 < p.nblk;
+  const int qb0 = 2 * pair;  // local index of tile A's query block
+  const bool validB = qb0 + 1 < p.nq;
 
 #ifdef BSA_TRACE
   if (p.trace && tid == 0) {
@@ -116,10 +116,10 @@ __global__ void __launch_bounds__(192, 1)
   // ---- live-slot lists of both tiles (one thread per tile)
   if (tid == 0 || tid == 32) {
     const int t = tid >> 5;
-    const int qblk = qb0 + t;
+    const int qi = qb0 + t, qblk = p.q0 + qi;
     int n = 0;
     if (t == 0 || validB) {
-      const int32_t *selrow = p.sel + b * p.sel_sb + hk * p.sel_sh + (long long)qblk * p.sel_sn;
+      const int32_t *selrow = p.sel + b * p.sel_sb + hk * p.sel_sh + (long long)qi * p.sel_sn;
       for (int slot = 0; slot < p.kk; ++slot) {
         const int kb = __ldg(selrow + slot);
         bool dup = false;
@@ -273,12 +273,12 @@ __global__ void __launch_bounds__(192, 1)
     // ================= softmax warps 0-3
     const int t = lane >> 4;            // tile of this thread
     const int r = warp * 16 + (lane & 15);  // query row within its block
-    const int qblk = qb0 + t;
+    const int qi = qb0 + t;                   // local query block (global p.q0 + qi)
     const int nmine = t ? nB : nA;
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
     const float *gaterow =
-        (p.gate && qblk < p.nblk)
-            ? p.gate + b * p.gate_sb + hk * p.gate_sh + (long long)qblk * p.gate_sn
+        (p.gate && qi < p.nq)
+            ? p.gate + b * p.gate_sb + hk * p.gate_sh + (long long)qi * p.gate_sn
             : nullptr;
     float m_used = -INFINITY, l = 0.f;
     float s[64];
@@ -384,11 +384,11 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
       for (int c = 0; c < 64; ++c) o[c] = 0.f;
     }
-    const long long grow = (long long)qblk * p.bs + r;
-    if (qblk < p.nblk) {
+    const long long grow = (long long)qi * p.bs + r;
+    if (qi < p.nq) {
       const long long bh = (long long)b * p.Hq + h;
       if (p.lse) p.lse[bh * p.Lp + grow] = l > 0.f ? m_used + __log2f(l) : INFINITY;
-      if (grow < p.L) {
+      if (grow < p.Lq) {
         const float inv = (nmine > 0 && l > 0.f) ? 1.f / l : 0.f;
         T *orow = reinterpret_cast<T *>(p.o) + b * p.o_sb + h * p.o_sh + grow * p.o_sl;
 #pragma unroll
@@ -423,14 +423,14 @@ bool fwd_sm100_applicable(const bsa_attn_args *a) {
 bsa_status launch_fwd_sm100(const bsa_attn_args *a, const AttnParams &p, cudaStream_t st) {
   TensorMap4 mq, mk, mv;
   bsa_status s;
-  if ((s = make_tmap(&mq, a->q.ptr, a->dtype, a->B, a->Hq, a->L, 64, a->q.sb, a->q.sh, a->q.sl, 64, "q")))
+  if ((s = make_tmap(&mq, a->q.ptr, a->dtype, a->B, a->Hq, p.Lq, 64, a->q.sb, a->q.sh, a->q.sl, 64, "q")))
     return s;
   if ((s = make_tmap(&mk, a->k.ptr, a->dtype, a->B, a->Hkv, a->L, 64, a->k.sb, a->k.sh, a->k.sl, 64, "k")))
     return s;
   if ((s = make_tmap(&mv, a->v.ptr, a->dtype, a->B, a->Hkv, a->L, 64, a->v.sb, a->v.sh, a->v.sl, 64, "v")))
     return s;
   auto pk = [](const TensorMap4 &m) { return m.perm[0] | (m.perm[1] << 2) | (m.perm[2] << 4); };
-  const long long grid = (long long)a->B * a->Hq * ((a->nblk + 1) / 2);
+  const long long grid = (long long)a->B * a->Hq * ((p.nq + 1) / 2);
 #ifdef BSA_TRACE
   AttnParams pt = p;
   if (const char *tp = getenv("BSA_TRACE_PTR")) pt.trace = (unsigned long long *)strtoull(tp, nullptr, 0);

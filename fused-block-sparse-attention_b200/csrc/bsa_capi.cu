@@ -50,6 +50,12 @@ bsa_status fill_attn_params(const bsa_attn_args *a, AttnParams *p, bool bwd) {
   if (a->sel && a->kk > kMaxKK)
     return fail(BSA_ERR_UNSUPPORTED, "attn: kk > 512 needs the identity selection");
   if (!(a->scale > 0.f) || !std::isfinite(a->scale)) return fail(BSA_ERR_ARG, "attn: bad scale");
+  const int Lq = a->Lq > 0 ? a->Lq : a->L;
+  if (a->q_blk0 < 0 || a->Lq < 0 || (long long)a->q_blk0 * a->bs + Lq > a->L ||
+      (Lq % a->bs && (long long)a->q_blk0 * a->bs + Lq != a->L))
+    return fail(BSA_ERR_SHAPE, "attn: query range must lie in [0, L) and end on a block or at L");
+  if (!a->sel && (a->q_blk0 || a->Lq))
+    return fail(BSA_ERR_UNSUPPORTED, "attn: a query range needs an explicit selection");
   const bool tc = a->dtype != BSA_F32;
   bsa_status s;
   if ((s = check_view(a->q, a->dtype, "q", tc)) || (s = check_view(a->k, a->dtype, "k", tc)) ||
@@ -79,7 +85,10 @@ bsa_status fill_attn_params(const bsa_attn_args *a, AttnParams *p, bool bwd) {
   P.bs = a->bs;
   P.mask_mode = a->mask_mode;
   P.causal = a->causal ? 1 : 0;
-  P.Lp = a->nblk * a->bs;
+  P.q0 = a->q_blk0;
+  P.Lq = Lq;
+  P.nq = (Lq + a->bs - 1) / a->bs;
+  P.Lp = P.nq * a->bs;
   P.scale = a->scale;
   P.scale2 = a->scale * 1.4426950408889634f;
   P.sel = a->sel;

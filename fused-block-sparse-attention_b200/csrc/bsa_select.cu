@@ -140,7 +140,9 @@ __global__ void __launch_bounds__(256) select_kernel(const bsa_select_args a, in
   float *B1 = As + dim * kLdA;               // [kDC][kLdA]
   float *B2 = B1 + kDC * kLdA;               // [kDC][kLdA]  (MAXDOT2 / QUEST)
   float *S = B2 + kDC * kLdA;                // [64][65]
-  const int ntiles = (a.nblk + kTile - 1) / kTile;
+  // query rows are local (nq of them, global block = qb0 + local); keys are global
+  const int nq = a.nq > 0 ? a.nq : a.nblk, qb0 = a.q_blk0;
+  const int ntiles = (nq + kTile - 1) / kTile, nktiles = (a.nblk + kTile - 1) / kTile;
   const int qt = ntiles - 1 - (int)blockIdx.x;  // heaviest causal tiles first
   const int g = blockIdx.y;
   const int q0 = qt * kTile;
@@ -148,12 +150,12 @@ __global__ void __launch_bounds__(256) select_kernel(const bsa_select_args a, in
   const int ty = tid >> 4, tx = tid & 15;
   const bool causal_like = a.layout == BSA_SEL_FINISH || a.causal;
 
-  const float *A = a.a + (long long)g * a.nblk * dim;
+  const float *A = a.a + (long long)g * nq * dim;
   const float *Bg1 = a.b1 + (long long)g * a.nblk * dim;
   const float *Bg2 = a.b2 ? a.b2 + (long long)g * a.nblk * dim : nullptr;
   for (int i = tid; i < kTile * dim; i += 256) {
     const int r = i / dim, d = i % dim;
-    As[d * kLdA + r] = (q0 + r < a.nblk) ? A[(long long)(q0 + r) * dim + d] : 0.f;
+    As[d * kLdA + r] = (q0 + r < nq) ? A[(long long)(q0 + r) * dim + d] : 0.f;
   }
 
   float es[8];
@@ -164,7 +166,8 @@ __global__ void __launch_bounds__(256) select_kernel(const bsa_select_args a, in
     ei[r] = INT_MAX;
   }
 
-  const int kt_last = causal_like ? qt : ntiles - 1;
+  const int kt_last = causal_like ? min(nktiles - 1, (qb0 + min(q0 + kTile, nq) - 1) / kTile)
+                                  : nktiles - 1;
   for (int kt = 0; kt <= kt_last; ++kt) {
     const int k0 = kt * kTile;
     float acc[4][4], acc2[4][4];
@@ -216,11 +219,11 @@ __global__ void __launch_bounds__(256) select_kernel(const bsa_select_args a, in
     // scores -> S with validity
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const int qi = q0 + ty * 4 + i;
+      const int qi = qb0 + q0 + ty * 4 + i;  // global query block
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const int kj = k0 + tx * 4 + j;
-        bool ok = qi < a.nblk && kj < a.nblk;
+        bool ok = q0 + ty * 4 + i < nq && kj < a.nblk;
         if (a.layout == BSA_SEL_SSA)
           ok = ok && kj != qi && (!a.causal || kj < qi);
         else
@@ -271,19 +274,20 @@ __global__ void __launch_bounds__(256) select_kernel(const bsa_select_args a, in
   int *scratch = reinterpret_cast<int *>(S) + warp * 128;
 #pragma unroll
   for (int r = 0; r < 8; ++r) {
-    const int row = q0 + warp * 8 + r;
-    if (row >= a.nblk) continue;  // warp-uniform
-    const long long ob = ((long long)g * a.nblk + row) * W;
+    const int lrow = q0 + warp * 8 + r;
+    if (lrow >= nq) continue;  // warp-uniform
+    const int row = qb0 + lrow;  // global query block
+    const long long ob = ((long long)g * nq + lrow) * W;
     const bool valid = lane < T && ei[r] != INT_MAX;
     if (a.layout == BSA_SEL_SSA) {
       float own = 0.f;
       if ((a.score_out || a.gate_out) && lane == 0) {
-        // the a-row of `row` is column (row - q0) of As
+        // the a-row of local row `lrow` is column (lrow - q0) of As
         float s = 0.f, s2 = 0.f;
         const float *b1r = Bg1 + (long long)row * dim;
         const float *b2r = Bg2 ? Bg2 + (long long)row * dim : nullptr;
         for (int d = 0; d < dim; ++d) {
-          const float av = As[d * kLdA + (row - q0)];
+          const float av = As[d * kLdA + (lrow - q0)];
           if (KIND == BSA_SCORE_QUEST)
             s = fmaf(av, av >= 0.f ? b1r[d] : b2r[d], s);
           else
@@ -345,7 +349,10 @@ bsa_status run_select(const bsa_select_args *a, cudaStream_t st) {
   if ((long long)a->G > 65535) return fail(BSA_ERR_SHAPE, "select: G > 65535");
   const int W = select_width(a);
   int T = a->layout == BSA_SEL_SSA ? W - 1 : std::min(a->topk, a->nblk);
-  const int ntiles = (a->nblk + kTile - 1) / kTile;
+  const int nq = a->nq > 0 ? a->nq : a->nblk;
+  if (a->q_blk0 < 0 || a->nq < 0 || (long long)a->q_blk0 + nq > a->nblk)
+    return fail(BSA_ERR_SHAPE, "select: query range outside [0, nblk)");
+  const int ntiles = (nq + kTile - 1) / kTile;
   const size_t smem = (size_t)(a->dim * kLdA + 2 * kDC * kLdA + kTile * 65) * 4;
   dim3 grid(ntiles, a->G);
   void (*kern)(const bsa_select_args, int, int) = nullptr;

@@ -98,6 +98,14 @@ typedef struct {
   float *lse;
   float *dgate; /* backward, optional: fp32 (B,Hq,nblk,kk) per-head d(loss)/d(gate) */
   int32_t *status;
+  /* Query-block range (a shard of the query side; 0, 0 = all queries): q, o,
+   * dout, dq, out_gate hold Lq rows that start at row q_blk0*bs of the sequence,
+   * i.e. the query blocks [q_blk0, q_blk0 + ceil(Lq/bs)); sel, gate, dgate, lse
+   * hold the rows of those blocks only; k, v, dk, dv cover the whole sequence
+   * (L rows, nblk blocks).  Masks use the global block indices.  Lq must be a
+   * multiple of bs unless the range ends at L.  No reference counterpart: used by
+   * the query-block sharding across GPUs. */
+  int32_t q_blk0, Lq;
 } bsa_attn_args;
 
 /* Forward: o = softmax(q k^T * scale + gate + mask) v over the selected blocks.
@@ -160,6 +168,11 @@ typedef struct {
   float *score_out;  /* optional (G, nblk, width) */
   float *gate_out;   /* optional (G, nblk, width) */
   int32_t *status;
+  /* query-block range (0, 0 = all): a holds the summaries of the query blocks
+   * [q_blk0, q_blk0 + nq) only and sel/score/gate their nq rows; b1/b2 keep all
+   * nblk key blocks; masks and the own block use global indices.  No reference
+   * counterpart: used by the query-block sharding across GPUs. */
+  int32_t q_blk0, nq;
 } bsa_select_args;
 int32_t bsa_select_width(const bsa_select_args *a);
 bsa_status bsa_select(const bsa_select_args *a, bsa_stream_t stream);
@@ -209,6 +222,9 @@ typedef struct {
   int64_t sel_sb, sel_sh, sel_sn;
   int32_t *row_ptr, *col;
   int32_t *status;
+  /* query-block range (0, 0 = all nblk): sel holds rows for the query blocks
+   * [q_blk0, q_blk0 + nq) and entries are e = (qblk - q_blk0)*kk + slot */
+  int32_t q_blk0, nq;
 } bsa_csr_args;
 size_t bsa_csr_workspace(const bsa_csr_args *a);
 bsa_status bsa_sel_csr(const bsa_csr_args *a, void *workspace, size_t workspace_bytes,

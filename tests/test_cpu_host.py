@@ -28,11 +28,30 @@ def test_header_symbols_exported():
     assert L.bsa_version() >= 100
 
 
-def test_struct_sizes_match_c_layout():
+def test_struct_layouts_match_the_header(tmp_path):
+    """The ctypes mirrors in _bsa must have the sizes and field offsets that a C
+    compiler gives the structs of include/bsa.h."""
+    import subprocess
     import _bsa
-    assert ctypes.sizeof(_bsa.View) == 32
-    assert ctypes.sizeof(_bsa.AttnArgs) == 48 + 9 * 32 + 4 * 8 + 4 * 8 + 3 * 8
-    assert ctypes.sizeof(_bsa.PoolArgs) == 32 + 32 + 4 * 8
+    structs = {"bsa_view": _bsa.View, "bsa_attn_args": _bsa.AttnArgs, "bsa_pool_args": _bsa.PoolArgs,
+               "bsa_select_args": _bsa.SelectArgs, "bsa_lsh_args": _bsa.LshArgs,
+               "bsa_csr_args": _bsa.CsrArgs, "bsa_rope_args": _bsa.RopeArgs}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "bsa.h"', "int main(void) {"]
+    for cname, cls in structs.items():
+        lines.append('printf("%s %%zu\\n", sizeof(%s));' % (cname, cname))
+        for f, _ in cls._fields_:
+            lines.append('printf("%s.%s %%zu\\n", offsetof(%s, %s));' % (cname, f, cname, f))
+    lines.append("return 0; }")
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    got = dict(l.split() for l in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                  check=True).stdout.splitlines())
+    for cname, cls in structs.items():
+        assert int(got[cname]) == ctypes.sizeof(cls), cname
+        for f, _ in cls._fields_:
+            assert int(got[cname + "." + f]) == getattr(cls, f).offset, (cname, f)
 
 
 def test_validation_errors_without_gpu():
