@@ -10,6 +10,8 @@ the total work is fixed ("strong" scaling); value = tokens of the whole job
 per second, timed on the device as the max over ranks.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py --config {2,3b,4,5} [--n N]     the other BASELINE configurations
+                                                   (one JSON line each, not the driver line)
 
 --impl reference times the CPU restatement of the reference's gather path
 (oracle/, the reference is Python and cannot be installed on the GPU box) on
@@ -372,6 +374,196 @@ def run_reference(a):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------- other configurations
+def _timed(fn, steps, warmup, flush, dev_index, phases=1):
+    """Runs fn(events) `steps` times after `warmup` untimed runs, flushing L2
+    before each timed run; fn records phases+1 events.  Returns (mean ms per
+    phase, clock summary)."""
+    for _ in range(warmup):
+        fn(None)
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(phases + 1)] for _ in range(steps)]
+    with ClockSampler(dev_index) as clk:
+        for i in range(steps):
+            flush.zero_()
+            fn(evs[i])
+        torch.cuda.synchronize()
+    ms = [statistics.mean(e[j].elapsed_time(e[j + 1]) for e in evs) for j in range(phases)]
+    return ms, clk.summary()
+
+
+def _line(metric, value, unit, ms, a, world, scaling, dtype, config, roofline, clocks, extra=None):
+    d = {"metric": metric, "value": round(value, 1), "unit": unit, "n_gpus": world, "steps": a.steps,
+         "warmup": a.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
+         "scaling": scaling, "vs_baseline": None, "dtype": dtype, "data": "synthetic N(0,1), seeded",
+         "config": config, "roofline": roofline, "clocks": clocks}
+    d.update(extra or {})
+    print(json.dumps(d), flush=True)
+
+
+def _roof(name, fl, ms, peak, src):
+    ach = fl / (ms * 1e-3) / 1e12
+    return {"kernel": name, "bound": "tensor", "achieved": round(ach, 2), "peak": peak,
+            "unit": "TFLOP/s", "frac": round(ach / peak, 4), "peak_source": src, "traffic": None}
+
+
+def run_config(a):
+    """BASELINE configurations 2, 3b, 4, 5 (see the module docstring of each branch)."""
+    import _bsa
+    import selection
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+    hbm, tf_burst, tf_sus, src = load_peaks()
+    psrc = "%s bf16_tflops_sustained" % src
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    g = torch.Generator(device=dev).manual_seed(11 + rank)
+
+    def rnd(*shape, scale=1.0):
+        return (torch.randn(*shape, generator=g, device=dev) * scale).to(torch.bfloat16)
+
+    if a.config == "2":
+        # small-LM training layer: B8 H8 N8192 D64 block 64, gate-coupled top-16 (+own)
+        B, H, N, D, bs, topk = 8, 8, 8192, 64, 64, 16
+        q, k, v = (rnd(B, H, N, D, scale=0.5) for _ in range(3))
+        do = rnd(B, H, N, D)
+
+        def fn(ev):
+            if ev:
+                ev[0].record()
+            sel, gate, _ = selection.select_meanpool(q, k, bs=bs, topk=topk, want_gate=True)
+            o, lse = _bsa.attn_fwd(q, k, v, sel, gate, bs=bs, causal=True)
+            _bsa.attn_bwd(q, k, v, o, do, sel, lse, gate, bs=bs, causal=True, want_dgate=True)
+            if ev:
+                ev[1].record()
+        (ms,), clk = _timed(fn, a.steps, a.warmup, flush, local)
+        fwd = 4.0 * B * H * N * (topk + 1) * bs * D
+        if rank == 0:
+            _line("layer fwd+bwd tokens/s (B8 H8 N8192, gate-coupled selection)", B * N / (ms * 1e-3),
+                  "tokens/s", ms, a, 1, "weak", "bf16",
+                  {"workload": "BASELINE config 2: B8 H8 N8192 D64 block64 top16 (+own) causal, "
+                               "gate = logsigmoid(selected scores), dgate computed", "B": B, "H": H,
+                   "N": N, "l2": "256 MB buffer written between timed steps"},
+                  _roof("selection+fwd+bwd", 3.5 * fwd, ms, tf_sus, psrc), clk)
+    elif a.config == "3b":
+        # long forward: B1 H8 D64 block 128 top-16 (+own), query blocks sharded over the ranks
+        import sharded
+        B, H, D, bs, topk = 1, 8, 64, 128, 16
+        N = a.n
+        if N % (world * bs):
+            raise SystemExit("N must be a multiple of world * 128")
+        Ls = N // world
+        q, k, v = (rnd(B, H, Ls, D) for _ in range(3))
+        m = sharded.ShardedBlockSparse(bs=bs, topk=topk, causal=True) if dist else None
+
+        def fn(ev):
+            if ev:
+                ev[0].record()
+            if m:
+                sel = m.select(q, k)
+                if ev:
+                    ev[1].record()
+                kf, vf = m.gather_kv(k, v)
+                o, _ = _bsa.attn_fwd(q, kf, vf, sel, bs=bs, causal=True, want_lse=False,
+                                     q_blk0=dist.get_rank() * (Ls // bs))
+            else:
+                sel, _, _ = selection.select_meanpool(q, k, bs=bs, topk=topk)
+                if ev:
+                    ev[1].record()
+                o, _ = _bsa.attn_fwd(q, k, v, sel, bs=bs, causal=True, want_lse=False)
+            if ev:
+                ev[2].record()
+        if dist:
+            dist.barrier()
+        (ms_sel, ms_fwd), clk = _timed(fn, a.steps, a.warmup, flush, local, phases=2)
+        vals = torch.tensor([ms_sel + ms_fwd, ms_sel, ms_fwd], device=dev)
+        if dist:
+            dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+        ms, ms_sel, ms_fwd = vals.tolist()
+        fwd = 4.0 * B * H * Ls * (topk + 1) * bs * D
+        if rank == 0:
+            _line("long-context fwd tokens/s at N=%d (selection + all-gather + forward)" % N,
+                  B * N / (ms * 1e-3), "tokens/s", ms, a, world, "strong", "bf16",
+                  {"workload": "BASELINE config 3b: forward only, B1 H8 N%d D64 block128 top16 "
+                               "(+own) causal, streaming top-k (no nblk^2 scores)" % N,
+                   "N": N, "parallelism": "query blocks sharded %d/rank, NCCL all-gather of K, V and "
+                                          "pooled keys" % (N // bs // world) if dist else "none",
+                   "l2": "256 MB buffer written between timed steps"},
+                  _roof("attn_fwd", fwd, ms_fwd, tf_sus, psrc), clk,
+                  {"phases": {"select(+pool/gather)": round(ms_sel, 3),
+                              "gather_kv+attn_fwd": round(ms_fwd, 3)}})
+    elif a.config == "4":
+        # Qwen GQA prefill: N65536 Hq16 Hkv2 D256 block 128, partial RoPE (64 dims, theta 1e7),
+        # SelectMax top-32 + own + sink, sigmoid output gate; also the all-blocks (dense) mode
+        import qwen_blocksparse as qb
+        B, Hq, Hkv, N, D, bs = 1, 16, 2, 65536, 256, 128
+        q = rnd(B, Hq, N, D)
+        k, v = rnd(B, Hkv, N, D), rnd(B, Hkv, N, D)
+        gate = rnd(B, N, Hq * D)
+        cos, sin = qb.rope_cos_sin(N, 64, 1e7, torch.bfloat16, dev)
+        sm = qb.SelectMax(32, bs)
+        out = {}
+        for mode, sel in (("select", sm), ("all_blocks", qb.SelectAll(bs))):
+            def fn(ev, sel=sel):
+                if ev:
+                    ev[0].record()
+                qb.qwen_attention(q, k, v, cos, sin, gate, selector=sel, topk=32, bs=bs)
+                if ev:
+                    ev[1].record()
+            (ms,), clk = _timed(fn, a.steps, a.warmup, flush, local)
+            out[mode] = (ms, clk)
+        ms, clk = out["select"]
+        kk = 34
+        fwd = 4.0 * B * Hq * N * kk * bs * D
+        dense = 2.0 * B * Hq * N * N * D      # causal dense: half of 4*N*N*D
+        if rank == 0:
+            _line("Qwen GQA prefill tokens/s (N65536 Hq16 Hkv2 D256, SelectMax top-32)",
+                  B * N / (ms * 1e-3), "tokens/s", ms, a, 1, "weak", "bf16",
+                  {"workload": "BASELINE config 4: RoPE(64 of 256 dims, theta 1e7) + SelectMax "
+                               "top32 + own + sink (width 34) + GQA attention + sigmoid gate",
+                   "N": N, "l2": "256 MB buffer written between timed steps"},
+                  _roof("rope+select+attn_fwd", fwd, ms, tf_sus, psrc), clk,
+                  {"all_blocks": {"ms": round(out["all_blocks"][0], 3),
+                                  "tokens_per_s": round(B * N / (out["all_blocks"][0] * 1e-3), 1),
+                                  "tflops": round(dense / out["all_blocks"][0] / 1e9, 1)}})
+    elif a.config == "5":
+        # LSH selector: B1 H8 N131072 D64 block 64, 4 sign planes x 4 rounds, cap 16, top-16
+        B, H, N, D, bs = 1, 8, 131072, 64, 64
+        q, k, v = (rnd(B, H, N, D) for _ in range(3))
+        planes = selection.lsh_planes(D, 4, 4, 0).to(dev)
+
+        def fn(ev):
+            if ev:
+                ev[0].record()
+            sel, _, _ = selection.select_lsh(q, k, bs=bs, topk=16, n_rounds=4, n_planes=4, cap=16,
+                                             planes=planes)
+            if ev:
+                ev[1].record()
+            _bsa.attn_fwd(q, k, v, sel, bs=bs, causal=True, want_lse=False)
+            if ev:
+                ev[2].record()
+        (ms_sel, ms_fwd), clk = _timed(fn, a.steps, a.warmup, flush, local, phases=2)
+        ms = ms_sel + ms_fwd
+        fwd = 4.0 * B * H * N * 17 * bs * D
+        if rank == 0:
+            _line("LSH-selected fwd tokens/s (N131072 H8, hash+bucket+candidates+read)",
+                  B * N / (ms * 1e-3), "tokens/s", ms, a, 1, "weak", "bf16",
+                  {"workload": "BASELINE config 5: B1 H8 N131072 D64 block64, pooled+normalised "
+                               "blocks, sign of 4 hyperplanes x 4 rounds, cap 16, top-16 (+own)",
+                   "N": N, "l2": "256 MB buffer written between timed steps"},
+                  _roof("attn_fwd", fwd, ms_fwd, tf_sus, psrc), clk,
+                  {"phases": {"lsh_select(pool+hash+bucket+select)": round(ms_sel, 3),
+                              "attn_fwd": round(ms_fwd, 3)}})
+    if dist:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -381,11 +573,17 @@ def main():
     ap.add_argument("--n", type=int, default=262144, help="sequence length (default 262144)")
     ap.add_argument("--cpu-sample", type=int, default=64, help="query blocks in the CPU sample")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--config", default="3a", choices=["3a", "2", "3b", "4", "5"],
+                    help="BASELINE configuration (3a = the driver line)")
     a = ap.parse_args()
     if a.warmup < 3:
         a.warmup = 3
     if a.impl == "reference":
         run_reference(a)
+    elif a.config != "3a":
+        if a.config == "3b" and a.n == 262144:
+            a.n = 1 << 20
+        run_config(a)
     else:
         run_ours(a)
 
