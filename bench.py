@@ -570,7 +570,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--n", type=int, default=262144, help="sequence length (default 262144)")
+    ap.add_argument("--seqlen", "--n", dest="n", type=int, default=262144,
+                    help="sequence length (default 262144; 1048576 for --config 3b)")
     ap.add_argument("--cpu-sample", type=int, default=64, help="query blocks in the CPU sample")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--config", default="3a", choices=["3a", "2", "3b", "4", "5"],
