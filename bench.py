@@ -34,6 +34,9 @@ for _p in (ROOT, PKG):
 import torch  # noqa: E402
 
 METRIC = "fwd+bwd tokens/s at 262k tok (selection+forward+backward)"
+# DRAM bytes per launch of each phase at N=262144, from the ncu launch list in
+# profiles/launches_bench262k.md (attn_bwd = dK/dV + dQ + reduce + CSR kernels).
+TRAFFIC_262K = {"attn_bwd": 5.22e9, "attn_fwd": 1.165e9, "select": 0.29e9}
 UNIT = "tokens/s"
 
 
@@ -273,7 +276,11 @@ def run_ours(a):
                              % (4 * q.numel() * 2 / 1e6)},
             "roofline": {"kernel": dom, "bound": "tensor", "achieved": round(achieved, 2),
                          "peak": tf_sus, "unit": "TFLOP/s", "frac": round(achieved / tf_sus, 4),
-                         "peak_source": "%s bf16_tflops_sustained" % src, "traffic": None},
+                         "peak_source": "%s bf16_tflops_sustained" % src,
+                         "traffic": TRAFFIC_262K.get(dom) if cfg["N"] == 262144 else None,
+                         "traffic_source": "ncu dram__bytes_read+write summed over the phase's "
+                                           "kernels, one capture, cold cache "
+                                           "(profiles/launches_bench262k.md)"},
             "phases": phases,
             "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 1), "unit": UNIT,
                     "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d * world,
