@@ -138,18 +138,14 @@ __global__ void plan_kernel(const int32_t *row_ptr, unsigned long long *plan_in,
   }
 }
 
-__device__ __forceinline__ int find_bin(const unsigned long long *plan, int nbins, unsigned x) {
-  // largest bin with chunk_off(bin) <= x
-  int lo = 0, hi = nbins - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if ((unsigned)(plan[mid] >> 32) <= x)
-      lo = mid;
-    else
-      hi = mid - 1;
+// chunk x -> its bin, for every chunk of the plan (consumers look bins up in O(1))
+__global__ void chunk_bin_kernel(const unsigned long long *plan, int nbins, int32_t *chunk_bin) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < nbins; i += gridDim.x * blockDim.x) {
+    const unsigned c0 = (unsigned)(plan[i] >> 32), c1 = (unsigned)(plan[i + 1] >> 32);
+    for (unsigned x = c0; x < c1; ++x) chunk_bin[x] = i;
   }
-  return lo;
 }
+
 
 // ------------------------------------------------------------------ dQ (tensor cores)
 template <int BS, int D>
@@ -453,7 +449,7 @@ __global__ void __launch_bounds__(TileCfg<BS, D>::NT)
   const unsigned x = blockIdx.x;
   const unsigned total = (unsigned)(pl.plan[pl.nbins] >> 32);
   if (x >= total) return;
-  const int bin = find_bin(pl.plan, pl.nbins, x);
+  const int bin = pl.chunk_bin[x];
   const unsigned chunk_off = (unsigned)(pl.plan[bin] >> 32);
   const unsigned part_off = (unsigned)(pl.plan[bin] & 0xffffffffu);
   const unsigned nch = (unsigned)(pl.plan[bin + 1] >> 32) - chunk_off;
@@ -833,7 +829,7 @@ __global__ void __launch_bounds__(256) attn_dkdv_f32_kernel(const AttnParams p, 
   const unsigned x = blockIdx.x;
   const unsigned total = (unsigned)(pl.plan[pl.nbins] >> 32);
   if (x >= total) return;
-  const int bin = find_bin(pl.plan, pl.nbins, x);
+  const int bin = pl.chunk_bin[x];
   const unsigned chunk_off = (unsigned)(pl.plan[bin] >> 32);
   const unsigned part_off = (unsigned)(pl.plan[bin] & 0xffffffffu);
   const unsigned nch = (unsigned)(pl.plan[bin + 1] >> 32) - chunk_off;
@@ -936,6 +932,7 @@ struct BwdWs {
   float *dvec;
   int32_t *row_ptr, *col;
   unsigned long long *plan_in, *plan;
+  int32_t *chunk_bin;
   void *csr_ws;
   size_t csr_bytes;
   void *scan_tmp;
@@ -991,6 +988,7 @@ static size_t bwd_layout(const bsa_attn_args *a, BwdWs *w, uint8_t *base) {
   w->col = (int32_t *)take(E * 4);
   w->plan_in = (unsigned long long *)take((nbins + 1) * 8);
   w->plan = (unsigned long long *)take((nbins + 1) * 8);
+  w->chunk_bin = (int32_t *)take((nbins + (E + kChunkEntries - 1) / kChunkEntries + 1) * 4);
   w->csr_bytes = sel_csr_workspace(&c);
   w->csr_ws = take(w->csr_bytes);
   w->scan_bytes = scan_bytes;
@@ -1122,6 +1120,8 @@ bsa_status run_attn_bwd(const bsa_attn_args *a, void *ws, size_t ws_bytes, cudaS
   if (cub::DeviceScan::ExclusiveSum(w.scan_tmp, tb, w.plan_in, w.plan, nbins + 1, st) !=
       cudaSuccess)
     return fail(BSA_ERR_LAUNCH, "attn_bwd: plan scan failed");
+  chunk_bin_kernel<<<(nbins + 255) / 256, 256, 0, st>>>(w.plan, nbins, w.chunk_bin);
+  if ((s = check_launch("chunk_bin"))) return s;
   BwdPlan pl;
   pl.Hs = c.Hs;
   pl.Y = a->Hkv / c.Hs;
@@ -1130,6 +1130,7 @@ bsa_status run_attn_bwd(const bsa_attn_args *a, void *ws, size_t ws_bytes, cudaS
   pl.row_ptr = w.row_ptr;
   pl.col = w.col;
   pl.plan = w.plan;
+  pl.chunk_bin = w.chunk_bin;
   pl.part = w.part;
   const long long E = (long long)a->B * c.Hs * attn_nq(a) * a->kk;
   pl.npart = 2 * ((E + kChunkEntries - 1) / kChunkEntries) + 1;

@@ -35,7 +35,7 @@ namespace bsa {
 #ifdef BSA_TRACE
 #define B5_TRACE(ev, j)                                                                  \
   do {                                                                                   \
-    if (p.trace && blockIdx.x == p.trace[1023] && (j) < 128) p.trace[(ev) * 128 + (j)] = clock64(); \
+    if (b5_tr && (j) < 128) p.trace[(ev) * 128 + (j)] = clock64();                  \
   } while (0)
 #else
 #define B5_TRACE(ev, j) \
@@ -55,18 +55,6 @@ constexpr uint32_t B5_TMEM_COLS = 512;
 constexpr int B5_SCOL = 0, B5_DPCOL = 128, B5_DVCOL = 256, B5_DKCOL = 320;  // +128: 2nd acc buffer
 }  // namespace
 
-__device__ __forceinline__ int b5_find_bin(const unsigned long long *plan, int nbins, unsigned x) {
-  int lo = 0, hi = nbins - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if ((unsigned)(plan[mid] >> 32) <= x)
-      lo = mid;
-    else
-      hi = mid - 1;
-  }
-  return lo;
-}
-
 // Work unit u -> (two chunks of the plan, KV head within the bin group).
 struct B5Unit {
   int n[2], kb[2], b[2], hk[2], ebeg[2], nch[2], cidx[2], poff[2];
@@ -85,7 +73,7 @@ __device__ __forceinline__ void b5_unit(const BwdPlan &pl, const AttnParams &p, 
     w.kb[t] = w.b[t] = w.hk[t] = w.ebeg[t] = w.cidx[t] = w.poff[t] = 0;
     w.nch[t] = 1;
     if (!w.valid[t]) continue;
-    const int bin = b5_find_bin(pl.plan, pl.nbins, x);
+    const int bin = pl.chunk_bin[x];
     const unsigned coff = (unsigned)(pl.plan[bin] >> 32);
     w.poff[t] = (int)(pl.plan[bin] & 0xffffffffu);
     w.nch[t] = (int)((unsigned)(pl.plan[bin + 1] >> 32) - coff);
@@ -124,9 +112,16 @@ __global__ void __launch_bounds__(320, 1)
   __shared__ __align__(8) uint64_t kv_full, kv_empty, r_full[B5_NST], r_empty[B5_NST],
       s_full[2], s_empty[2], p_full[2], g_done[2], acc_empty[2];
   __shared__ uint32_t tmem_base_sh;
+  // per ring stage and tile: (local query block, slot, query head) and the gate
+  // value of the step, written by the producer before it arrives on r_full
+  __shared__ int s_meta[B5_NST][2][3];
+  __shared__ float s_g2[B5_NST][2];
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const unsigned total = (unsigned)(pl.plan[pl.nbins] >> 32);
+#ifdef BSA_TRACE
+  const bool b5_tr = p.trace && blockIdx.x == p.trace[1023];
+#endif
   const int nunits = (int)((total + 1) / 2) * pl.Y;
 
   if (tid == 0) {
@@ -198,7 +193,7 @@ __global__ void __launch_bounds__(320, 1)
           idle = 0;
           B5_TRACE(0, gs);
           const int act = (j < w.n[0]) + (j < w.n[1]);
-          mbar_expect_tx(&r_full[st], act * (2 * B5_TILE + 2 * B5_ROWB));
+          int mq[2], mh[2];
           for (int t = 0; t < 2; ++t) {
             if (j >= w.n[t]) continue;
             int qblk, slot, h;
@@ -209,6 +204,20 @@ __global__ void __launch_bounds__(320, 1)
               h = 0;
               w.b[t] = 0;
             }
+            mq[t] = qblk;
+            mh[t] = h;
+            s_meta[st][t][0] = qblk;
+            s_meta[st][t][1] = slot;
+            s_meta[st][t][2] = h;
+            s_g2[st][t] = p.gate ? __ldg(p.gate + w.b[t] * p.gate_sb + w.hk[t] * p.gate_sh +
+                                         (long long)qblk * p.gate_sn + slot) * kLog2e
+                                 : 0.f;
+          }
+          // the arrive below releases the metadata stores to the r_full waiters
+          mbar_expect_tx(&r_full[st], act * (2 * B5_TILE + 2 * B5_ROWB));
+          for (int t = 0; t < 2; ++t) {
+            if (j >= w.n[t]) continue;
+            const int qblk = mq[t], h = mh[t];
             const int row = qblk * p.bs;
             uint8_t *dst = sR + (st * 2 + t) * 2 * B5_TILE;
             tma_load_rhb(dst, &tq, &r_full[st], perm_q, 0, row, h, w.b[t]);
@@ -336,11 +345,12 @@ __global__ void __launch_bounds__(320, 1)
       b5_unit(pl, p, total, u, w);
       const int ns = max(w.n[0], w.n[1]);
       const int nmine = w.n[t], kb = w.kb[t], b = w.b[t], hk = w.hk[t];
-      const float *gbase = p.gate ? p.gate + b * p.gate_sb + hk * p.gate_sh : nullptr;
       const bool key_ok = (long long)kb * p.bs + kr < p.L;
       for (int j = 0; j < ns; ++j, ++gs) {
         const int bb = gs & 1, st = gs % B5_NST;
         if (!mbar_wait(&s_full[bb], (gs >> 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
+        // acquire the stage's TMA / bulk data and the producer's metadata
+        if (!mbar_wait(&r_full[st], (gs / B5_NST) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
         if (tid == 0) B5_TRACE(3, gs);
         tc05::fence_after();
         float sv[32], dp[32];
@@ -352,11 +362,10 @@ __global__ void __launch_bounds__(320, 1)
         uint32_t wp[16], wd[16];
         const bool active = j < nmine;
         if (active) {
-          int qblk, slot, h;
-          item(w, t, j, qblk, slot, h);
+          const int qblk = s_meta[st][t][0], slot = s_meta[st][t][1];
           // qblk is the local query block; kb is global
           const bool triu = p.causal && ((p.mask_mode == BSA_MASK_SLOT) ? slot == 0 : kb == p.q0 + qblk);
-          const float g2 = gbase ? __ldg(gbase + (long long)qblk * p.gate_sn + slot) * kLog2e : 0.f;
+          const float g2 = s_g2[st][t];
           const float *lsep = sRow + (st * 2 + t) * 2 * B5_BS + 32 * hf;
           const long long q0 = (long long)qblk * p.bs + 32 * hf;
           if (triu || !key_ok || q0 + 32 > p.Lq) {  // diagonal / padded steps: explicit masks
