@@ -82,6 +82,15 @@ class LshArgs(ctypes.Structure):
         ("gate_out", ctypes.c_void_p), ("status", ctypes.c_void_p)]
 
 
+class DecodeArgs(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in
+                ("dtype", "B", "Hq", "Hkv", "L", "D", "bs", "T", "kk", "mask_mode")] + [
+        ("scale", ctypes.c_float)] + [(n, View) for n in ("q", "k", "v", "o")] + [
+        ("sel", ctypes.c_void_p), ("sel_sb", ctypes.c_int64), ("sel_sh", ctypes.c_int64),
+        ("gate", ctypes.c_void_p), ("gate_sb", ctypes.c_int64), ("gate_sh", ctypes.c_int64),
+        ("status", ctypes.c_void_p)]
+
+
 class CsrArgs(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int32) for n in
                 ("B", "Hs", "nblk", "kk", "bs", "L", "mask_mode", "causal")] + [
@@ -114,6 +123,9 @@ SYMBOLS = {
                                    ctypes.c_void_p]),
     "bsa_sel_csr_noalloc": (ctypes.c_int, [ctypes.POINTER(CsrArgs), ctypes.c_void_p]),
     "bsa_rope": (ctypes.c_int, [ctypes.POINTER(RopeArgs), ctypes.c_void_p]),
+    "bsa_decode_workspace": (ctypes.c_size_t, [ctypes.POINTER(DecodeArgs)]),
+    "bsa_decode": (ctypes.c_int, [ctypes.POINTER(DecodeArgs), ctypes.c_void_p, ctypes.c_size_t,
+                                  ctypes.c_void_p]),
     "bsa_status_decode": (ctypes.c_int, [ctypes.c_int32]),
     "bsa_last_error": (ctypes.c_char_p, []),
     "bsa_version": (ctypes.c_int32, []),
@@ -418,6 +430,52 @@ def select_lsh(a_sum, b_sum, planes, *, hash_kind=HASH_SIGN, cap=16, causal=True
     s.status = status_tensor(a_sum.device).data_ptr()
     _check(L.bsa_select_lsh(ctypes.byref(s), ctypes.c_void_p(ws.data_ptr()), nws, _stream()))
     return sel, score, gate
+
+
+def decode(q, k, v, sel, gate=None, *, bs, L=None, mask_mode=MASK_TOKEN, scale=None, out=None):
+    """Decode step (bsa_decode): q (B, Hq, T, D) are the tokens at positions L-T .. L-1
+    (all in the last block); k, v (B, Hkv, >= L, D) the cache; sel int32 (B, Hkv, kk) or
+    (B, kk) block ids of this step; gate optional fp32 like sel.  Returns o (B, Hq, T, D)."""
+    _need_cuda(q, k, v, sel, gate)
+    B, Hq, T, D = q.shape
+    Hkv = k.shape[1]
+    L = k.shape[2] if L is None else int(L)
+    if sel.dtype != torch.int32 or sel.stride(-1) != 1:
+        sel = sel.to(torch.int32).contiguous()
+    a = DecodeArgs()
+    a.dtype = _dtype(q)
+    a.B, a.Hq, a.Hkv, a.L, a.D, a.bs, a.T, a.kk = B, Hq, Hkv, L, D, bs, T, sel.shape[-1]
+    a.mask_mode = mask_mode
+    a.scale = float(D ** -0.5 if scale is None else scale)
+    if k.stride(-1) != 1:
+        k = k.contiguous()
+    if v.stride(-1) != 1:
+        v = v.contiguous()
+    if q.stride(-1) != 1:
+        q = q.contiguous()
+    o = torch.empty_like(q, memory_format=torch.contiguous_format) if out is None else out
+    a.q, a.k, a.v, a.o = _view4(q), _view4(k), _view4(v), _view4(o)
+    if sel.dim() == 2:
+        a.sel, a.sel_sb, a.sel_sh = sel.data_ptr(), sel.stride(0), 0
+    elif sel.dim() == 3 and sel.shape[1] in (1, Hkv):
+        a.sel, a.sel_sb = sel.data_ptr(), sel.stride(0)
+        a.sel_sh = sel.stride(1) if sel.shape[1] > 1 else 0
+    else:
+        raise BsaShapeError(ERR_SHAPE, "decode: sel must be (B, kk) or (B, Hkv, kk)")
+    if gate is not None:
+        gate = gate.to(torch.float32).contiguous()
+        if gate.shape != sel.shape:
+            raise BsaShapeError(ERR_SHAPE, "decode: gate must have the shape of sel")
+        a.gate, a.gate_sb = gate.data_ptr(), gate.stride(0)
+        a.gate_sh = gate.stride(1) if gate.dim() == 3 and gate.shape[1] > 1 else 0
+    a.status = status_tensor(q.device).data_ptr()
+    L_ = lib()
+    nbytes = L_.bsa_decode_workspace(ctypes.byref(a))
+    if nbytes == 0:
+        _check(L_.bsa_decode(ctypes.byref(a), None, 0, _stream()))
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
+    _check(L_.bsa_decode(ctypes.byref(a), ctypes.c_void_p(ws.data_ptr()), nbytes, _stream()))
+    return o
 
 
 def sel_csr(sel, *, bs, L, causal, mask_mode=MASK_SLOT):

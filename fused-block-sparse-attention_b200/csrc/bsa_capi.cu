@@ -19,6 +19,8 @@ int32_t lsh_width(const bsa_lsh_args *a);
 size_t lsh_workspace(const bsa_lsh_args *a);
 bsa_status run_lsh(const bsa_lsh_args *a, void *ws, size_t ws_bytes, cudaStream_t st);
 bsa_status run_rope(const bsa_rope_args *a, cudaStream_t st);
+size_t decode_workspace(const bsa_decode_args *a);
+bsa_status run_decode(const bsa_decode_args *a, void *ws, size_t ws_bytes, cudaStream_t st);
 
 static bsa_status check_view(const bsa_view &v, int dtype, const char *name, bool vec16) {
   if (!v.ptr) return fail(BSA_ERR_ARG, std::string(name) + " is NULL");
@@ -210,6 +212,14 @@ bsa_status bsa_sel_csr(const bsa_csr_args *a, void *workspace, size_t workspace_
   if (bsa_status s = check_csr(a)) return s;
   if (!a->row_ptr || !a->col) return fail(BSA_ERR_ARG, "sel_csr: NULL output");
   return run_sel_csr(a, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+size_t bsa_decode_workspace(const bsa_decode_args *a) { return a ? decode_workspace(a) : 0; }
+
+bsa_status bsa_decode(const bsa_decode_args *a, void *workspace, size_t workspace_bytes,
+                      bsa_stream_t stream) {
+  if (!a) return fail(BSA_ERR_ARG, "decode: args is NULL");
+  return run_decode(a, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
 }
 
 bsa_status bsa_rope(const bsa_rope_args *a, bsa_stream_t stream) {

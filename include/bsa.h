@@ -209,6 +209,30 @@ size_t bsa_select_lsh_workspace(const bsa_lsh_args *a);
 bsa_status bsa_select_lsh(const bsa_lsh_args *a, void *workspace, size_t workspace_bytes,
                           bsa_stream_t stream);
 
+/* Decode: the T newest tokens (positions L-T .. L-1, all in the last block
+ * (L-1)/bs) attend to the selected blocks of a K/V cache.  No reference
+ * counterpart (the reference has no decode path); the arithmetic is
+ * bsa_attn_fwd's restricted to those rows: logit = scale * q.k + gate[slot],
+ * causal by position, SLOT or TOKEN masks as in bsa_attn_args (slot 0 = the own
+ * block in SLOT mode).  q, o: (B, Hq, T, D); k, v: (B, Hkv, >= L, D) with rows
+ * [0, L) valid; sel: int32 (B, Hs, kk) block ids for this step (sel_sh = 0 shares
+ * one row over the KV heads), gate: optional fp32 addressed like sel.  Split-K
+ * over the selected blocks with a fp32 workspace of bsa_decode_workspace bytes.
+ * Limits: (Hq/Hkv)*T <= 32, D and bs divide 256, bs <= 128. */
+typedef struct {
+  int32_t dtype, B, Hq, Hkv, L, D, bs, T, kk, mask_mode;
+  float scale;
+  bsa_view q, k, v, o;
+  const int32_t *sel;
+  int64_t sel_sb, sel_sh;
+  const float *gate;
+  int64_t gate_sb, gate_sh;
+  int32_t *status;
+} bsa_decode_args;
+size_t bsa_decode_workspace(const bsa_decode_args *a);
+bsa_status bsa_decode(const bsa_decode_args *a, void *workspace, size_t workspace_bytes,
+                      bsa_stream_t stream);
+
 /* CSR transpose of a selection: for every (b, sel head, key block) the list of
  * entries e = qblk*kk + slot whose slot is active under the mask rules of
  * bsa_attn_args, in ascending e.  row_ptr: int32 (B*Hs*nblk + 1);
