@@ -19,7 +19,7 @@ DEVERR_INDEX, DEVERR_TIMEOUT = 1, 2
 BF16, F16, F32 = 0, 1, 2
 MASK_SLOT, MASK_TOKEN = 0, 1
 SCORE_DOT, SCORE_MAXDOT2, SCORE_QUEST = 0, 1, 2
-SEL_SSA, SEL_FINISH = 0, 1
+SEL_SSA, SEL_FINISH, SEL_RAW = 0, 1, 2
 HASH_ARGMAX, HASH_SIGN = 0, 1
 
 _STATUS_NAMES = {ERR_SHAPE: "shape", ERR_DTYPE: "dtype", ERR_STRIDE: "stride",
@@ -91,6 +91,18 @@ class DecodeArgs(ctypes.Structure):
         ("status", ctypes.c_void_p)]
 
 
+class ScoresArgs(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in ("G", "nblk", "topk", "sink")] + [
+        ("score", ctypes.c_void_p), ("score_sg", ctypes.c_int64), ("score_si", ctypes.c_int64),
+        ("sel", ctypes.c_void_p), ("status", ctypes.c_void_p)]
+
+
+class QmaxArgs(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in ("G", "nblk", "bs", "dim", "topk", "sink", "M")] + [
+        ("qtok", ctypes.c_void_p), ("kmax", ctypes.c_void_p), ("kmin", ctypes.c_void_p),
+        ("cand", ctypes.c_void_p), ("sel", ctypes.c_void_p), ("status", ctypes.c_void_p)]
+
+
 class CsrArgs(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int32) for n in
                 ("B", "Hs", "nblk", "kk", "bs", "L", "mask_mode", "causal")] + [
@@ -118,6 +130,9 @@ SYMBOLS = {
     "bsa_select_lsh_workspace": (ctypes.c_size_t, [ctypes.POINTER(LshArgs)]),
     "bsa_select_lsh": (ctypes.c_int, [ctypes.POINTER(LshArgs), ctypes.c_void_p, ctypes.c_size_t,
                                       ctypes.c_void_p]),
+    "bsa_select_scores_width": (ctypes.c_int32, [ctypes.POINTER(ScoresArgs)]),
+    "bsa_select_scores": (ctypes.c_int, [ctypes.POINTER(ScoresArgs), ctypes.c_void_p]),
+    "bsa_select_qmax": (ctypes.c_int, [ctypes.POINTER(QmaxArgs), ctypes.c_void_p]),
     "bsa_csr_workspace": (ctypes.c_size_t, [ctypes.POINTER(CsrArgs)]),
     "bsa_sel_csr": (ctypes.c_int, [ctypes.POINTER(CsrArgs), ctypes.c_void_p, ctypes.c_size_t,
                                    ctypes.c_void_p]),
@@ -476,6 +491,53 @@ def decode(q, k, v, sel, gate=None, *, bs, L=None, mask_mode=MASK_TOKEN, scale=N
     ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
     _check(L_.bsa_decode(ctypes.byref(a), ctypes.c_void_p(ws.data_ptr()), nbytes, _stream()))
     return o
+
+
+def select_scores(score, *, topk, sink=True):
+    """_finish top-k of a score matrix (bsa_select_scores).  score: (..., nblk, nblk) ->
+    int32 (..., nblk, min(topk, nblk) + 1 + sink), ascending."""
+    _need_cuda(score)
+    lead = score.shape[:-2]
+    nblk = score.shape[-1]
+    S = score.reshape(-1, nblk, nblk).float()
+    if S.stride(-1) != 1:
+        S = S.contiguous()
+    a = ScoresArgs()
+    a.G, a.nblk, a.topk, a.sink = S.shape[0], nblk, topk, 1 if sink else 0
+    a.score, a.score_sg, a.score_si = S.data_ptr(), S.stride(0), S.stride(1)
+    W = lib().bsa_select_scores_width(ctypes.byref(a))
+    sel = torch.empty(*lead, nblk, W, dtype=torch.int32, device=score.device)
+    a.sel = sel.data_ptr()
+    a.status = status_tensor(score.device).data_ptr()
+    _check(lib().bsa_select_scores(ctypes.byref(a), _stream()))
+    return sel
+
+
+def select_qmax(qtok, kmax, kmin, *, topk, sink=True, cand=None):
+    """Max-over-tokens Quest selection (bsa_select_qmax).  qtok: (..., nblk, bs, dim)
+    fp32; kmax/kmin: (..., nblk, dim); cand: optional int32 (..., nblk, M).
+    Returns int32 (..., nblk, min(topk, nblk) + 1 + sink), ascending."""
+    _need_cuda(qtok, kmax, kmin, cand)
+    lead = qtok.shape[:-3]
+    nblk, bs, dim = qtok.shape[-3:]
+    Q = qtok.reshape(-1, nblk, bs, dim).float().contiguous()
+    KX = kmax.reshape(-1, nblk, dim).float().contiguous()
+    KN = kmin.reshape(-1, nblk, dim).float().contiguous()
+    a = QmaxArgs()
+    a.G, a.nblk, a.bs, a.dim, a.topk, a.sink = Q.shape[0], nblk, bs, dim, topk, 1 if sink else 0
+    a.qtok, a.kmax, a.kmin = Q.data_ptr(), KX.data_ptr(), KN.data_ptr()
+    C = None
+    if cand is not None:
+        C = cand.reshape(-1, nblk, cand.shape[-1]).to(torch.int32).contiguous()
+        a.cand, a.M = C.data_ptr(), C.shape[-1]
+    s = ScoresArgs()
+    s.nblk, s.topk, s.sink = nblk, topk, a.sink
+    W = lib().bsa_select_scores_width(ctypes.byref(s))
+    sel = torch.empty(*lead, nblk, W, dtype=torch.int32, device=qtok.device)
+    a.sel = sel.data_ptr()
+    a.status = status_tensor(qtok.device).data_ptr()
+    _check(lib().bsa_select_qmax(ctypes.byref(a), _stream()))
+    return sel
 
 
 def sel_csr(sel, *, bs, L, causal, mask_mode=MASK_SLOT):

@@ -19,6 +19,9 @@ int32_t lsh_width(const bsa_lsh_args *a);
 size_t lsh_workspace(const bsa_lsh_args *a);
 bsa_status run_lsh(const bsa_lsh_args *a, void *ws, size_t ws_bytes, cudaStream_t st);
 bsa_status run_rope(const bsa_rope_args *a, cudaStream_t st);
+int32_t scores_width(int nblk, int topk, int sink);
+bsa_status run_scores_topk(const bsa_scores_args *a, cudaStream_t st);
+bsa_status run_qmax(const bsa_qmax_args *a, cudaStream_t st);
 size_t decode_workspace(const bsa_decode_args *a);
 bsa_status run_decode(const bsa_decode_args *a, void *ws, size_t ws_bytes, cudaStream_t st);
 
@@ -220,6 +223,20 @@ bsa_status bsa_decode(const bsa_decode_args *a, void *workspace, size_t workspac
                       bsa_stream_t stream) {
   if (!a) return fail(BSA_ERR_ARG, "decode: args is NULL");
   return run_decode(a, workspace, workspace_bytes, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int32_t bsa_select_scores_width(const bsa_scores_args *a) {
+  return a ? scores_width(a->nblk, a->topk, a->sink) : 0;
+}
+
+bsa_status bsa_select_scores(const bsa_scores_args *a, bsa_stream_t stream) {
+  if (!a) return fail(BSA_ERR_ARG, "select_scores: args is NULL");
+  return run_scores_topk(a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+bsa_status bsa_select_qmax(const bsa_qmax_args *a, bsa_stream_t stream) {
+  if (!a) return fail(BSA_ERR_ARG, "select_qmax: args is NULL");
+  return run_qmax(a, reinterpret_cast<cudaStream_t>(stream));
 }
 
 bsa_status bsa_rope(const bsa_rope_args *a, bsa_stream_t stream) {

@@ -308,6 +308,9 @@ __global__ void __launch_bounds__(256) select_kernel(const bsa_select_args a, in
         if (a.score_out) a.score_out[ob + 1 + lane] = sc;
         if (a.gate_out) a.gate_out[ob + 1 + lane] = logsigmoid(sc);
       }
+    } else if (a.layout == BSA_SEL_RAW) {
+      // RAW: the picks in rank order, -1 where fewer than T candidates exist
+      if (lane < T) a.sel[ob + lane] = valid ? ei[r] : -1;
     } else {
       // FINISH: picks (invalid -> own), own, optional sink; ascending sort
       if (lane < T) scratch[lane] = valid ? ei[r] : row;
@@ -332,6 +335,7 @@ __global__ void __launch_bounds__(256) select_kernel(const bsa_select_args a, in
 
 int32_t select_width(const bsa_select_args *a) {
   if (a->layout == BSA_SEL_SSA) return 1 + std::max(0, std::min(a->topk, a->nblk - 1));
+  if (a->layout == BSA_SEL_RAW) return std::max(0, std::min(a->topk, a->nblk));
   return std::max(0, std::min(a->topk, a->nblk)) + 1 + (a->sink ? 1 : 0);
 }
 
@@ -342,13 +346,14 @@ bsa_status run_select(const bsa_select_args *a, cudaStream_t st) {
   if (a->topk < 0 || a->topk > 32) return fail(BSA_ERR_UNSUPPORTED, "select: topk must be in [0, 32]");
   if (a->score_kind != BSA_SCORE_DOT && !a->b2)
     return fail(BSA_ERR_ARG, "select: MAXDOT2/QUEST need b2");
-  if (a->layout != BSA_SEL_SSA && a->layout != BSA_SEL_FINISH)
+  if (a->layout != BSA_SEL_SSA && a->layout != BSA_SEL_FINISH && a->layout != BSA_SEL_RAW)
     return fail(BSA_ERR_ARG, "select: bad layout");
-  if (a->layout == BSA_SEL_FINISH && (a->score_out || a->gate_out))
+  if (a->layout != BSA_SEL_SSA && (a->score_out || a->gate_out))
     return fail(BSA_ERR_ARG, "select: score/gate outputs are SSA-layout only");
   if ((long long)a->G > 65535) return fail(BSA_ERR_SHAPE, "select: G > 65535");
   const int W = select_width(a);
   int T = a->layout == BSA_SEL_SSA ? W - 1 : std::min(a->topk, a->nblk);
+  if (a->layout == BSA_SEL_RAW && T == 0) return BSA_OK;
   const int nq = a->nq > 0 ? a->nq : a->nblk;
   if (a->q_blk0 < 0 || a->nq < 0 || (long long)a->q_blk0 + nq > a->nblk)
     return fail(BSA_ERR_SHAPE, "select: query range outside [0, nblk)");

@@ -4,6 +4,12 @@ on sm_100a.
   blocksparse_forward(q, k, v, *, selector, topk, bs, causal=True, scale=None, q_chunk=4)
   SelectMax(topk, bs, sink=True).select(q, k)     Quest min/max bound (:102-121)
   SelectAll(bs).select(q, k)                       all blocks (:155-165)
+  SelectOracle(topk, bs, sink=True, mass=None)     top-k of a given block mass (:124-137)
+  SelectRandom(topk, bs, sink=True, seed=0)        uniform random scores (:140-152)
+  SelectLastTok(topk, bs, sink=True)               Quest bound of each block's last token (:250-267)
+  SelectMaxQMax(topk, bs, sink=True)               Quest bound maxed over the block's tokens (:221-247)
+  SelectTwoStage(topk, bs, sink=True, over=4)      block-mean Quest candidates, max-over-token
+                                                   re-score (:270-299)
   qwen_attention(...)                              the Qwen-style variant: partial RoPE,
                                                    selection, GQA attention and the sigmoid
                                                    output gate in one call (src/patch_qwen.py:41-55)
@@ -19,7 +25,8 @@ import torch
 import _bsa
 from selection import select_quest
 
-__all__ = ["blocksparse_forward", "SelectMax", "SelectAll", "qwen_attention", "rope_cos_sin"]
+__all__ = ["blocksparse_forward", "SelectMax", "SelectAll", "SelectOracle", "SelectRandom",
+           "SelectLastTok", "SelectMaxQMax", "SelectTwoStage", "qwen_attention", "rope_cos_sin"]
 
 
 class SelectMax:
@@ -45,6 +52,99 @@ class SelectAll:
         nblk = (L + self.bs - 1) // self.bs
         return torch.arange(nblk, device=q.device).view(1, 1, 1, nblk).expand(
             B, k.shape[1], nblk, nblk).contiguous()
+
+
+class SelectOracle:
+    """Top-k key blocks by a supplied per-block attention mass (B, Hkv, nblk, nblk)."""
+
+    def __init__(self, topk, bs, sink=True, mass=None):
+        self.topk, self.bs, self.sink, self.mass = topk, bs, sink, mass
+
+    @torch.no_grad()
+    def select_from_mass(self, mass):
+        return _bsa.select_scores(mass, topk=self.topk, sink=self.sink).long()
+
+    @torch.no_grad()
+    def select(self, q, k):
+        if self.mass is None:
+            raise ValueError("SelectOracle needs mass set (per-layer teacher)")
+        return self.select_from_mass(self.mass)
+
+
+class SelectRandom:
+    """Random causal blocks (lower-bound baseline): the same uniform draws as the
+    reference's generator on the same device, then the device top-k."""
+
+    def __init__(self, topk, bs, sink=True, seed=0):
+        self.topk, self.bs, self.sink, self.seed = topk, bs, sink, seed
+
+    @torch.no_grad()
+    def select(self, q, k):
+        B, Hq, L, d = q.shape
+        nblk = (L + self.bs - 1) // self.bs
+        g = torch.Generator(device=q.device).manual_seed(self.seed)
+        score = torch.rand(B, k.shape[1], nblk, nblk, generator=g, device=q.device)
+        return _bsa.select_scores(score, topk=self.topk, sink=self.sink).long()
+
+
+def _token_summaries(q, k, bs):
+    """Group-mean query tokens (B, Hkv, nblk, bs, d) with zero padding rows, and the
+    key blocks' min / max (B, Hkv, nblk, d), all fp32."""
+    B, Hq, L, d = q.shape
+    Hkv = k.shape[1]
+    nblk = (L + bs - 1) // bs
+    (qt,) = _bsa.pool(q, 1, grp=Hq // Hkv)                       # (B, Hkv, L, d)
+    if nblk * bs != L:
+        qt = torch.nn.functional.pad(qt, (0, 0, 0, nblk * bs - L))
+    kmin, kmax = _bsa.pool(k, bs, mean=False, vmin=True, vmax=True)
+    return qt.view(B, Hkv, nblk, bs, d), kmin, kmax
+
+
+class SelectLastTok:
+    """SelectMax scored by each query block's last token (group mean) instead of the
+    block mean; a padded last block scores with its (zero) padding row, as the
+    reference does."""
+
+    def __init__(self, topk, bs, sink=True):
+        self.topk, self.bs, self.sink = topk, bs, sink
+
+    @torch.no_grad()
+    def select(self, q, k):
+        qt, kmin, kmax = _token_summaries(q, k, self.bs)
+        qlast = qt[:, :, :, -1, :].contiguous()
+        sel, _, _ = _bsa.select(qlast, kmax, kmin, kind=_bsa.SCORE_QUEST, layout=_bsa.SEL_FINISH,
+                                topk=self.topk, sink=self.sink)
+        return sel.long()
+
+
+class SelectMaxQMax:
+    """Quest bound maxed over the query block's tokens (group-mean per token)."""
+
+    def __init__(self, topk, bs, sink=True):
+        self.topk, self.bs, self.sink = topk, bs, sink
+
+    @torch.no_grad()
+    def select(self, q, k):
+        qt, kmin, kmax = _token_summaries(q, k, self.bs)
+        return _bsa.select_qmax(qt, kmax, kmin, topk=self.topk, sink=self.sink).long()
+
+
+class SelectTwoStage:
+    """Stage 1: block-mean Quest picks over*topk candidates (causal); stage 2: the
+    max-over-token Quest bound re-scores them and keeps top-k."""
+
+    def __init__(self, topk, bs, sink=True, over=4):
+        self.topk, self.bs, self.sink, self.over = topk, bs, sink, over
+
+    @torch.no_grad()
+    def select(self, q, k):
+        B, Hq, L, d = q.shape
+        nblk = (L + self.bs - 1) // self.bs
+        qt, kmin, kmax = _token_summaries(q, k, self.bs)
+        (qp,) = _bsa.pool(q, self.bs, grp=Hq // k.shape[1])
+        M = min(self.over * self.topk, nblk)
+        cand, _, _ = _bsa.select(qp, kmax, kmin, kind=_bsa.SCORE_QUEST, layout=_bsa.SEL_RAW, topk=M)
+        return _bsa.select_qmax(qt, kmax, kmin, topk=self.topk, sink=self.sink, cand=cand).long()
 
 
 def _attend(q, k, v, sel, bs, causal, scale):

@@ -156,10 +156,13 @@ bsa_status bsa_pool(const bsa_pool_args *a, bsa_stream_t stream);
  *  layout FINISH: top-T over j <= i with T = min(topk, nblk), missing picks -> i,
  *                 then append i (and block 0 when sink), sorted ascending
  *                 (src/qwen_blocksparse.py:87-99).
+ *  layout RAW:    the top-T over j <= i, T = min(topk, nblk), in rank order,
+ *                 -1 where fewer exist (stage 1 of SelectTwoStage,
+ *                 src/qwen_blocksparse.py:285-286).
  *  score_out / gate_out (optional, SSA only): the score of each selected block
  *  and logsigmoid(score) (src/ssa_model.py:189-191).  topk <= 32. */
 typedef enum { BSA_SCORE_DOT = 0, BSA_SCORE_MAXDOT2 = 1, BSA_SCORE_QUEST = 2 } bsa_score_kind;
-typedef enum { BSA_SEL_SSA = 0, BSA_SEL_FINISH = 1 } bsa_sel_layout;
+typedef enum { BSA_SEL_SSA = 0, BSA_SEL_FINISH = 1, BSA_SEL_RAW = 2 } bsa_sel_layout;
 typedef struct {
   int32_t G, nblk, dim;
   int32_t score_kind, layout, causal, topk, sink;
@@ -232,6 +235,39 @@ typedef struct {
 size_t bsa_decode_workspace(const bsa_decode_args *a);
 bsa_status bsa_decode(const bsa_decode_args *a, void *workspace, size_t workspace_bytes,
                       bsa_stream_t stream);
+
+/* Top-k of a caller-supplied score matrix with _finish semantics (reference
+ * src/qwen_blocksparse.py:87-99): per row i of score (G, nblk, nblk) (element
+ * strides score_sg, score_si, unit column stride) the top min(topk, nblk) over
+ * j <= i by (score desc, block asc), non-finite or missing picks -> i, then i
+ * and (sink) block 0 appended, ascending.  Backs SelectOracle (a per-block
+ * attention mass, :124-137) and SelectRandom (uniform draws, :140-152). */
+typedef struct {
+  int32_t G, nblk, topk, sink;
+  const float *score;
+  int64_t score_sg, score_si;
+  int32_t *sel; /* (G, nblk, bsa_select_scores_width) */
+  int32_t *status;
+} bsa_scores_args;
+int32_t bsa_select_scores_width(const bsa_scores_args *a);
+bsa_status bsa_select_scores(const bsa_scores_args *a, bsa_stream_t stream);
+
+/* Per-token Quest bound, max over the query block's tokens, with _finish
+ * semantics: score(i, j) = max_t sum_d q[i,t,d] * (q >= 0 ? kmax[j,d] : kmin[j,d])
+ * over the bs token rows of query block i (padding rows included as zeros, as
+ * the reference pads), candidates j <= i — all of them (SelectMaxQMax,
+ * src/qwen_blocksparse.py:221-247) or the M per-row candidates in cand, -1 or
+ * j > i ignored (SelectTwoStage's re-score, :270-299).  qtok: fp32
+ * (G, nblk, bs, dim) group-mean query tokens; kmax/kmin: fp32 (G, nblk, dim).
+ * Each token score is one fp32 fma chain over d from 0. */
+typedef struct {
+  int32_t G, nblk, bs, dim, topk, sink, M;
+  const float *qtok, *kmax, *kmin;
+  const int32_t *cand; /* optional (G, nblk, M) */
+  int32_t *sel;        /* (G, nblk, bsa_select_scores_width) */
+  int32_t *status;
+} bsa_qmax_args;
+bsa_status bsa_select_qmax(const bsa_qmax_args *a, bsa_stream_t stream);
 
 /* CSR transpose of a selection: for every (b, sel head, key block) the list of
  * entries e = qblk*kk + slot whose slot is active under the mask rules of

@@ -16,6 +16,8 @@
  *                                  top-k content blocks, own excluded, future masked)
  *                    layout FINISH src/qwen_blocksparse.py:87-99 (_finish: causal mask,
  *                                  topk, non-finite -> own, + own + sink, sorted)
+ *                    layout RAW    the causal top-k picks in rank order, -1 when fewer
+ *                                  (stage 1 of SelectTwoStage, :285-286)
  *                    scores        DOT   q.k of mean-pooled blocks
  *                                  MAXDOT2 src/ssa_model.py:118-119
  *                                  QUEST src/qwen_blocksparse.py:117-120
@@ -28,6 +30,11 @@
  *                    dropped after an empty slot of an earlier round, because the
  *                    reference dedups ids clamped at 0, :452-457), re-scored by
  *                    scale * cosine, top-k, own block first (:470-476).
+ *   oracle_select_scores — _finish top-k of a given score matrix (SelectOracle /
+ *                    SelectRandom, src/qwen_blocksparse.py:124-152, :87-99)
+ *   oracle_select_qmax — per-token Quest bound maxed over the query block's tokens,
+ *                    over all causal blocks (SelectMaxQMax :221-247) or a per-row
+ *                    candidate list (SelectTwoStage :270-299)
  *   oracle_csr     — key-block transpose of the active (qblk, slot) entries under the
  *                    masks of src/triton_kernel.py:57-61 (SLOT) or
  *                    src/qwen_blocksparse.py:67-72 (TOKEN).
@@ -94,6 +101,7 @@ int oracle_select_width(int layout, int nblk, int topk, int sink) {
     return 1 + (t > 0 ? t : 0);
   }
   t = topk < nblk ? topk : nblk;
+  if (layout == 2) return t > 0 ? t : 0; /* RAW: the picks only */
   return (t > 0 ? t : 0) + 1 + (sink ? 1 : 0);
 }
 
@@ -109,7 +117,7 @@ void oracle_select(const float *a, const float *b1, const float *b2, int G, int 
                    int kind, int layout, int causal, int topk, int sink, int32_t *sel,
                    float *score_out, float *gate_out) {
   const int W = oracle_select_width(layout, nblk, topk, sink);
-  const int T = layout == 0 ? W - 1 : W - 1 - (sink ? 1 : 0);
+  const int T = layout == 0 ? W - 1 : (layout == 2 ? W : W - 1 - (sink ? 1 : 0));
   float *ls = (float *)malloc(sizeof(float) * (T > 0 ? T : 1));
   int *li = (int *)malloc(sizeof(int) * (T > 0 ? T : 1));
   int *tmp = (int *)malloc(sizeof(int) * (W + 1));
@@ -155,6 +163,8 @@ void oracle_select(const float *a, const float *b1, const float *b2, int G, int 
           if (score_out) score_out[ob + 1 + l] = sc;
           if (gate_out) gate_out[ob + 1 + l] = logsigmoidf_(sc);
         }
+      } else if (layout == 2) {
+        for (int l = 0; l < T; ++l) out[l] = l < n ? li[l] : -1;
       } else {
         for (int l = 0; l < T; ++l) tmp[l] = l < n ? li[l] : i;
         tmp[T] = i;
@@ -317,4 +327,82 @@ void oracle_select_lsh(const float *a, const float *b, const float *planes, int 
     }
   }
   free(yq); free(yk); free(qc); free(kc); free(list); free(cnt); free(cid); free(csc);
+}
+
+/* _finish over per-row candidate scores: top T=min(topk,nblk) of (sc[m], id[m])
+ * for m < n with finite scores and id <= i, missing -> i, + i (+ sink 0), ascending. */
+static void finish_from(const float *sc, const int *id, int n, int i, int nblk, int topk, int sink,
+                        int32_t *dst) {
+  int T = topk < nblk ? topk : nblk, W = T + 1 + (sink ? 1 : 0);
+  int *out = malloc(sizeof(int) * (W > 1 ? W : 1));
+  char *used = calloc(n > 0 ? n : 1, 1);
+  for (int t = 0; t < T; ++t) {
+    int b = -1;
+    for (int m = 0; m < n; ++m) {
+      if (used[m] || id[m] < 0 || id[m] > i || !(sc[m] > -INFINITY)) continue;
+      if (b < 0 || better(sc[m], id[m], sc[b], id[b])) b = m;
+    }
+    if (b >= 0) used[b] = 1;
+    out[t] = b >= 0 ? id[b] : i;
+  }
+  out[T] = i;
+  if (sink) out[T + 1] = 0;
+  qsort(out, W, sizeof(int), cmp_int);
+  for (int w = 0; w < W; ++w) dst[w] = out[w];
+  free(out);
+  free(used);
+}
+
+int oracle_scores_width(int nblk, int topk, int sink) {
+  return (topk < nblk ? topk : nblk) + 1 + (sink ? 1 : 0);
+}
+
+/* score: (G, nblk, nblk) contiguous; sel: (G, nblk, W) */
+void oracle_select_scores(const float *score, int G, int nblk, int topk, int sink, int32_t *sel) {
+  const int W = oracle_scores_width(nblk, topk, sink);
+  int *id = malloc(sizeof(int) * nblk);
+  float *sc = malloc(sizeof(float) * nblk);
+  for (int g = 0; g < G; ++g)
+    for (int i = 0; i < nblk; ++i) {
+      const float *row = score + ((int64_t)g * nblk + i) * nblk;
+      for (int j = 0; j < nblk; ++j) {
+        id[j] = j;
+        sc[j] = row[j] != row[j] ? -INFINITY : row[j];
+      }
+      finish_from(sc, id, nblk, i, nblk, topk, sink, sel + ((int64_t)g * nblk + i) * W);
+    }
+  free(id);
+  free(sc);
+}
+
+/* qtok: (G, nblk, bs, dim); kmax/kmin: (G, nblk, dim); cand: NULL or (G, nblk, M). */
+void oracle_select_qmax(const float *qtok, const float *kmax, const float *kmin, const int32_t *cand,
+                        int G, int nblk, int bs, int dim, int M, int topk, int sink, int32_t *sel) {
+  const int W = oracle_scores_width(nblk, topk, sink);
+  const int NC = cand ? M : nblk;
+  int *id = malloc(sizeof(int) * NC);
+  float *sc = malloc(sizeof(float) * NC);
+  for (int g = 0; g < G; ++g)
+    for (int i = 0; i < nblk; ++i) {
+      const float *qb = qtok + ((int64_t)g * nblk + i) * bs * dim;
+      for (int m = 0; m < NC; ++m) {
+        int j = cand ? cand[((int64_t)g * nblk + i) * M + m] : m;
+        if (j > i || j >= nblk) j = -1;
+        id[m] = j;
+        sc[m] = -INFINITY;
+        if (j < 0) continue;
+        const float *kx = kmax + ((int64_t)g * nblk + j) * dim, *kn = kmin + ((int64_t)g * nblk + j) * dim;
+        for (int t = 0; t < bs; ++t) {
+          float s = 0.f;
+          for (int d = 0; d < dim; ++d) {
+            const float q = qb[(int64_t)t * dim + d];
+            s = fmaf(q, q >= 0.f ? kx[d] : kn[d], s);
+          }
+          if (s > sc[m]) sc[m] = s;
+        }
+      }
+      finish_from(sc, id, NC, i, nblk, topk, sink, sel + ((int64_t)g * nblk + i) * W);
+    }
+  free(id);
+  free(sc);
 }

@@ -20,6 +20,9 @@ Fixtures (npz, fp32 / int32):
                       its planes R, and the selection it attends with, decoded from the
                       gathered keys (key rows carry their block id) and the -inf mask it
                       hands to _sdpa (invalid picks).
+  selectors.npz       SelectOracle (random mass), SelectRandom (its CPU draws), SelectLastTok,
+                      SelectMaxQMax and SelectTwoStage (src/qwen_blocksparse.py:124-299) on
+                      one seeded GQA input with a padded last block.
   rope.npz            transformers' apply_rotary_pos_emb (qwen3_5_moe) on bf16 inputs, and
                       the cos/sin of Qwen3_5MoeTextRotaryEmbedding for text positions.
 """
@@ -186,6 +189,24 @@ def lsh_case(name, B, L, d, h, bs, topk, n_rounds, n_buckets, cap, causal, seed)
          causal=torch.tensor(int(causal)))
 
 
+def selectors_case(name, B, Hq, Hkv, L, d, bs, topk, seed):
+    import qwen_blocksparse as qb
+    torch.manual_seed(seed)
+    q = torch.randn(B, Hq, L, d)
+    k = torch.randn(B, Hkv, L, d)
+    nblk = (L + bs - 1) // bs
+    mass = torch.rand(B, Hkv, nblk, nblk)
+    g = torch.Generator().manual_seed(3)
+    rnd = torch.rand(B, Hkv, nblk, nblk, generator=g)
+    out = dict(q=q, k=k, mass=mass, rnd=rnd, bs=torch.tensor(bs), topk=torch.tensor(topk))
+    out["oracle"] = qb.SelectOracle(topk, bs).select_from_mass(mass)
+    out["random"] = qb.SelectRandom(topk, bs, seed=3).select(q, k)
+    out["lasttok"] = qb.SelectLastTok(topk, bs).select(q, k)
+    out["qmax"] = qb.SelectMaxQMax(topk, bs).select(q, k)
+    out["twostage"] = qb.SelectTwoStage(topk, bs, over=2).select(q, k)
+    save(name, **out)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("BSA_REFERENCE", ""))
@@ -207,6 +228,7 @@ def main():
         ("qwen_fastpath.npz", qwen_case, (1, 4, 2, 256, 64, 64, 0, 9, "fast")),
         ("lsh_causal.npz", lsh_case, (2, 2048, 64, 2, 16, 6, 4, 8, 8, True, 10)),
         ("lsh_noncausal.npz", lsh_case, (1, 1024, 64, 2, 16, 4, 3, 6, 5, False, 11)),
+        ("selectors.npz", selectors_case, (1, 4, 2, 600, 16, 32, 3, 12)),
     ]
     for name, fn, args in cases:
         if name.startswith(a.only):

@@ -243,3 +243,55 @@ def test_lsh_module_matches_oracle_attention(cuda, monkeypatch):
                           mask_mode=seen["mode"])
         err = (seen["out"].detach().float().cpu() - ref).abs().max().item()
         assert err < 1e-4, err
+
+
+def test_scores_topk_and_qmax_bit_exact(cuda):
+    """bsa_select_scores, bsa_select_qmax (all causal / candidate lists) and the RAW
+    layout of bsa_select against the oracle on the same inputs."""
+    import _bsa
+    gen = torch.Generator().manual_seed(21)
+    G, nblk, bs, dim, topk = 3, 70, 32, 48, 7
+    score = torch.rand(G, nblk, nblk, generator=gen)
+    score[0, 5, :] = 0.5                                   # a fully tied row
+    score[1, 9, 3] = float("nan")
+    assert np.array_equal(_bsa.select_scores(score.to(cuda), topk=topk).cpu().numpy(),
+                          O.select_scores(score, topk=topk))
+    qt = torch.randn(G, nblk, bs, dim, generator=gen)
+    kmax = torch.randn(G, nblk, dim, generator=gen).abs()
+    kmin = -torch.randn(G, nblk, dim, generator=gen).abs()
+    assert np.array_equal(_bsa.select_qmax(qt.to(cuda), kmax.to(cuda), kmin.to(cuda), topk=topk,
+                                           sink=False).cpu().numpy(),
+                          O.select_qmax(qt, kmax, kmin, topk=topk, sink=False))
+    qp = qt.mean(2)
+    raw, _, _ = _bsa.select(qp.to(cuda), kmax.to(cuda), kmin.to(cuda), kind=_bsa.SCORE_QUEST,
+                            layout=_bsa.SEL_RAW, topk=20)
+    oraw, _, _ = O.select(qp, kmax, kmin, kind=O.SCORE_QUEST, layout=O.SEL_RAW, topk=20)
+    assert np.array_equal(raw.cpu().numpy(), oraw)
+    assert np.array_equal(_bsa.select_qmax(qt.to(cuda), kmax.to(cuda), kmin.to(cuda), topk=topk,
+                                           cand=raw).cpu().numpy(),
+                          O.select_qmax(qt, kmax, kmin, topk=topk, cand=oraw))
+
+
+def test_other_selectors_golden(cuda):
+    """The device SelectOracle / SelectLastTok / SelectMaxQMax / SelectTwoStage on the
+    reference's own inputs give the reference's selections (tie rows aside, see the
+    oracle test); SelectRandom equals the _finish top-k of its own draws."""
+    import qwen_blocksparse as qb
+    g = golden("selectors.npz")
+    bs, topk = int(g["bs"]), int(g["topk"])
+    q, k = torch.from_numpy(g["q"]).to(cuda), torch.from_numpy(g["k"]).to(cuda)
+    sel = qb.SelectOracle(topk, bs).select_from_mass(torch.from_numpy(g["mass"]).to(cuda))
+    assert np.array_equal(sel.cpu().numpy(), g["oracle"])
+    last = g["q"].reshape(1, 2, 2, -1, g["q"].shape[-1]).mean(2)
+    lt = qb.SelectLastTok(topk, bs).select(q, k).cpu().numpy()
+    nblk = lt.shape[2]
+    tied = np.zeros(lt.shape[:3], bool)
+    if g["q"].shape[2] % bs:
+        tied[:, :, nblk - 1] = True
+    assert np.array_equal(lt[~tied], g["lasttok"][~tied])
+    assert np.array_equal(qb.SelectMaxQMax(topk, bs).select(q, k).cpu().numpy(), g["qmax"])
+    assert np.array_equal(qb.SelectTwoStage(topk, bs, over=2).select(q, k).cpu().numpy(), g["twostage"])
+    r = qb.SelectRandom(topk, bs, seed=3).select(q, k)
+    gen = torch.Generator(device=cuda).manual_seed(3)
+    draws = torch.rand(1, 2, nblk, nblk, generator=gen, device=cuda)
+    assert np.array_equal(r.cpu().numpy(), O.select_scores(draws.cpu(), topk=topk))

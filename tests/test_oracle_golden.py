@@ -189,3 +189,39 @@ def test_lsh_sign_hash_structure():
     sel1, _, _ = O.select_lsh(a, b, Z, hash_kind=O.HASH_SIGN, cap=nblk, causal=True, topk=8)
     dense, _, _ = O.select(qn, kn, kind=O.SCORE_DOT, layout=O.SEL_SSA, causal=True, topk=8)
     assert np.array_equal(sel1, dense)
+
+
+def _selector_summaries(g):
+    q, k, bs = g["q"], g["k"], int(g["bs"])
+    B, Hq, L, d = q.shape
+    Hkv = k.shape[1]
+    nblk = (L + bs - 1) // bs
+    qt, _, _ = O.pool(q, 1, grp=Hq // Hkv)
+    qt = np.concatenate([qt, np.zeros((B, Hkv, nblk * bs - L, d), np.float32)], 2)
+    qt = qt.reshape(B, Hkv, nblk, bs, d)
+    _, kmin, kmax = O.pool(k, bs)
+    qp, _, _ = O.pool(q, bs, grp=Hq // Hkv)
+    return qt, kmin, kmax, qp
+
+
+def test_other_selectors_match_reference():
+    """SelectOracle, SelectRandom, SelectLastTok, SelectMaxQMax, SelectTwoStage
+    (src/qwen_blocksparse.py:124-299) restated on the oracle's exact summaries.
+    The reference breaks score ties in torch.topk's order; the restatement takes
+    the lower block id, which only shows on rows whose scores all tie (the padded
+    last block's zero last token under SelectLastTok)."""
+    g = golden("selectors.npz")
+    topk = int(g["topk"])
+    assert np.array_equal(O.select_scores(g["mass"], topk=topk), g["oracle"])
+    assert np.array_equal(O.select_scores(g["rnd"], topk=topk), g["random"])
+    qt, kmin, kmax, qp = _selector_summaries(g)
+    last = np.ascontiguousarray(qt[:, :, :, -1])
+    sel, _, _ = O.select(last, kmax, kmin, kind=O.SCORE_QUEST, layout=O.SEL_FINISH, topk=topk,
+                         sink=True)
+    tied = ~last.any(-1)                                    # all-zero query token
+    assert np.array_equal(sel[~tied], g["lasttok"][~tied])
+    assert (sel[tied][:, :topk] <= np.arange(topk)).all()  # ties -> lowest block ids
+    assert np.array_equal(O.select_qmax(qt, kmax, kmin, topk=topk), g["qmax"])
+    M = min(2 * topk, qt.shape[2])
+    cand, _, _ = O.select(qp, kmax, kmin, kind=O.SCORE_QUEST, layout=O.SEL_RAW, topk=M)
+    assert np.array_equal(O.select_qmax(qt, kmax, kmin, topk=topk, cand=cand), g["twostage"])
