@@ -499,6 +499,8 @@ static bsa_status dispatch_fwd_tc(const bsa_attn_args *a, const AttnParams &p, c
 
 bsa_status fill_attn_params(const bsa_attn_args *a, AttnParams *p, bool bwd);
 bool fwd_sm100_applicable(const bsa_attn_args *a);
+bool fwd_b128_applicable(const bsa_attn_args *a);
+bsa_status launch_fwd_b128(const bsa_attn_args *a, const AttnParams &p, cudaStream_t st);
 bsa_status launch_fwd_sm100(const bsa_attn_args *a, const AttnParams &p, cudaStream_t st);
 
 bsa_status run_attn_fwd(const bsa_attn_args *a, cudaStream_t st) {
@@ -522,6 +524,7 @@ bsa_status run_attn_fwd(const bsa_attn_args *a, cudaStream_t st) {
                                          std::to_string(a->bs) + ", " + std::to_string(a->D) + ")");
   }
   if (fwd_sm100_applicable(a)) return launch_fwd_sm100(a, p, st);
+  if (fwd_b128_applicable(a)) return launch_fwd_b128(a, p, st);
   if (a->dtype == BSA_BF16) return dispatch_fwd_tc<__nv_bfloat16>(a, p, st);
   return dispatch_fwd_tc<__half>(a, p, st);
 }

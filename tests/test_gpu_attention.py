@@ -182,24 +182,29 @@ def test_module_drop_in_runs_and_trains(cuda):
     assert m.sel_q[0].weight.grad is not None and m.sel_q[0].weight.grad.abs().sum() > 0
 
 
-@pytest.mark.parametrize("B,H,L,kk,causal,mode", [(1, 2, 4096, 17, True, 0), (2, 2, 1984, 5, False, 0),
-                                                  (1, 4, 2048 + 64, 9, True, 1)])
-def test_tcgen05_forward_matches_mma_sync_path(cuda, monkeypatch, B, H, L, kk, causal, mode):
-    """The block-64/D-64 forward runs on tcgen05 (TMEM accumulators); the mma.sync
-    kernel (selected with BSA_FWD_LEGACY) must agree, and both match the oracle."""
+@pytest.mark.parametrize("B,H,L,kk,causal,mode,bs", [(1, 2, 4096, 17, True, 0, 64),
+                                                     (2, 2, 1984, 5, False, 0, 64),
+                                                     (1, 4, 2048 + 64, 9, True, 1, 64),
+                                                     (1, 2, 8192, 17, True, 0, 128),
+                                                     (2, 2, 3968, 6, False, 0, 128),
+                                                     (1, 4, 4096 + 128, 9, True, 1, 128)])
+def test_tcgen05_forward_matches_mma_sync_path(cuda, monkeypatch, B, H, L, kk, causal, mode, bs):
+    """The block-64 and block-128 D-64 forwards run on tcgen05 (TMEM accumulators);
+    the mma.sync kernel (selected with BSA_FWD_LEGACY) must agree, and both match
+    the oracle."""
     import _bsa
     gen = torch.Generator().manual_seed(L + kk)
     q, k, v = (torch.randn(B, H, L, 64, generator=gen).to(torch.bfloat16) for _ in range(3))
-    nblk = L // 64
+    nblk = L // bs
     sel = torch.randint(0, nblk, (B, H, nblk, kk), generator=gen)
     sel[..., 0] = torch.arange(nblk)
     gate = (torch.randn(B, H, nblk, kk, generator=gen) * 0.3) if mode == 0 else None
     args = [t.to(cuda) for t in (q, k, v)] + [sel.to(cuda, torch.int32),
                                               gate.to(cuda) if gate is not None else None]
-    o5, l5 = _bsa.attn_fwd(*args, bs=64, causal=causal, mask_mode=mode)
+    o5, l5 = _bsa.attn_fwd(*args, bs=bs, causal=causal, mask_mode=mode)
     monkeypatch.setenv("BSA_FWD_LEGACY", "1")
-    o1, l1 = _bsa.attn_fwd(*args, bs=64, causal=causal, mask_mode=mode)
-    ref = O.attention(q, k, v, sel, gate, bs=64, causal=causal, mask_mode=mode)
+    o1, l1 = _bsa.attn_fwd(*args, bs=bs, causal=causal, mask_mode=mode)
+    ref = O.attention(q, k, v, sel, gate, bs=bs, causal=causal, mask_mode=mode)
     _cmp(o5, ref, torch.bfloat16, "o tcgen05")
     _cmp(o1, ref, torch.bfloat16, "o mma.sync")
     assert (l5 - l1).abs().max().item() < 1e-4
