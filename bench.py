@@ -473,10 +473,10 @@ def run_config(a):
             if ev:
                 ev[0].record()
             if m:
+                kf, vf = m.gather_kv(k, v)
                 sel = m.select(q, k)
                 if ev:
                     ev[1].record()
-                kf, vf = m.gather_kv(k, v)
                 o, _ = _bsa.attn_fwd(q, kf, vf, sel, bs=bs, causal=True, want_lse=False,
                                      q_blk0=dist.get_rank() * (Ls // bs))
             else:
@@ -503,8 +503,8 @@ def run_config(a):
                                           "pooled keys" % (N // bs // world) if dist else "none",
                    "l2": "256 MB buffer written between timed steps"},
                   _roof("attn_fwd", fwd, ms_fwd, tf_sus, psrc), clk,
-                  {"phases": {"select(+pool/gather)": round(ms_sel, 3),
-                              "gather_kv+attn_fwd": round(ms_fwd, 3)}})
+                  {"phases": {"gather_kv+select" if dist else "select": round(ms_sel, 3),
+                              "attn_fwd": round(ms_fwd, 3)}})
     elif a.config == "4":
         # Qwen GQA prefill: N65536 Hq16 Hkv2 D256 block 128, partial RoPE (64 dims, theta 1e7),
         # SelectMax top-32 + own + sink, sigmoid output gate; also the all-blocks (dense) mode

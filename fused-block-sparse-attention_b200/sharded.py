@@ -6,10 +6,10 @@ dO rows, their selection rows, O and dQ.  K and V arrive sharded the same way
 (each rank holds the rows of its own blocks, as a sequence-parallel model
 produces them).
 
-  forward   1. pool this rank's K blocks (mean, fp32) and all-gather the pooled
-               summaries (nblk x D per head, small);
-            2. all-gather K and V into local HBM (sequence-major buffers, so the
+  forward   1. all-gather K and V into local HBM (sequence-major buffers, so the
                gathered tensor is a strided (B, H, L, D) view with no copy);
+            2. pool this rank's K blocks (mean, fp32) and all-gather the pooled
+               summaries (nblk x D per head, small);
             3. select: this rank's pooled queries against every key block,
                causal top-k with the own block first (bsa_select with a query
                range);
@@ -130,8 +130,10 @@ class ShardedBlockSparse:
         """Returns (o, ctx): o is this rank's (B, H, Ls, D) output; ctx carries what
         backward needs (the gathered K/V, the selection and the row lse)."""
         _, _, _, a = self._geometry(q)
-        sel = self.select(q, k)
+        # K/V first: every rank reaches this collective at once, before the
+        # position-dependent (causal, unbalanced) selection work
         kf, vf = self.gather_kv(k, v)
+        sel = self.select(q, k)
         o, lse = self.ops.attn_fwd(q, kf, vf, sel, bs=self.bs, causal=self.causal, q_blk0=a)
         return o, (kf, vf, sel, lse)
 
