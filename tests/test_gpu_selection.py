@@ -295,3 +295,29 @@ def test_other_selectors_golden(cuda):
     gen = torch.Generator(device=cuda).manual_seed(3)
     draws = torch.rand(1, 2, nblk, nblk, generator=gen, device=cuda)
     assert np.array_equal(r.cpu().numpy(), O.select_scores(draws.cpu(), topk=topk))
+
+
+@pytest.mark.parametrize("layout,causal,topk,dim", [(O.SEL_SSA, True, 16, 64), (O.SEL_SSA, False, 8, 128),
+                                                    (O.SEL_FINISH, True, 12, 64), (O.SEL_RAW, True, 16, 128)])
+def test_select_tensor_core_path_exact_with_ties(cuda, monkeypatch, layout, causal, topk, dim):
+    """The tf32 tensor-core scoring path (opt-in, BSA_SELECT_TC=1) must give the exact
+    fp32 selection: checked against the oracle and against the SIMT kernel, on data
+    with many exactly tied scores (repeated key summaries) that force the exact
+    fallback."""
+    import _bsa
+    gen = torch.Generator().manual_seed(topk + dim)
+    G, nblk = 4, 700
+    a = torch.randn(G, nblk, dim, generator=gen)
+    b = torch.randn(G, nblk, dim, generator=gen)
+    b[1] = b[1, :1]                       # group 1: every key summary identical (all ties)
+    b[2, ::3] = b[2, 5]                   # group 2: a third of the keys identical
+    args = dict(kind=_bsa.SCORE_DOT, layout=layout, causal=causal, topk=topk, want_score=layout == 0)
+    s_simt, sc_simt, _ = _bsa.select(a.to(cuda), b.to(cuda), **args)
+    monkeypatch.setenv("BSA_SELECT_TC", "1")
+    s_tc, sc_tc, _ = _bsa.select(a.to(cuda), b.to(cuda), **args)
+    o_sel, o_sc, _ = O.select(a, b, kind=O.SCORE_DOT, layout=layout, causal=causal, topk=topk,
+                              want_score=layout == 0)
+    assert np.array_equal(s_tc.cpu().numpy(), o_sel)
+    assert torch.equal(s_tc, s_simt)
+    if layout == 0:
+        assert np.array_equal(sc_tc.cpu().numpy(), o_sc)
