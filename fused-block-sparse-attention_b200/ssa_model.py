@@ -6,6 +6,9 @@ BlockSparseSSA(d, h, block=64, topk=8, sel_dim=32, gate=False, causal=False,
 LSHBucketSSA(d, h, block=32, topk=4, sel_dim=32, n_rounds=4, n_buckets=8, cap=8,
              gate=False, causal=False, scale=None, ...).forward(x, needle_pos=None)
                                                         (src/ssa_model.py:336-513)
+CentroidSSA(d, h, block=64, topk=8, sel_dim=32, n_centroids=16, cpq=2, cap=4,
+            gate=False, refine_topk=None).forward(x, needle_pos=None)
+                                                        (src/ssa_model.py:204-333)
 
 Same parameters (qkv, o, sel_q, sel_k MLP selectors) and outputs.  Selection
 runs on device: the selector features are block-pooled (mean for queries,
@@ -24,7 +27,7 @@ import torch.nn.functional as F
 import _bsa
 from triton_kernel import bsattn
 
-__all__ = ["BlockSparseSSA", "LSHBucketSSA"]
+__all__ = ["BlockSparseSSA", "LSHBucketSSA", "CentroidSSA", "centroid_select"]
 
 
 def _mlp_sel(d, sel_dim):
@@ -204,4 +207,117 @@ class LSHBucketSSA(nn.Module):
         if needle_pos is not None:
             chosen_last = sel[:, nblk - 1, :].long()
             self.last_hit = (chosen_last == (needle_pos // Bs).unsqueeze(-1)).any(-1).float().mean().item()
+        return self.o(out)
+
+
+@torch.no_grad()
+def centroid_select(sq, sk, cent, *, cpq, cap, refine=None):
+    """CentroidSSA's routing (src/ssa_model.py:254-299): key block j -> bucket
+    argmax_c sk_j . cent_c (the first `cap` blocks of each bucket by index); query
+    block i reads the buckets of its top-`cpq` centroids by sq_i . cent_c, its own
+    block dropped from them; optional refine = (q_blk, k_blk, rk): keep the rk
+    candidates with the largest q_blk_i . k_blk_j.  sq, sk: (B, nblk, s);
+    cent: (C, s).  Returns (sel (B, nblk, 1 + m) int64 with the own block first and
+    -1 for empty slots, key_cent (B, nblk), qc (B, nblk, C)).  O(nblk * C) tensors
+    only; no nblk x nblk score matrix.  Ties follow torch's argmax / topk."""
+    B, nblk, _ = sq.shape
+    C = cent.shape[0]
+    cpq, cap = min(cpq, C), min(cap, nblk)
+    dev = sq.device
+    kc = sk @ cent.t()
+    qc = sq @ cent.t()
+    key_cent = kc.argmax(-1)                                            # (B, nblk)
+    top_c = qc.topk(cpq, dim=-1).indices                                # (B, nblk, cpq)
+    # bucket lists: a stable sort by centroid keeps block order inside a bucket;
+    # a block's rank is its sorted position minus its bucket's first position
+    order = torch.sort(key_cent, dim=1, stable=True).indices            # (B, nblk)
+    sorted_c = key_cent.gather(1, order)
+    counts = F.one_hot(key_cent, C).sum(1)                              # (B, C)
+    first = torch.cumsum(counts, 1) - counts                            # (B, C)
+    rank = torch.arange(nblk, device=dev).view(1, nblk) - first.gather(1, sorted_c)
+    lists = torch.full((B, C, cap), -1, dtype=torch.long, device=dev)
+    ok = rank < cap
+    bidx = torch.arange(B, device=dev).view(B, 1).expand(B, nblk)
+    lists[bidx[ok], sorted_c[ok], rank[ok]] = order[ok]
+    selb = lists[torch.arange(B, device=dev).view(B, 1, 1), top_c].reshape(B, nblk, cpq * cap)
+    own = torch.arange(nblk, device=dev).view(1, nblk, 1).expand(B, nblk, 1)
+    selb = selb.masked_fill(selb == own, -1)
+    if refine is not None:
+        q_blk, k_blk, rk = refine
+        if rk < cpq * cap:
+            valid = selb >= 0
+            kcand = k_blk[torch.arange(B, device=dev).view(B, 1, 1), selb.clamp(min=0)]
+            score = (q_blk.unsqueeze(2) * kcand).sum(-1).masked_fill(~valid, float("-inf"))
+            selb = selb.gather(-1, score.topk(rk, dim=-1).indices)
+    return torch.cat([own, selb], dim=-1), key_cent, qc
+
+
+class CentroidSSA(nn.Module):
+    """Centroid-routed selection + block-sparse attention (reference
+    src/ssa_model.py:204-333); same parameters (qkv, o, sel_q, sel_k, cent).
+
+    The routing tensors are O(nblk * C) (centroid_select); empty slots repeat the
+    own block, which the attention skips as a repeated id (TOKEN masks, not
+    causal: the reference's CentroidSSA attends without a causal mask and with
+    -inf on empty slots, :318-320)."""
+
+    def __init__(self, d, h, block=64, topk=8, sel_dim=32, n_centroids=16, cpq=2, cap=4,
+                 gate=False, refine_topk=None):
+        super().__init__()
+        self.h, self.dh = h, d // h
+        self.block, self.topk = block, topk
+        self.cpq, self.cap = cpq, cap
+        self.qkv = nn.Linear(d, 3 * d)
+        self.o = nn.Linear(d, d)
+        self.sel_q = _mlp_sel(d, sel_dim)
+        self.sel_k = _mlp_sel(d, sel_dim)
+        self.sel_dim = sel_dim
+        self.cent = nn.Parameter(torch.randn(n_centroids, sel_dim) * (sel_dim ** -0.5))
+        self.refine_topk = refine_topk
+        self.gate = gate
+        self.last_hit = None
+        self.last_block_logits = None
+        self.align_q = None
+        self.align_k = None
+
+    def forward(self, x, needle_pos=None):
+        B, L, D = x.shape
+        Bs = self.block
+        pad = (Bs - L % Bs) % Bs
+        if pad:
+            x = F.pad(x, (0, 0, 0, pad))
+        Lp = L + pad
+        nblk = Lp // Bs
+        H, dh = self.h, self.dh
+        q, k, v = self.qkv(x).chunk(3, -1)
+        q = q.view(B, Lp, H, dh).transpose(1, 2)
+        k = k.view(B, Lp, H, dh).transpose(1, 2)
+        v = v.view(B, Lp, H, dh).transpose(1, 2)
+        sq = self.sel_q(x).view(B, nblk, Bs, self.sel_dim).mean(2)
+        skv = self.sel_k(x).view(B, nblk, Bs, self.sel_dim)
+        sk = torch.maximum(skv.mean(2), skv.max(2).values)
+        refine = None
+        if self.refine_topk is not None:
+            q_blk = q.detach().reshape(B, H, nblk, Bs, dh).mean(3).mean(1)
+            k_blk = k.detach().reshape(B, H, nblk, Bs, dh).mean(3).mean(1)
+            refine = (q_blk, k_blk, self.refine_topk)
+        sel_raw, key_cent, qc_ng = centroid_select(sq.detach(), sk.detach(), self.cent.detach(),
+                                                   cpq=self.cpq, cap=self.cap, refine=refine)
+        qc = sq @ self.cent.t()
+        self.last_block_logits = qc[:, nblk - 1, :].gather(1, key_cent)
+        valid = sel_raw >= 0
+        own = torch.arange(nblk, device=x.device).view(1, nblk, 1)
+        sel = torch.where(valid, sel_raw, own).to(torch.int32)
+        gate_bias = None
+        if self.gate:
+            sel_cent = key_cent.gather(1, sel.long().reshape(B, -1)).reshape(B, nblk, -1)
+            gate_bias = F.logsigmoid(torch.gather(qc, 2, sel_cent).float()).masked_fill(~valid, 0.0)
+        out = bsattn(q, k, v, sel, gate_bias, causal=False, gate_grad=self.gate,
+                     mask_mode=_bsa.MASK_TOKEN)
+        out = out.reshape(B, H, Lp, dh).transpose(1, 2).reshape(B, Lp, D)[:, :L]
+        if needle_pos is not None:
+            chosen_last = sel_raw[:, nblk - 1, :]
+            self.last_hit = (chosen_last == (needle_pos // Bs).unsqueeze(-1)).any(-1).float().mean().item()
+            self.align_q = qc[:, nblk - 1, :]
+            self.align_k_all = sk @ self.cent.t()
         return self.o(out)

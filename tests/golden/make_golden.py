@@ -20,6 +20,9 @@ Fixtures (npz, fp32 / int32):
                       its planes R, and the selection it attends with, decoded from the
                       gathered keys (key rows carry their block id) and the -inf mask it
                       hands to _sdpa (invalid picks).
+  centroid_*.npz      CentroidSSA's routing (src/ssa_model.py:254-299): its selector summaries,
+                      centroids, the head-averaged block means its refine step scores with,
+                      and the selection it attends with (read back like lsh_*.npz).
   selectors.npz       SelectOracle (random mass), SelectRandom (its CPU draws), SelectLastTok,
                       SelectMaxQMax and SelectTwoStage (src/qwen_blocksparse.py:124-299) on
                       one seeded GQA input with a padded last block.
@@ -189,6 +192,51 @@ def lsh_case(name, B, L, d, h, bs, topk, n_rounds, n_buckets, cap, causal, seed)
          causal=torch.tensor(int(causal)))
 
 
+def centroid_case(name, B, L, d, h, bs, C, cpq, cap, refine, seed):
+    import ssa_model
+    torch.manual_seed(seed)
+    nblk = L // bs
+    m = ssa_model.CentroidSSA(d, h, block=bs, n_centroids=C, cpq=cpq, cap=cap, refine_topk=refine)
+    m.eval()
+    x = torch.randn(B, L, d)
+    dh = d // h
+    qkv_real = m.qkv(x).detach()
+    kid = (torch.arange(L) // bs).float().view(1, L, 1, 1).expand(B, L, h, dh).clone()
+    q_real, k_real, _ = qkv_real.chunk(3, -1)
+    # keys carry their block id; the refine step scores with the real q/k, so feed those
+    # through a second projection call order: the module calls qkv once
+    qkv = torch.cat([q_real, kid.reshape(B, L, d), torch.zeros(B, L, d)], -1)
+    del m.qkv
+    m.qkv = lambda x_: qkv
+    cap_ = {}
+
+    def spy(q, k, v, mask):
+        cap_["k"], cap_["mask"] = k.detach().clone(), mask.detach().clone()
+        return torch.zeros_like(q)
+
+    orig = ssa_model._sdpa
+    ssa_model._sdpa = spy
+    try:
+        with torch.no_grad():
+            m(x)
+    finally:
+        ssa_model._sdpa = orig
+    kk = cap_["k"].shape[1] // bs
+    ksel = cap_["k"].view(B, h, nblk, kk, bs, dh)[:, 0, :, :, 0, 0].round().to(torch.int32)
+    mlast = cap_["mask"].reshape(B, h, nblk, -1, kk * bs)[:, 0, :, -1, :]
+    valid = torch.isfinite(mlast.reshape(B, nblk, kk, bs)[..., 0])
+    with torch.no_grad():
+        s = m.sel_dim
+        sq = m.sel_q(x).view(B, nblk, bs, s).mean(2)
+        skv = m.sel_k(x).view(B, nblk, bs, s)
+        sk = torch.maximum(skv.mean(2), skv.max(2).values)
+        kid_blk = kid.reshape(B, L, h, dh).transpose(1, 2).reshape(B, h, nblk, bs, dh).mean(3).mean(1)
+        q_blk = q_real.view(B, L, h, dh).transpose(1, 2).reshape(B, h, nblk, bs, dh).mean(3).mean(1)
+    save(name, sq=sq, sk=sk, cent=m.cent, q_blk=q_blk, k_blk=kid_blk, sel=ksel,
+         valid=valid.to(torch.int32), cpq=torch.tensor(cpq), cap=torch.tensor(cap),
+         refine=torch.tensor(refine if refine is not None else -1))
+
+
 def selectors_case(name, B, Hq, Hkv, L, d, bs, topk, seed):
     import qwen_blocksparse as qb
     torch.manual_seed(seed)
@@ -229,6 +277,8 @@ def main():
         ("lsh_causal.npz", lsh_case, (2, 2048, 64, 2, 16, 6, 4, 8, 8, True, 10)),
         ("lsh_noncausal.npz", lsh_case, (1, 1024, 64, 2, 16, 4, 3, 6, 5, False, 11)),
         ("selectors.npz", selectors_case, (1, 4, 2, 600, 16, 32, 3, 12)),
+        ("centroid_plain.npz", centroid_case, (2, 2048, 64, 2, 32, 8, 2, 6, None, 13)),
+        ("centroid_refine.npz", centroid_case, (1, 2048, 64, 2, 32, 8, 3, 8, 5, 14)),
     ]
     for name, fn, args in cases:
         if name.startswith(a.only):

@@ -321,3 +321,34 @@ def test_select_tensor_core_path_exact_with_ties(cuda, monkeypatch, layout, caus
     assert torch.equal(s_tc, s_simt)
     if layout == 0:
         assert np.array_equal(sc_tc.cpu().numpy(), o_sc)
+
+
+def test_centroid_module_matches_oracle_attention(cuda, monkeypatch):
+    """ssa_model.CentroidSSA: its attention over the centroid-routed selection (empty
+    slots skipped, no causal mask, gate) equals the oracle attention, and gradients
+    reach the selector MLPs and the centroids."""
+    import ssa_model
+    real = ssa_model.bsattn
+    for refine in (None, 3):
+        torch.manual_seed(5)
+        m = ssa_model.CentroidSSA(128, 2, block=32, n_centroids=6, cpq=2, cap=3, gate=True,
+                                  refine_topk=refine).to(cuda)
+        x = torch.randn(2, 1000, 128, device=cuda)
+        seen = {}
+
+        def spy(q, k, v, sel, gate, causal=False, gate_grad=False, mask_mode=0):
+            out = real(q, k, v, sel, gate, causal=causal, gate_grad=gate_grad, mask_mode=mask_mode)
+            seen.update(q=q, k=k, v=v, sel=sel, gate=gate, mode=mask_mode, causal=causal, out=out)
+            return out
+
+        monkeypatch.setattr(ssa_model, "bsattn", spy)
+        out = m(x)
+        out.float().sum().backward()
+        assert torch.isfinite(out).all()
+        assert m.cent.grad is not None and torch.isfinite(m.cent.grad).all()
+        ref = O.attention(seen["q"].detach().float().cpu(), seen["k"].detach().float().cpu(),
+                          seen["v"].detach().float().cpu(), seen["sel"].cpu().long(),
+                          seen["gate"].detach().float().cpu(), bs=32, causal=seen["causal"],
+                          mask_mode=seen["mode"])
+        err = (seen["out"].detach().float().cpu() - ref).abs().max().item()
+        assert err < 1e-4, err

@@ -225,3 +225,20 @@ def test_other_selectors_match_reference():
     M = min(2 * topk, qt.shape[2])
     cand, _, _ = O.select(qp, kmax, kmin, kind=O.SCORE_QUEST, layout=O.SEL_RAW, topk=M)
     assert np.array_equal(O.select_qmax(qt, kmax, kmin, topk=topk, cand=cand), g["twostage"])
+
+
+def test_centroid_routing_matches_reference():
+    """ssa_model.centroid_select (torch, no nblk^2 tensor) reproduces CentroidSSA's
+    selection (src/ssa_model.py:254-299), with and without the refine step."""
+    import ssa_model
+    for name in ("centroid_plain.npz", "centroid_refine.npz"):
+        g = golden(name)
+        rk = int(g["refine"])
+        refine = (_t(g["q_blk"]), _t(g["k_blk"]), rk) if rk > 0 else None
+        sel, _, _ = ssa_model.centroid_select(_t(g["sq"]), _t(g["sk"]), _t(g["cent"]),
+                                              cpq=int(g["cpq"]), cap=int(g["cap"]), refine=refine)
+        sel = sel.numpy()
+        valid = g["valid"].astype(bool)
+        assert sel.shape == g["sel"].shape, name
+        assert np.array_equal(sel[valid], g["sel"][valid]), name
+        assert (sel[~valid] == -1).all(), name
