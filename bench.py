@@ -163,43 +163,69 @@ def count_launches(cfg, q, k, v, do):
 
 
 def e2e_run(cfg, heads, q, k, v, do, steps, warmup):
-    """Same step through the public drop-in API with host buffers: pinned H2D of
-    q, k, v, dO, then selection + bsattn forward/backward, then D2H of o, dq, dk, dv."""
+    """Same step through the public drop-in API with host buffers: every step copies
+    its q, k, v, dO in from pinned host memory, runs selection + bsattn forward and
+    backward, and copies o, dq, dk, dv back out.  Copies run on their own streams
+    and overlap the neighbouring steps' compute (inputs double-buffered on the
+    device, outputs double-buffered on the host); the timed region spans the first
+    step's input copy to the last step's output copy."""
     import selection
     import triton_kernel as tk
     hs = [t.cpu().pin_memory() for t in (q, k, v, do)]
-    outs = [torch.empty_like(h).pin_memory() for h in hs]
-    dev_in = [torch.empty_like(t) for t in (q, k, v, do)]
-    s = torch.cuda.current_stream()
+    outs = [[torch.empty_like(h).pin_memory() for h in hs] for _ in range(2)]
+    dev_in = [[torch.empty_like(t) for t in (q, k, v, do)] for _ in range(2)]
+    comp = torch.cuda.current_stream()
+    up, down = torch.cuda.Stream(), torch.cuda.Stream()
+    in_ready = [torch.cuda.Event() for _ in range(2)]
+    used = [torch.cuda.Event() for _ in range(2)]
 
-    def one():
-        for d, h in zip(dev_in, hs):
-            d.copy_(h, non_blocking=True)
-        qd, kd, vd, dod = dev_in
+    def upload(buf):
+        with torch.cuda.stream(up):
+            up.wait_event(used[buf])
+            for d, h in zip(dev_in[buf], hs):
+                d.copy_(h, non_blocking=True)
+            in_ready[buf].record(up)
+
+    def compute(buf):
+        comp.wait_event(in_ready[buf])
+        qd, kd, vd, dod = (t.detach() for t in dev_in[buf])
         sel, _, _ = selection.select_meanpool(qd, kd, bs=cfg["bs"], topk=cfg["topk"])
         qd.requires_grad_(True)
         kd.requires_grad_(True)
         vd.requires_grad_(True)
         o = tk.bsattn(qd, kd, vd, sel, None, causal=cfg["causal"])
         o.backward(dod)
-        for h, d in zip(outs, (o, qd.grad, kd.grad, vd.grad)):
-            h.copy_(d.detach(), non_blocking=True)
-        for t in (qd, kd, vd):
-            t.grad = None
-            t.requires_grad_(False)
+        res = [o.detach(), qd.grad, kd.grad, vd.grad]
+        used[buf].record(comp)
+        return res
 
-    for _ in range(warmup):
-        one()
+    def download(buf, res):
+        with torch.cuda.stream(down):
+            down.wait_event(used[buf])
+            for h, d in zip(outs[buf], res):
+                h.copy_(d, non_blocking=True)
+                d.record_stream(down)
+
+    def run(n):
+        upload(0)
+        for i in range(n):
+            if i + 1 < n:
+                upload((i + 1) % 2)
+            res = compute(i % 2)
+            download(i % 2, res)
+
+    for e in used:
+        e.record(comp)
+    run(warmup)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(s)
-    for _ in range(steps):
-        one()
-    e1.record(s)
+    e0.record(up)
+    run(steps)
+    e1.record(down)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / steps
     nbytes = sum(t.numel() * t.element_size() for t in hs)
-    return ms, nbytes, sum(t.numel() * t.element_size() for t in outs)
+    return ms, nbytes, sum(t.numel() * t.element_size() for t in outs[0])
 
 
 def run_ours(a):
@@ -245,7 +271,7 @@ def run_ours(a):
         dist.all_reduce(vals, op=dist.ReduceOp.MAX)
     ms_step, ms_sel, ms_fwd, ms_bwd = vals.tolist()
 
-    e2e_ms, h2d, d2h = e2e_run(cfg, heads, q, k, v, do, max(2, a.steps // 4), 1)
+    e2e_ms, h2d, d2h = e2e_run(cfg, heads, q, k, v, do, max(4, a.steps), 2)
     ev = torch.tensor([e2e_ms], device=dev)
     if dist:
         dist.all_reduce(ev, op=dist.ReduceOp.MAX)
@@ -356,7 +382,7 @@ def run_reference(a):
     if rank != 0:
         return
     cfg = workload(a)
-    smp = CpuSample(cfg, cfg["H"], a.cpu_sample)
+    smp = CpuSample(cfg, cfg["H"], a.ref_sample)
     for _ in range(a.warmup):
         smp.run()
     ts = [smp.run() for _ in range(a.steps)]
@@ -374,7 +400,7 @@ def run_reference(a):
                    "kk": cfg["kk"]},
         "cpu_baseline": {"value": round(value, 1), "unit": UNIT, "cores": cores, "kind": "port",
                          "sample": "%d query blocks x %d heads per step (%d tokens), mean of %d "
-                                   "steps" % (a.cpu_sample, cfg["H"], smp.tokens(), a.steps)},
+                                   "steps" % (a.ref_sample, cfg["H"], smp.tokens(), a.steps)},
         "e2e": {"value": round(value, 1), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -579,7 +605,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--seqlen", "--n", dest="n", type=int, default=262144,
                     help="sequence length (default 262144; 1048576 for --config 3b)")
-    ap.add_argument("--cpu-sample", type=int, default=64, help="query blocks in the CPU sample")
+    ap.add_argument("--cpu-sample", type=int, default=2048,
+                    help="query blocks in the cpu_baseline sample (about 10 s of CPU work)")
+    ap.add_argument("--ref-sample", type=int, default=256,
+                    help="query blocks per step of the --impl reference arm")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--config", default="3a", choices=["3a", "2", "3b", "4", "5"],
                     help="BASELINE configuration (3a = the driver line)")
