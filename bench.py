@@ -333,6 +333,7 @@ class CpuSample:
 
     def __init__(self, cfg, heads, S):
         from oracle import oracle as O
+        S = min(S, cfg["nblk"] - 1)
         self.O = O
         torch.set_num_threads(os.cpu_count() or 1)
         self.cfg, self.heads, self.S = cfg, heads, S
@@ -358,8 +359,9 @@ class CpuSample:
         sel_rows = torch.cat([own, top], -1)
         sel = torch.zeros(B, H, nblk, cfg["kk"], dtype=torch.long)
         sel[:, :, i0:] = sel_rows
-        self.O.attention_grads(self.q, self.k, self.v, sel, self.do, None, bs=bs, causal=True,
-                               dtype=torch.float32, qblk_range=(i0, nblk))
+        for c0 in range(i0, nblk, 128):     # bounded memory: 128 query blocks at a time
+            self.O.attention_grads(self.q, self.k, self.v, sel, self.do, None, bs=bs, causal=True,
+                                   dtype=torch.float32, qblk_range=(c0, min(c0 + 128, nblk)))
         return time.perf_counter() - t0
 
     def tokens(self):
