@@ -187,7 +187,9 @@ def test_module_drop_in_runs_and_trains(cuda):
                                                      (1, 4, 2048 + 64, 9, True, 1, 64),
                                                      (1, 2, 8192, 17, True, 0, 128),
                                                      (2, 2, 3968, 6, False, 0, 128),
-                                                     (1, 4, 4096 + 128, 9, True, 1, 128)])
+                                                     (1, 4, 4096 + 128, 9, True, 1, 128),
+                                                     (1, 2, 8192 - 37, 9, True, 0, 128),
+                                                     (1, 2, 4096 - 5, 9, True, 1, 64)])
 def test_tcgen05_forward_matches_mma_sync_path(cuda, monkeypatch, B, H, L, kk, causal, mode, bs):
     """The block-64 and block-128 D-64 forwards run on tcgen05 (TMEM accumulators);
     the mma.sync kernel (selected with BSA_FWD_LEGACY) must agree, and both match
@@ -195,7 +197,7 @@ def test_tcgen05_forward_matches_mma_sync_path(cuda, monkeypatch, B, H, L, kk, c
     import _bsa
     gen = torch.Generator().manual_seed(L + kk)
     q, k, v = (torch.randn(B, H, L, 64, generator=gen).to(torch.bfloat16) for _ in range(3))
-    nblk = L // bs
+    nblk = (L + bs - 1) // bs                     # ragged L: a partial last block
     sel = torch.randint(0, nblk, (B, H, nblk, kk), generator=gen)
     sel[..., 0] = torch.arange(nblk)
     gate = (torch.randn(B, H, nblk, kk, generator=gen) * 0.3) if mode == 0 else None
