@@ -1,13 +1,16 @@
 // Block-sparse attention forward on tcgen05 for block 128, head dim 64 (the
-// long-context configuration).
+// long-context configuration) or 256 (the Qwen GQA configuration).
 //
 // One CTA computes one query block (128 rows = one M=128 UMMA tile) of one
-// head.  Per live slot j (a selected key block):
-//   S_j  = Q K_j^T      4 x tcgen05.mma 128x128x16 into TMEM (fp32)
+// query head.  K and V move through shared memory in 64-column chunks
+// (16 KB each), so D = 256 needs no more buffer than D = 64 per ring slot.
+// Per live slot j (a selected key block):
+//   S_j  = Q K_j^T      per 64-column chunk 4 x tcgen05.mma 128x128x16 (fp32, TMEM)
 //   P_j  = 2^(S_j * scale * log2e + gate - m)   (bf16, shared memory)
-//   O   += P_j V_j      8 x tcgen05.mma 128x64x16, O accumulated in TMEM
-// TMEM: S columns [0, 128), O columns [128, 192) (256 allocated: two CTAs per SM).
-// Row m of every tile lives in TMEM lane m.
+//   O   += P_j V_j      per 64-column chunk 8 x tcgen05.mma 128x64x16 into TMEM
+// TMEM: S columns [0, 128), O columns [128, 128 + D) (D = 64: 256 allocated,
+// two CTAs per SM; D = 256: 512, one).  Row m of every tile lives in lane m.
+// An optional sigmoid output gate (Qwen) is applied in the epilogue.
 //
 // Warp roles (320 threads; <= 96 registers per thread keeps two CTAs per SM):
 //   warps 0-7  softmax: warp w reads rows 32*(w&3).. and key columns
@@ -17,8 +20,9 @@
 //              when the block raises it by more than 2^8 (lazy rescaling; O is
 //              rescaled in TMEM); P is written 128B-swizzled K-major in two
 //              64-key regions; final O / l.
-//   warp 8     TMA producer (one thread): Q once, then K and V blocks into two
-//              rings of two stages (K freed by S_j's completion, V by PV_j's).
+//   warp 8     TMA producer (one thread): Q once, then the K and V chunks of
+//              every step into two rings of 64-column slots (a K slot is freed
+//              by the S MMAs that read it, a V slot by the PV MMAs).
 //   warp 9     TMEM owner and MMA-issuing thread: S_{j+1} as soon as all
 //              softmax warps have read S_j, PV_j as soon as P_j is complete.
 // Every mbarrier wait is bounded; a timeout sets BSA_DEVERR_TIMEOUT.
@@ -31,37 +35,47 @@
 namespace bsa {
 
 namespace {
-constexpr int G8_BS = 128, G8_D = 64, G8_NST = 2;
-constexpr int G8_TILE = G8_BS * G8_D * 2;  // 16 KB: a 128-row block of 64 dims
-constexpr int G8_MAXN = 64;                // live slots kept in shared memory
-constexpr int G8_SMEM = 1024 + G8_TILE + 2 * G8_NST * G8_TILE + 2 * G8_TILE;  // Q, K, V rings, P
+constexpr int G8_BS = 128;
+constexpr int G8_TILE = G8_BS * 64 * 2;  // 16 KB: a 128-row block of 64 columns
 constexpr int G8_WPROD = 8, G8_WMMA = 9, G8_THREADS = 320;
-constexpr uint32_t G8_TMEM_COLS = 256;
 constexpr int G8_SCOL = 0, G8_OCOL = 128;
 constexpr float G8_RESCALE = 8.f;  // log2 units
+template <int D>
+struct G8 {
+  static constexpr int NCH = D / 64;                 // 64-column chunks per row
+  static constexpr int NSL = D == 64 ? 2 : 3;        // ring slots (K and V each)
+  static constexpr int SMEM = 1024 + NCH * G8_TILE + 2 * NSL * G8_TILE + 2 * G8_TILE;
+  static constexpr uint32_t TMEM_COLS = D == 64 ? 256 : 512;
+  static constexpr int MINB = D == 64 ? 2 : 1;       // CTAs per SM
+  // live slots kept in shared memory (D = 256 also runs the identity selection,
+  // every causal block, for up to 512 blocks)
+  static constexpr int MAXN = D == 64 ? 64 : 512;
+};
 }  // namespace
 
-template <typename T>
-__global__ void __launch_bounds__(G8_THREADS, 2)
+template <typename T, int D>
+__global__ void __launch_bounds__(G8_THREADS, G8<D>::MINB)
     attn_fwd_b128_kernel(const __grid_constant__ CUtensorMap tq,
                          const __grid_constant__ CUtensorMap tk,
                          const __grid_constant__ CUtensorMap tv, const int perm_q,
                          const int perm_k, const int perm_v, const AttnParams p) {
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr uint32_t IDESC_S = tc05::idesc_f16(kBF16, 128, 128, false);
-  constexpr uint32_t IDESC_PV = tc05::idesc_f16(kBF16, 128, G8_D, true);
+  constexpr uint32_t IDESC_PV = tc05::idesc_f16(kBF16, 128, 64, true);
+  constexpr int NCH = G8<D>::NCH, NSL = G8<D>::NSL;
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~uintptr_t(1023));
-  uint8_t *sQ = smem;
-  uint8_t *sK = sQ + G8_TILE;               // K ring
-  uint8_t *sV = sK + G8_NST * G8_TILE;      // V ring
-  uint8_t *sP = sV + G8_NST * G8_TILE;      // P: keys 0-63 at sP, 64-127 at sP + TILE
-  __shared__ __align__(8) uint64_t bar_q, k_full[G8_NST], k_empty[G8_NST], v_full[G8_NST],
-      v_empty[G8_NST], s_full, s_empty, p_full, o_done;
+  uint8_t *sQ = smem;                       // Q chunk c at sQ + c * TILE
+  uint8_t *sK = sQ + NCH * G8_TILE;         // K ring: NSL chunk slots
+  uint8_t *sV = sK + NSL * G8_TILE;         // V ring: NSL chunk slots
+  uint8_t *sP = sV + NSL * G8_TILE;         // P: keys 0-63 at sP, 64-127 at sP + TILE
+  __shared__ __align__(8) uint64_t bar_q, k_full[NSL], k_empty[NSL], v_full[NSL], v_empty[NSL],
+      s_full, s_empty, p_full, o_done;
   __shared__ uint32_t tmem_base_sh;
-  __shared__ int s_item[G8_MAXN];   // (kb << 3) | kind of the j-th live slot
-  __shared__ int s_islot[G8_MAXN];
+  constexpr int MAXN = G8<D>::MAXN;
+  __shared__ int s_item[MAXN];   // (kb << 3) | kind of the j-th live slot
+  __shared__ int s_islot[MAXN];
   __shared__ int s_n;
   __shared__ float s_xch[2][4][2][32];  // half-row maxima (by step parity), then sums
 
@@ -77,24 +91,36 @@ __global__ void __launch_bounds__(G8_THREADS, 2)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
   if (tid == 0) {
-    const int32_t *selrow = p.sel + b * p.sel_sb + hk * p.sel_sh + (long long)qi * p.sel_sn;
     int n = 0;
-    for (int slot = 0; slot < p.kk; ++slot) {
-      const int kb = __ldg(selrow + slot);
-      bool dup = false;
-      if (p.mask_mode == BSA_MASK_TOKEN)
-        for (int i = 0; i < slot && !dup; ++i) dup = __ldg(selrow + i) == kb;
-      const int kind =
-          slot_kind(kb, slot, dup, qblk, p.nblk, p.bs, p.L, p.mask_mode, p.causal, p.status);
-      if (kind != KIND_SKIP && n < G8_MAXN) {
-        s_item[n] = (kb << 3) | kind;
-        s_islot[n] = slot;
-        ++n;
+    if (p.sel) {
+      const int32_t *selrow = p.sel + b * p.sel_sb + hk * p.sel_sh + (long long)qi * p.sel_sn;
+      for (int slot = 0; slot < p.kk; ++slot) {
+        const int kb = __ldg(selrow + slot);
+        bool dup = false;
+        if (p.mask_mode == BSA_MASK_TOKEN)
+          for (int i = 0; i < slot && !dup; ++i) dup = __ldg(selrow + i) == kb;
+        const int kind =
+            slot_kind(kb, slot, dup, qblk, p.nblk, p.bs, p.L, p.mask_mode, p.causal, p.status);
+        if (kind != KIND_SKIP && n < MAXN) {
+          s_item[n] = (kb << 3) | kind;
+          s_islot[n] = slot;
+          ++n;
+        }
+      }
+    } else {  // identity selection: slot j is block j
+      for (int kb = 0; kb < p.nblk && n < MAXN; ++kb) {
+        const int kind = slot_kind(kb, kb, false, qblk, p.nblk, p.bs, p.L, p.mask_mode, p.causal,
+                                   p.status);
+        if (kind != KIND_SKIP) {
+          s_item[n] = (kb << 3) | kind;
+          s_islot[n] = kb;
+          ++n;
+        }
       }
     }
     s_n = n;
     mbar_init(&bar_q, 1);
-    for (int s = 0; s < G8_NST; ++s) {
+    for (int s = 0; s < NSL; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
       mbar_init(&v_full[s], 1);
@@ -107,7 +133,7 @@ __global__ void __launch_bounds__(G8_THREADS, 2)
     fence_mbar_init();
   }
   if (warp == G8_WMMA) {
-    tc05::alloc(&tmem_base_sh, G8_TMEM_COLS);
+    tc05::alloc(&tmem_base_sh, G8<D>::TMEM_COLS);
     tc05::relinquish();
   }
   tc05::fence_before();
@@ -116,20 +142,25 @@ __global__ void __launch_bounds__(G8_THREADS, 2)
   const uint32_t tmem = tmem_base_sh;
   const int nsteps = s_n;
 
+  // Chunk sequence of each ring: step j's chunks c = 0 .. NCH-1, in step order;
+  // chunk number n = j * NCH + c uses slot n % NSL.  The producer issues the K
+  // chunks of step j + 1 before the V chunks of step j.
   if (warp == G8_WPROD) {
-    // ================= TMA producer: Q once; K_{j+1} before waiting for V_j's slot
+    // ================= TMA producer
     if (lane == 0) {
-      mbar_expect_tx(&bar_q, G8_TILE);
-      tma_load_rhb(sQ, &tq, &bar_q, perm_q, 0, qi * p.bs, h, b);
+      mbar_expect_tx(&bar_q, NCH * G8_TILE);
+      for (int c = 0; c < NCH; ++c)
+        tma_load_rhb(sQ + c * G8_TILE, &tq, &bar_q, perm_q, 64 * c, qi * p.bs, h, b);
       auto load = [&](bool isv, int j) {
-        const int st = j % G8_NST;
-        uint64_t *full = isv ? &v_full[st] : &k_full[st];
-        uint64_t *empty = isv ? &v_empty[st] : &k_empty[st];
-        if (j >= G8_NST && !mbar_wait(empty, ((j / G8_NST) - 1) & 1))
-          report(p.status, BSA_DEVERR_TIMEOUT);
-        mbar_expect_tx(full, G8_TILE);
-        tma_load_rhb((isv ? sV : sK) + st * G8_TILE, isv ? &tv : &tk, full, isv ? perm_v : perm_k,
-                     0, (s_item[j] >> 3) * p.bs, hk, b);
+        for (int c = 0; c < NCH; ++c) {
+          const int n = j * NCH + c, sl = n % NSL;
+          uint64_t *full = isv ? &v_full[sl] : &k_full[sl];
+          uint64_t *empty = isv ? &v_empty[sl] : &k_empty[sl];
+          if (n >= NSL && !mbar_wait(empty, ((n / NSL) - 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
+          mbar_expect_tx(full, G8_TILE);
+          tma_load_rhb((isv ? sV : sK) + sl * G8_TILE, isv ? &tv : &tk, full, isv ? perm_v : perm_k,
+                       64 * c, (s_item[j] >> 3) * p.bs, hk, b);
+        }
       };
       if (nsteps > 0) load(false, 0);
       for (int j = 0; j < nsteps; ++j) {
@@ -143,31 +174,38 @@ __global__ void __launch_bounds__(G8_THREADS, 2)
       if (!mbar_wait(&bar_q, 0)) report(p.status, BSA_DEVERR_TIMEOUT);
       const uint64_t dq = tc05::sdesc(smem_u32(sQ), 16, 1024);
       auto issue_s = [&](int js) {
-        const int st = js % G8_NST;
-        if (!mbar_wait(&k_full[st], (js / G8_NST) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
         if (js >= 1 && !mbar_wait(&s_empty, (js - 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
-        tc05::fence_after();
-        const uint64_t dk = tc05::sdesc(smem_u32(sK + st * G8_TILE), 16, 1024);
+        for (int c = 0; c < NCH; ++c) {
+          const int n = js * NCH + c, sl = n % NSL;
+          if (!mbar_wait(&k_full[sl], (n / NSL) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
+          tc05::fence_after();
+          const uint64_t dk = tc05::sdesc(smem_u32(sK + sl * G8_TILE), 16, 1024);
+          const uint64_t dqc = dq + c * (G8_TILE >> 4);
 #pragma unroll
-        for (int ks = 0; ks < G8_D / 16; ++ks)
-          tc05::mma_f16(tc05::taddr(tmem, 0, G8_SCOL), dq + 2 * ks, dk + 2 * ks, IDESC_S, ks > 0);
+          for (int ks = 0; ks < 4; ++ks)
+            tc05::mma_f16(tc05::taddr(tmem, 0, G8_SCOL), dqc + 2 * ks, dk + 2 * ks, IDESC_S,
+                          (c > 0 || ks > 0) ? 1u : 0u);
+          tc05::commit(&k_empty[sl]);
+        }
         tc05::commit(&s_full);
-        tc05::commit(&k_empty[st]);
       };
       if (nsteps > 0) issue_s(0);
       for (int jp = 0; jp < nsteps; ++jp) {
         if (jp + 1 < nsteps) issue_s(jp + 1);
-        const int st = jp % G8_NST;
         if (!mbar_wait(&p_full, jp & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
-        if (!mbar_wait(&v_full[st], (jp / G8_NST) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
-        tc05::fence_after();
-        const uint64_t dv = tc05::sdesc(smem_u32(sV + st * G8_TILE), G8_TILE, 1024);
         const uint64_t dp = tc05::sdesc(smem_u32(sP), 16, 1024);
+        for (int c = 0; c < NCH; ++c) {
+          const int n = jp * NCH + c, sl = n % NSL;
+          if (!mbar_wait(&v_full[sl], (n / NSL) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
+          tc05::fence_after();
+          const uint64_t dv = tc05::sdesc(smem_u32(sV + sl * G8_TILE), G8_TILE, 1024);
 #pragma unroll
-        for (int ks = 0; ks < G8_BS / 16; ++ks)  // keys 16*ks: region ks/4, +32 B per 16 keys
-          tc05::mma_f16(tc05::taddr(tmem, 0, G8_OCOL), dp + (ks >> 2) * (G8_TILE >> 4) + 2 * (ks & 3),
-                        dv + 128 * ks, IDESC_PV, (jp > 0 || ks > 0) ? 1u : 0u);
-        tc05::commit(&v_empty[st]);
+          for (int ks = 0; ks < G8_BS / 16; ++ks)  // keys 16*ks: P region ks/4, +32 B per 16 keys
+            tc05::mma_f16(tc05::taddr(tmem, 0, G8_OCOL + 64 * c),
+                          dp + (ks >> 2) * (G8_TILE >> 4) + 2 * (ks & 3), dv + 128 * ks, IDESC_PV,
+                          (jp > 0 || ks > 0) ? 1u : 0u);
+          tc05::commit(&v_empty[sl]);
+        }
         tc05::commit(&o_done);
       }
     }
@@ -178,8 +216,9 @@ __global__ void __launch_bounds__(G8_THREADS, 2)
     const int cb = 64 * hf;          // first key column of this warp
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
     const uint32_t pbase = smem_u32(sP + hf * G8_TILE);
-    const float *gaterow =
-        p.gate ? p.gate + b * p.gate_sb + hk * p.gate_sh + (long long)qi * p.gate_sn : nullptr;
+    const float *gaterow = (p.gate && p.sel)
+                               ? p.gate + b * p.gate_sb + hk * p.gate_sh + (long long)qi * p.gate_sn
+                               : nullptr;
     float m_used = -INFINITY, l = 0.f;
     for (int j = 0; j < nsteps; ++j) {
       if (!mbar_wait(&s_full, j & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
@@ -252,14 +291,17 @@ __global__ void __launch_bounds__(G8_THREADS, 2)
       }
       l += ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
       if (__any_sync(0xffffffffu, need) && j >= 1) {
-        // O columns [32*hf, +32) of this warp's rows
-        float o[32];
-        const uint32_t ta = tmem + lane_base + G8_OCOL + 32 * hf;
-        tc05::ld32(ta, o);
-        tc05::wait_ld();
+        // O columns [hf * D/2, +D/2) of this warp's rows, 32 at a time
+#pragma unroll 1
+        for (int c32 = 0; c32 < D / 64; ++c32) {
+          float o[32];
+          const uint32_t ta = tmem + lane_base + G8_OCOL + hf * (D / 2) + 32 * c32;
+          tc05::ld32(ta, o);
+          tc05::wait_ld();
 #pragma unroll
-        for (int c = 0; c < 32; ++c) o[c] *= alpha;
-        tc05::st32(ta, o);
+          for (int c = 0; c < 32; ++c) o[c] *= alpha;
+          tc05::st32(ta, o);
+        }
         tc05::wait_st();
       }
       fence_proxy_async_smem();
@@ -275,27 +317,38 @@ __global__ void __launch_bounds__(G8_THREADS, 2)
       if (!mbar_wait(&o_done, (nsteps - 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
       tc05::fence_after();
     }
-    float o[32];
-    tc05::ld32(tmem + lane_base + G8_OCOL + 32 * hf, o);
-    tc05::wait_ld();
-    if (nsteps == 0) {
-#pragma unroll
-      for (int c = 0; c < 32; ++c) o[c] = 0.f;
-    }
     const long long grow = (long long)qi * p.bs + r;
     const long long bh = (long long)b * p.Hq + h;
     if (p.lse && hf == 0) p.lse[bh * p.Lp + grow] = lt > 0.f ? m_used + __log2f(lt) : INFINITY;
-    if (grow < p.Lq) {
-      const float inv = (nsteps > 0 && lt > 0.f) ? 1.f / lt : 0.f;
-      T *orow = reinterpret_cast<T *>(p.o) + b * p.o_sb + h * p.o_sh + grow * p.o_sl + 32 * hf;
+    const float inv = (nsteps > 0 && lt > 0.f) ? 1.f / lt : 0.f;
+    T *orow = reinterpret_cast<T *>(p.o) + b * p.o_sb + h * p.o_sh + grow * p.o_sl + hf * (D / 2);
+    const T *grow_g = p.og ? reinterpret_cast<const T *>(p.og) + b * p.og_sb + h * p.og_sh +
+                                 grow * p.og_sl + hf * (D / 2)
+                           : nullptr;
+#pragma unroll 1
+    for (int c32 = 0; c32 < D / 64; ++c32) {
+      float o[32];
+      tc05::ld32(tmem + lane_base + G8_OCOL + hf * (D / 2) + 32 * c32, o);
+      tc05::wait_ld();
+      if (grow >= p.Lq) continue;
 #pragma unroll
       for (int c8 = 0; c8 < 4; ++c8) {
         uint4 wv;
-        wv.x = Mma<T>::pack(o[c8 * 8 + 0] * inv, o[c8 * 8 + 1] * inv);
-        wv.y = Mma<T>::pack(o[c8 * 8 + 2] * inv, o[c8 * 8 + 3] * inv);
-        wv.z = Mma<T>::pack(o[c8 * 8 + 4] * inv, o[c8 * 8 + 5] * inv);
-        wv.w = Mma<T>::pack(o[c8 * 8 + 6] * inv, o[c8 * 8 + 7] * inv);
-        *reinterpret_cast<uint4 *>(orow + c8 * 8) = wv;
+        uint32_t *w = reinterpret_cast<uint32_t *>(&wv);
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          w[e] = Mma<T>::pack(o[c8 * 8 + 2 * e] * inv, o[c8 * 8 + 2 * e + 1] * inv);
+        if (grow_g) {  // sigmoid output gate, rounded as the reference's bf16 ops
+          const uint4 gq = *reinterpret_cast<const uint4 *>(grow_g + 32 * c32 + c8 * 8);
+          T *ov = reinterpret_cast<T *>(&wv);
+          const T *gv = reinterpret_cast<const T *>(&gq);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float sg = Mma<T>::to_f(Mma<T>::from_f(1.f / (1.f + expf(-Mma<T>::to_f(gv[e])))));
+            ov[e] = Mma<T>::from_f(Mma<T>::to_f(ov[e]) * sg);
+          }
+        }
+        *reinterpret_cast<uint4 *>(orow + 32 * c32 + c8 * 8) = wv;
       }
     }
   }
@@ -303,29 +356,41 @@ __global__ void __launch_bounds__(G8_THREADS, 2)
   __syncthreads();
   if (warp == G8_WMMA) {
     tc05::fence_after();
-    tc05::dealloc(tmem, G8_TMEM_COLS);
+    tc05::dealloc(tmem, G8<D>::TMEM_COLS);
   }
 }
 
 bool fwd_b128_applicable(const bsa_attn_args *a) {
-  return a->dtype != BSA_F32 && a->bs == 128 && a->D == 64 && a->sel && a->kk <= G8_MAXN &&
-         !a->out_gate.ptr && !getenv("BSA_FWD_LEGACY");
+  if (a->dtype == BSA_F32 || a->bs != 128 || (a->D != 64 && a->D != 256) || getenv("BSA_FWD_LEGACY"))
+    return false;
+  const int maxn = a->D == 64 ? G8<64>::MAXN : G8<256>::MAXN;
+  return a->sel ? a->kk <= maxn : (a->D == 256 && a->nblk <= maxn);
 }
 
 bsa_status launch_fwd_b128(const bsa_attn_args *a, const AttnParams &p, cudaStream_t st) {
   TensorMap4 mq, mk, mv;
   bsa_status s;
-  if ((s = make_tmap(&mq, a->q.ptr, a->dtype, a->B, a->Hq, p.Lq, 64, a->q.sb, a->q.sh, a->q.sl, 128, "q")))
+  if ((s = make_tmap(&mq, a->q.ptr, a->dtype, a->B, a->Hq, p.Lq, a->D, a->q.sb, a->q.sh, a->q.sl, 128, "q")))
     return s;
-  if ((s = make_tmap(&mk, a->k.ptr, a->dtype, a->B, a->Hkv, a->L, 64, a->k.sb, a->k.sh, a->k.sl, 128, "k")))
+  if ((s = make_tmap(&mk, a->k.ptr, a->dtype, a->B, a->Hkv, a->L, a->D, a->k.sb, a->k.sh, a->k.sl, 128, "k")))
     return s;
-  if ((s = make_tmap(&mv, a->v.ptr, a->dtype, a->B, a->Hkv, a->L, 64, a->v.sb, a->v.sh, a->v.sl, 128, "v")))
+  if ((s = make_tmap(&mv, a->v.ptr, a->dtype, a->B, a->Hkv, a->L, a->D, a->v.sb, a->v.sh, a->v.sl, 128, "v")))
     return s;
   auto pk = [](const TensorMap4 &m) { return m.perm[0] | (m.perm[1] << 2) | (m.perm[2] << 4); };
   const long long grid = (long long)a->B * a->Hq * p.nq;
-  auto kern = a->dtype == BSA_BF16 ? attn_fwd_b128_kernel<__nv_bfloat16> : attn_fwd_b128_kernel<__half>;
-  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G8_SMEM);
-  kern<<<(unsigned)grid, G8_THREADS, G8_SMEM, st>>>(mq.map, mk.map, mv.map, pk(mq), pk(mk), pk(mv), p);
+#define BSA_G8(T_, D_)                                                                         \
+  {                                                                                            \
+    auto kern = attn_fwd_b128_kernel<T_, D_>;                                                  \
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, G8<D_>::SMEM);     \
+    kern<<<(unsigned)grid, G8_THREADS, G8<D_>::SMEM, st>>>(mq.map, mk.map, mv.map, pk(mq),     \
+                                                            pk(mk), pk(mv), p);                \
+  }
+  if (a->dtype == BSA_BF16) {
+    if (a->D == 64) BSA_G8(__nv_bfloat16, 64) else BSA_G8(__nv_bfloat16, 256)
+  } else {
+    if (a->D == 64) BSA_G8(__half, 64) else BSA_G8(__half, 256)
+  }
+#undef BSA_G8
   return check_launch("attn_fwd_b128");
 }
 

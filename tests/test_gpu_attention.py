@@ -245,3 +245,49 @@ def test_tcgen05_backward_matches_mma_sync_path(cuda, monkeypatch, Hq, Hkv, shar
     for i, (ref, name) in enumerate(((rq, "dq"), (rk, "dk"), (rv, "dv"))):
         _cmp(r5[i], ref, torch.bfloat16, name + " tcgen05")
         _cmp(r1[i], ref, torch.bfloat16, name + " mma.sync")
+
+
+@pytest.mark.parametrize("L,with_gate", [(2048 - 50, True), (3072, False)])
+def test_tcgen05_forward_d256_qwen_layout(cuda, monkeypatch, L, with_gate):
+    """Block 128 / D 256 (the Qwen configuration) on the tcgen05 kernel: GQA, TOKEN
+    masks with repeated ids, a ragged last block and the sigmoid output gate, against
+    the mma.sync kernel and the oracle."""
+    import _bsa
+    B, Hq, Hkv, D, bs, kk = 1, 4, 2, 256, 128, 7
+    gen = torch.Generator().manual_seed(L)
+    q = torch.randn(B, Hq, L, D, generator=gen).to(torch.bfloat16)
+    k, v = (torch.randn(B, Hkv, L, D, generator=gen).to(torch.bfloat16) for _ in range(2))
+    nblk = (L + bs - 1) // bs
+    sel = torch.randint(0, nblk, (B, Hkv, nblk, kk), generator=gen)
+    sel[..., 0] = torch.arange(nblk)
+    sel[..., 3] = sel[..., 2]
+    og = torch.randn(B, Hq, L, D, generator=gen).to(torch.bfloat16) if with_gate else None
+    args = [t.to(cuda) for t in (q, k, v)] + [sel.to(cuda, torch.int32), None]
+    kw = dict(bs=bs, causal=True, mask_mode=_bsa.MASK_TOKEN,
+              out_gate=og.to(cuda) if og is not None else None)
+    o5, l5 = _bsa.attn_fwd(*args, **kw)
+    monkeypatch.setenv("BSA_FWD_LEGACY", "1")
+    o1, l1 = _bsa.attn_fwd(*args, **kw)
+    ref = O.attention(q, k, v, sel, None, bs=bs, causal=True, mask_mode=1, out_gate=og)
+    _cmp(o5, ref, torch.bfloat16, "o tcgen05")
+    _cmp(o1, ref, torch.bfloat16, "o mma.sync")
+    assert (l5 - l1).abs().max().item() < 1e-4
+
+
+def test_tcgen05_forward_d256_identity_selection(cuda, monkeypatch):
+    """All-blocks mode (sel = NULL: every causal block) on the block-128 / D-256
+    tcgen05 kernel equals the mma.sync kernel and the oracle (dense causal)."""
+    import _bsa
+    B, Hq, Hkv, D, bs, L = 1, 4, 2, 256, 128, 1500
+    gen = torch.Generator().manual_seed(3)
+    q = torch.randn(B, Hq, L, D, generator=gen).to(torch.bfloat16)
+    k, v = (torch.randn(B, Hkv, L, D, generator=gen).to(torch.bfloat16) for _ in range(2))
+    nblk = (L + bs - 1) // bs
+    args = [t.to(cuda) for t in (q, k, v)] + [None, None]
+    o5, _ = _bsa.attn_fwd(*args, bs=bs, causal=True, mask_mode=_bsa.MASK_TOKEN)
+    monkeypatch.setenv("BSA_FWD_LEGACY", "1")
+    o1, _ = _bsa.attn_fwd(*args, bs=bs, causal=True, mask_mode=_bsa.MASK_TOKEN)
+    ident = torch.arange(nblk).view(1, 1, 1, nblk).expand(B, Hkv, nblk, nblk)
+    ref = O.attention(q, k, v, ident, None, bs=bs, causal=True, mask_mode=1)
+    _cmp(o5, ref, torch.bfloat16, "o tcgen05")
+    _cmp(o1, ref, torch.bfloat16, "o mma.sync")
