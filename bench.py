@@ -23,6 +23,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -57,7 +58,7 @@ def workload(a):
 
 
 def flops(cfg, heads):
-    """Algorithmic FLOPs (SURVEY 8d convention): fwd 4*B*H*N*kk*bs*D, bwd 2.5x fwd,
+    """Algorithmic FLOPs (FA2 5-GEMM convention): fwd 4*B*H*N*kk*bs*D, bwd 2.5x fwd,
     selection 2*D per causal block pair plus the two pooling passes (negligible)."""
     fwd = 4.0 * cfg["B"] * heads * cfg["N"] * cfg["kk"] * cfg["bs"] * cfg["D"]
     nb = cfg["nblk"]
@@ -72,10 +73,9 @@ class ClockSampler:
     def __init__(self, index):
         self.index = index
         self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", "clocks_%d.csv" % index)
+        self.path = os.path.join(tempfile.gettempdir(), "bsa_bench_clocks_%d_%d.csv" % (index, os.getpid()))
 
     def __enter__(self):
-        os.makedirs(os.path.dirname(self.path), exist_ok=True)
         q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
