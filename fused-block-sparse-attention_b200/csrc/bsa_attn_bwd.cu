@@ -1007,6 +1007,10 @@ bsa_status fill_attn_params(const bsa_attn_args *a, AttnParams *p, bool bwd);
 bool dkdv_sm100_applicable(int dtype, int bs, int D);
 bool dq_sm100_applicable(const AttnParams &p, int dtype, int D);
 bsa_status launch_dvec(int dtype, const AttnParams &p, int D, cudaStream_t st);
+bool dq_f5_applicable(const AttnParams &p, int dtype, int D);
+bsa_status launch_dq_f5(int dtype, const CUtensorMap &mq, const CUtensorMap &mdo,
+                        const CUtensorMap &mk, const CUtensorMap &mv, int pq, int pdo, int pk,
+                        int pv, const AttnParams &p, cudaStream_t st);
 bsa_status launch_dq_sm100(int dtype, const CUtensorMap &mq, const CUtensorMap &mdo,
                            const CUtensorMap &mk, const CUtensorMap &mv, int pq, int pdo, int pk,
                            int pv, const AttnParams &p, cudaStream_t st);
@@ -1048,7 +1052,12 @@ static bsa_status launch_bwd_tc(const bsa_attn_args *a, const AttnParams &p, con
                      "v")))
     return s;
   auto pk = [](const TensorMap4 &m) { return m.perm[0] | (m.perm[1] << 2) | (m.perm[2] << 4); };
-  if (dq_sm100_applicable(p, a->dtype, D) && a->sel) {
+  if (BS == 64 && D == 64 && dq_f5_applicable(p, a->dtype, D)) {
+    if ((s = launch_dvec(a->dtype, p, D, st))) return s;
+    if ((s = launch_dq_f5(a->dtype, mq.map, mdo.map, mk.map, mv.map, pk(mq), pk(mdo), pk(mk),
+                          pk(mv), p, st)))
+      return s;
+  } else if (dq_sm100_applicable(p, a->dtype, D) && a->sel) {
     if ((s = launch_dvec(a->dtype, p, D, st))) return s;
     if ((s = launch_dq_sm100(a->dtype, mq.map, mdo.map, mkc.map, mvc.map, pk(mq), pk(mdo), pk(mkc),
                              pk(mvc), p, st)))
