@@ -5,7 +5,7 @@
 // the key-block CSR plan, each a key block of one KV head with up to 32 listed
 // (query block, slot) entries.  The key block's K and V stay in shared memory
 // as the stationary A operands; the listed query blocks stream through a
-// 3-stage ring (Q, dO by TMA, lse and Dvec rows by bulk copy).
+// 4-stage ring (Q, dO by TMA, lse and Dvec rows by bulk copy).
 //
 // Per step j (one entry and query head of each tile):
 //   S^T  = K  Q_j^T    dP^T = V dO_j^T         (tcgen05, fp32 in TMEM, 2 buffers)
@@ -17,7 +17,8 @@
 // Warp roles (320 threads, one CTA per SM):
 //   warps 0-7  elementwise: TMEM -> registers, P^T / dS^T (bf16) -> shared
 //              memory in the 128B-swizzled K-major layout, final dK / dV.
-//   warp 8     TMA producer (one thread, polls the ring).
+//   warp 8     TMA producer: the warp reads a unit's CSR entries and gate values
+//              at once, then one thread issues the ring loads.
 //   warp 9     TMEM allocation (512 columns) and the MMA-issuing thread, which
 //              polls two queues: dV/dK of step j as soon as P/dS are written,
 //              S/dP of the next step as soon as its ring stage has landed.
@@ -35,7 +36,7 @@ namespace bsa {
 #ifdef BSA_TRACE
 #define B5_TRACE(ev, j)                                                                  \
   do {                                                                                   \
-    if (b5_tr && (j) < 128) p.trace[(ev) * 128 + (j)] = clock64();                  \
+    if (b5_tr && (j) < 127) p.trace[(ev) * 128 + (j)] = clock64();                  \
   } while (0)
 #else
 #define B5_TRACE(ev, j) \
@@ -44,13 +45,16 @@ namespace bsa {
 #endif
 
 namespace {
-constexpr int B5_BS = 64, B5_D = 64, B5_NST = 3;
+constexpr int B5_BS = 64, B5_D = 64;
 constexpr int B5_TILE = B5_BS * B5_D * 2;            // 8 KB
 constexpr int B5_ROWB = B5_BS * 4;                   // one lse / Dvec row chunk
-constexpr int B5_SMEM = 1024 + 4 * B5_TILE           // K, V of both tiles
-                        + B5_NST * 4 * B5_TILE       // ring: (stage, tile) Q, dO
-                        + 8 * B5_TILE                // P^T, dS^T of both tiles, 2 buffers
-                        + B5_NST * 2 * 2 * B5_ROWB;  // ring: (stage, tile) lse, Dvec
+// NKV K/V buffers, NST ring stages, NPD P^T/dS^T buffers
+constexpr int b5_smem(int NST, int NPD, int NKV) {
+  return 1024 + NKV * 4 * B5_TILE    // K, V of both tiles
+         + NST * 4 * B5_TILE         // ring: (stage, tile) Q, dO
+         + NPD * 4 * B5_TILE         // P^T, dS^T of both tiles
+         + NST * 2 * 2 * B5_ROWB;    // ring: (stage, tile) lse, Dvec
+}
 constexpr uint32_t B5_TMEM_COLS = 512;
 constexpr int B5_SCOL = 0, B5_DPCOL = 128, B5_DVCOL = 256, B5_DKCOL = 320;  // +128: 2nd acc buffer
 }  // namespace
@@ -87,7 +91,7 @@ __device__ __forceinline__ void b5_unit(const BwdPlan &pl, const AttnParams &p, 
   }
 }
 
-template <typename T>
+template <typename T, int B5_NST, int NPD, int NKV>
 __global__ void __launch_bounds__(320, 1)
     attn_dkdv_sm100_kernel(const __grid_constant__ CUtensorMap tq,
                            const __grid_constant__ CUtensorMap tdo,
@@ -101,16 +105,16 @@ __global__ void __launch_bounds__(320, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~uintptr_t(1023));
-  uint8_t *sKV = smem;                       // tile t: K, V
-  uint8_t *sR = sKV + 4 * B5_TILE;           // (stage, tile): Q, dO
+  uint8_t *sKV = smem;                       // (buffer, tile): K, V
+  uint8_t *sR = sKV + NKV * 4 * B5_TILE;     // (stage, tile): Q, dO
   uint8_t *sPD = sR + B5_NST * 4 * B5_TILE;  // (buffer, tile): P^T, dS^T
-  float *sRow = reinterpret_cast<float *>(sPD + 8 * B5_TILE);  // (stage, tile): lse[64], Dvec[64]
+  float *sRow = reinterpret_cast<float *>(sPD + NPD * 4 * B5_TILE);  // (stage, tile): lse[64], Dvec[64]
   // p_full[b] / g_done[b]: P/dS of a step with parity b written / consumed by
   // its dV/dK MMAs.  One barrier per buffer: with two buffers the elementwise
   // warps may run one step ahead of the MMA issuer, and a single barrier would
   // then be two phases ahead of its waiter (ambiguous parity).
-  __shared__ __align__(8) uint64_t kv_full, kv_empty, r_full[B5_NST], r_empty[B5_NST],
-      s_full[2], s_empty[2], p_full[2], g_done[2], acc_empty[2];
+  __shared__ __align__(8) uint64_t kv_full[NKV], kv_empty[NKV], r_full[B5_NST], r_empty[B5_NST],
+      s_full[2], s_empty[2], p_full[NPD], g_done[NPD], acc_empty[2];
   __shared__ uint32_t tmem_base_sh;
   // per ring stage and tile: (local query block, slot, query head) and the gate
   // value of the step, written by the producer before it arrives on r_full
@@ -125,12 +129,16 @@ __global__ void __launch_bounds__(320, 1)
   const int nunits = (int)((total + 1) / 2) * pl.Y;
 
   if (tid == 0) {
-    mbar_init(&kv_full, 1);
-    mbar_init(&kv_empty, 1);
+    for (int s = 0; s < NKV; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
       mbar_init(&s_empty[s], 256);
       mbar_init(&acc_empty[s], 256);
+    }
+    for (int s = 0; s < NPD; ++s) {
       mbar_init(&g_done[s], 1);
       mbar_init(&p_full[s], 256);
     }
@@ -149,39 +157,60 @@ __global__ void __launch_bounds__(320, 1)
   tc05::fence_after();
   const uint32_t tmem = tmem_base_sh;
 
-  auto item = [&](const B5Unit &w, int t, int j, int &qblk, int &slot, int &h) {
-    int ci = w.ebeg[t] + j / p.grp;
-    if (ci < 0 || ci >= pl.ncol) {  // self-check: never read outside the CSR list
-      report(p.status, BSA_DEVERR_INDEX);
-      ci = 0;
-    }
-    const int e = pl.col[ci];
-    qblk = e / p.kk;
-    slot = e - qblk * p.kk;
-    h = w.hk[t] * p.grp + (j % p.grp);
-  };
-
   if (warp == 8) {
-    // ================= producer: K/V per unit (2 buffers), Q/dO/lse/Dvec per step (ring)
-    if (lane == 0) {
-      int gs = 0, ne = 0;
-      uint32_t idle = 0;
-      for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
-        B5Unit w;
-        b5_unit(pl, p, total, u, w);
-        const int ns = max(w.n[0], w.n[1]);
-        if (ns == 0) continue;
-        // single K/V buffer: the previous unit's last S/dP MMAs must be done
-        if (ne >= 1 && !mbar_wait(&kv_empty, (ne - 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
-        mbar_expect_tx(&kv_full, ((w.n[0] > 0) + (w.n[1] > 0)) * 2 * B5_TILE);
-        for (int t = 0; t < 2; ++t) {
-          if (w.n[t] == 0) continue;
-          uint8_t *dst = sKV + t * 2 * B5_TILE;
-          tma_load_rhb(dst, &tk, &kv_full, perm_k, 0, w.kb[t] * p.bs, w.hk[t], w.b[t]);
-          tma_load_rhb(dst + B5_TILE, &tv, &kv_full, perm_v, 0, w.kb[t] * p.bs, w.hk[t], w.b[t]);
+    // ================= producer: K/V per unit (2 buffers), Q/dO/lse/Dvec per step (ring).
+    // The whole warp reads a unit's CSR entries (<= 32 per tile) and gate values
+    // at once; lane 0 then issues the loads step by step from shared memory.
+    __shared__ int s_pq[2][32], s_ps[2][32];
+    __shared__ float s_pg[2][32];
+    int gs = 0, ne = 0;
+    uint32_t idle = 0;
+    for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
+      B5Unit w;
+      b5_unit(pl, p, total, u, w);
+      const int ns = max(w.n[0], w.n[1]);
+      if (ns == 0) continue;
+      if (w.b[0] < 0 || w.b[0] >= p.B || w.b[1] < 0 || w.b[1] >= p.B) {
+        report(p.status, BSA_DEVERR_INDEX);  // self-check: keep every address in range
+        w.b[0] = w.b[1] = 0;
+      }
+      __syncwarp();  // lane 0 is done with the previous unit's entries
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        if (lane < w.n[t] / p.grp) {
+          int ci = w.ebeg[t] + lane;
+          if (ci < 0 || ci >= pl.ncol) {  // self-check: never read outside the CSR list
+            report(p.status, BSA_DEVERR_INDEX);
+            ci = 0;
+          }
+          const int e = pl.col[ci];
+          int qblk = e / p.kk, slot = e - (e / p.kk) * p.kk;
+          if (qblk < 0 || qblk >= p.nq) {
+            report(p.status, BSA_DEVERR_INDEX);
+            qblk = slot = 0;
+          }
+          s_pq[t][lane] = qblk;
+          s_ps[t][lane] = slot;
+          s_pg[t][lane] = p.gate ? __ldg(p.gate + w.b[t] * p.gate_sb + w.hk[t] * p.gate_sh +
+                                         (long long)qblk * p.gate_sn + slot) * kLog2e
+                                 : 0.f;
         }
-        ++ne;
-        for (int j = 0; j < ns; ++j, ++gs) {
+      }
+      __syncwarp();
+      if (lane != 0) continue;
+      // single K/V buffer: the previous unit's last S/dP MMAs must be done
+      const int kvb = ne % NKV;
+      if (ne >= NKV && !mbar_wait(&kv_empty[kvb], ((ne / NKV) - 1) & 1))
+        report(p.status, BSA_DEVERR_TIMEOUT);
+      mbar_expect_tx(&kv_full[kvb], ((w.n[0] > 0) + (w.n[1] > 0)) * 2 * B5_TILE);
+      for (int t = 0; t < 2; ++t) {
+        if (w.n[t] == 0) continue;
+        uint8_t *dst = sKV + (kvb * 2 + t) * 2 * B5_TILE;
+        tma_load_rhb(dst, &tk, &kv_full[kvb], perm_k, 0, w.kb[t] * p.bs, w.hk[t], w.b[t]);
+        tma_load_rhb(dst + B5_TILE, &tv, &kv_full[kvb], perm_v, 0, w.kb[t] * p.bs, w.hk[t], w.b[t]);
+      }
+      ++ne;
+      for (int j = 0; j < ns; ++j, ++gs) {
           const int st = gs % B5_NST;
           while (gs >= B5_NST && !mbar_test(&r_empty[st], ((gs / B5_NST) - 1) & 1)) {
             if (++idle > kSpinLimit) {
@@ -196,22 +225,14 @@ __global__ void __launch_bounds__(320, 1)
           int mq[2], mh[2];
           for (int t = 0; t < 2; ++t) {
             if (j >= w.n[t]) continue;
-            int qblk, slot, h;
-            item(w, t, j, qblk, slot, h);
-            if (qblk < 0 || qblk >= p.nq || h < 0 || h >= p.Hq || w.b[t] < 0 || w.b[t] >= p.B) {
-              report(p.status, BSA_DEVERR_INDEX);  // self-check: keep every address in range
-              qblk = 0;
-              h = 0;
-              w.b[t] = 0;
-            }
+            const int en = j / p.grp;
+            const int qblk = s_pq[t][en], h = w.hk[t] * p.grp + (j - en * p.grp);
             mq[t] = qblk;
             mh[t] = h;
             s_meta[st][t][0] = qblk;
-            s_meta[st][t][1] = slot;
+            s_meta[st][t][1] = s_ps[t][en];
             s_meta[st][t][2] = h;
-            s_g2[st][t] = p.gate ? __ldg(p.gate + w.b[t] * p.gate_sb + w.hk[t] * p.gate_sh +
-                                         (long long)qblk * p.gate_sn + slot) * kLog2e
-                                 : 0.f;
+            s_g2[st][t] = s_pg[t][en];
           }
           // the arrive below releases the metadata stores to the r_full waiters
           mbar_expect_tx(&r_full[st], act * (2 * B5_TILE + 2 * B5_ROWB));
@@ -228,7 +249,6 @@ __global__ void __launch_bounds__(320, 1)
             bulk_load(rw + B5_BS, p.dvec + rb, B5_ROWB, &r_full[st]);
           }
         }
-      }
     }
   } else if (warp == 9) {
     // ================= MMA issuer: S/dP queue and dV/dK queue, polled
@@ -257,7 +277,7 @@ __global__ void __launch_bounds__(320, 1)
       while (have_g) {
         bool progress = false;
         // ---- dV += P^T dO, dK += dS^T Q for step (ug, jg)
-        if (gsg < gss && mbar_test(&p_full[gsg & 1], (gsg >> 1) & 1) &&
+        if (gsg < gss && mbar_test(&p_full[gsg % NPD], (gsg / NPD) & 1) &&
             (jg > 0 || neg < 2 || mbar_test(&acc_empty[neg & 1], ((neg >> 1) - 1) & 1))) {
           const int st = gsg % B5_NST, ab = neg & 1;
           B5_TRACE(2, gsg);
@@ -266,7 +286,7 @@ __global__ void __launch_bounds__(320, 1)
             if (jg >= wg.n[t]) continue;
             const uint32_t q_addr = smem_u32(sR + (st * 2 + t) * 2 * B5_TILE);
             const uint32_t do_addr = q_addr + B5_TILE;
-            const uint32_t p_addr = smem_u32(sPD + ((gsg & 1) * 2 + t) * 2 * B5_TILE);
+            const uint32_t p_addr = smem_u32(sPD + ((gsg % NPD) * 2 + t) * 2 * B5_TILE);
             const uint32_t ds_addr = p_addr + B5_TILE;
             const uint32_t dv = tc05::taddr(tmem, 16 * t, B5_DVCOL + 128 * ab);
             const uint32_t dk = tc05::taddr(tmem, 16 * t, B5_DKCOL + 128 * ab);
@@ -280,7 +300,7 @@ __global__ void __launch_bounds__(320, 1)
             }
           }
           tc05::commit(&r_empty[st]);
-          tc05::commit(&g_done[gsg & 1]);
+          tc05::commit(&g_done[gsg % NPD]);
           ++gsg;
           if (++jg == max(wg.n[0], wg.n[1])) {
             jg = 0;
@@ -292,7 +312,7 @@ __global__ void __launch_bounds__(320, 1)
         // ---- S^T = K Q^T, dP^T = V dO^T for step (us, js)
         if (have_s && mbar_test(&r_full[gss % B5_NST], (gss / B5_NST) & 1) &&
             (gss < 2 || mbar_test(&s_empty[gss & 1], ((gss >> 1) - 1) & 1)) &&
-            (js > 0 || mbar_test(&kv_full, nes & 1))) {
+            (js > 0 || mbar_test(&kv_full[nes % NKV], (nes / NKV) & 1))) {
           const int st = gss % B5_NST, bb = gss & 1;
           B5_TRACE(1, gss);
           tc05::fence_after();
@@ -300,7 +320,7 @@ __global__ void __launch_bounds__(320, 1)
             if (js >= ws.n[t]) continue;
             const uint32_t q_addr = smem_u32(sR + (st * 2 + t) * 2 * B5_TILE);
             const uint32_t do_addr = q_addr + B5_TILE;
-            const uint32_t k_addr = smem_u32(sKV + t * 2 * B5_TILE);
+            const uint32_t k_addr = smem_u32(sKV + ((nes % NKV) * 2 + t) * 2 * B5_TILE);
             const uint32_t v_addr = k_addr + B5_TILE;
             const uint32_t ds = tc05::taddr(tmem, 16 * t, B5_SCOL + 64 * bb);
             const uint32_t ddp = tc05::taddr(tmem, 16 * t, B5_DPCOL + 64 * bb);
@@ -315,7 +335,7 @@ __global__ void __launch_bounds__(320, 1)
           tc05::commit(&s_full[bb]);
           ++gss;
           if (++js == max(ws.n[0], ws.n[1])) {
-            tc05::commit(&kv_empty);  // last reader of this unit's K/V
+            tc05::commit(&kv_empty[nes % NKV]);  // last reader of this unit's K/V
             js = 0;
             us += gridDim.x;
             have_s = next_unit(us, ws, nes);
@@ -357,6 +377,7 @@ __global__ void __launch_bounds__(320, 1)
         tc05::ld32(tmem + lane_base + B5_SCOL + 64 * bb + 32 * hf, sv);
         tc05::ld32(tmem + lane_base + B5_DPCOL + 64 * bb + 32 * hf, dp);
         tc05::wait_ld();
+        if (tid == 0) B5_TRACE(6, gs);
         tc05::fence_before();
         tc05::mbar_arrive(&s_empty[bb]);
         uint32_t wp[16], wd[16];
@@ -389,12 +410,14 @@ __global__ void __launch_bounds__(320, 1)
             wd[(c >> 1) + 1] = Mma<T>::pack(p2 * (dp[c + 2] - d4.z), p3 * (dp[c + 3] - d4.w));
           }
         }
-        if (gs >= 2) {  // dV/dK of step gs-2 read P / dS buffer gs & 1
-          if (!mbar_wait(&g_done[gs & 1], ((gs >> 1) - 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
+        if (tid == 0) B5_TRACE(5, gs);
+        if (gs >= NPD) {  // dV/dK of step gs-NPD read P / dS buffer gs % NPD
+          if (!mbar_wait(&g_done[gs % NPD], ((gs / NPD) - 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
           tc05::fence_after();
         }
+        if (tid == 0) B5_TRACE(7, gs);
         if (active) {
-          const uint32_t pa = smem_u32(sPD + ((gs & 1) * 2 + t) * 2 * B5_TILE);
+          const uint32_t pa = smem_u32(sPD + ((gs % NPD) * 2 + t) * 2 * B5_TILE);
 #pragma unroll
           for (int c8 = 0; c8 < 4; ++c8) {
             const int col = 32 * hf + 8 * c8;
@@ -408,14 +431,14 @@ __global__ void __launch_bounds__(320, 1)
         }
         fence_proxy_async_smem();
         tc05::fence_before();
-        if (lane == 0 && (warp == 0 || warp == 7)) B5_TRACE(warp == 0 ? 4 : 5, gs);
-        tc05::mbar_arrive(&p_full[gs & 1]);
+        if (tid == 0) B5_TRACE(4, gs);
+        tc05::mbar_arrive(&p_full[gs % NPD]);
       }
       // ---- dK (scaled) and dV of this unit: this thread's row, columns [32*hf, +32)
       float dkv[32], dvv[32];
       if (ns > 0) {
         const int gl = gs - 1;  // last step of this unit
-        if (!mbar_wait(&g_done[gl & 1], (gl >> 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
+        if (!mbar_wait(&g_done[gl % NPD], (gl / NPD) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
         tc05::fence_after();
         const int ab = ne & 1;
         tc05::ld32(tmem + lane_base + B5_DKCOL + 128 * ab + 32 * hf, dkv);
@@ -495,15 +518,28 @@ bsa_status launch_dkdv_sm100(int dtype, const CUtensorMap &mq, const CUtensorMap
   if (const char *tp = getenv("BSA_TRACE_PTR")) pt.trace = (unsigned long long *)strtoull(tp, nullptr, 0);
 #define p pt
 #endif
-  if (dtype == BSA_BF16) {
-    auto kern = attn_dkdv_sm100_kernel<__nv_bfloat16>;
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, B5_SMEM);
-    kern<<<grid, 320, B5_SMEM, st>>>(mq, mdo, mk, mv, pq, pdo, pk, pv, p, pl);
-  } else {
-    auto kern = attn_dkdv_sm100_kernel<__half>;
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, B5_SMEM);
-    kern<<<grid, 320, B5_SMEM, st>>>(mq, mdo, mk, mv, pq, pdo, pk, pv, p, pl);
+  // ring stages / P-dS buffers: 4/1 by default (the deeper ring hides more of
+  // the Q/dO load latency than a second P/dS buffer saves); BSA_DKDV_CFG=32 for 3/2
+  const char *cfg = getenv("BSA_DKDV_CFG");
+  const int variant = cfg ? atoi(cfg) : 41;
+#define BSA_B5_LAUNCH(T_, N_, P_, KV_)                                                      \
+  {                                                                                         \
+    auto kern = attn_dkdv_sm100_kernel<T_, N_, P_, KV_>;                                    \
+    constexpr int sm = b5_smem(N_, P_, KV_);                                                \
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);            \
+    kern<<<grid, 320, sm, st>>>(mq, mdo, mk, mv, pq, pdo, pk, pv, p, pl);                   \
   }
+#define BSA_B5_PICK(T_)                                      \
+  if (variant == 32) BSA_B5_LAUNCH(T_, 3, 2, 1)              \
+  else if (variant == 312) BSA_B5_LAUNCH(T_, 3, 1, 2)        \
+  else BSA_B5_LAUNCH(T_, 4, 1, 1)
+  if (dtype == BSA_BF16) {
+    BSA_B5_PICK(__nv_bfloat16)
+  } else {
+    BSA_B5_PICK(__half)
+  }
+#undef BSA_B5_PICK
+#undef BSA_B5_LAUNCH
 #ifdef BSA_TRACE
 #undef p
 #endif
