@@ -20,9 +20,11 @@
 //              when the block raises it by more than 2^8 (lazy rescaling; O is
 //              rescaled in TMEM); P is written 128B-swizzled K-major in two
 //              64-key regions; final O / l.
-//   warp 8     TMA producer (one thread): Q once, then the K and V chunks of
-//              every step into two rings of 64-column slots (a K slot is freed
-//              by the S MMAs that read it, a V slot by the PV MMAs).
+//   warp 8     TMA producer (one thread): Q once, then the K and V chunks into
+//              ONE ring of 64-column slots, in the order the MMAs consume them
+//              (K of step 0; then K of step j + 1 and V of step j for each j),
+//              so a slot is freed by whichever MMAs read it (S for K, PV for V)
+//              and both kinds share the buffering.
 //   warp 9     TMEM owner and MMA-issuing thread: S_{j+1} as soon as all
 //              softmax warps have read S_j, PV_j as soon as P_j is complete.
 // Every mbarrier wait is bounded; a timeout sets BSA_DEVERR_TIMEOUT.
@@ -43,8 +45,9 @@ constexpr float G8_RESCALE = 8.f;  // log2 units
 template <int D>
 struct G8 {
   static constexpr int NCH = D / 64;                 // 64-column chunks per row
-  static constexpr int NSL = D == 64 ? 2 : 3;        // ring slots (K and V each)
-  static constexpr int SMEM = 1024 + NCH * G8_TILE + 2 * NSL * G8_TILE + 2 * G8_TILE;
+  // ring slots shared by K and V chunks (D = 64: 3 x 16 KB keeps two CTAs per SM)
+  static constexpr int NSL = D == 64 ? 3 : 6;
+  static constexpr int SMEM = 1024 + NCH * G8_TILE + NSL * G8_TILE + 2 * G8_TILE;
   static constexpr uint32_t TMEM_COLS = D == 64 ? 256 : 512;
   static constexpr int MINB = D == 64 ? 2 : 1;       // CTAs per SM
   // live slots kept in shared memory (D = 256 also runs the identity selection,
@@ -67,11 +70,10 @@ __global__ void __launch_bounds__(G8_THREADS, G8<D>::MINB)
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                               ~uintptr_t(1023));
   uint8_t *sQ = smem;                       // Q chunk c at sQ + c * TILE
-  uint8_t *sK = sQ + NCH * G8_TILE;         // K ring: NSL chunk slots
-  uint8_t *sV = sK + NSL * G8_TILE;         // V ring: NSL chunk slots
-  uint8_t *sP = sV + NSL * G8_TILE;         // P: keys 0-63 at sP, 64-127 at sP + TILE
-  __shared__ __align__(8) uint64_t bar_q, k_full[NSL], k_empty[NSL], v_full[NSL], v_empty[NSL],
-      s_full, s_empty, p_full, o_done;
+  uint8_t *sR = sQ + NCH * G8_TILE;         // K/V ring: NSL chunk slots
+  uint8_t *sP = sR + NSL * G8_TILE;         // P: keys 0-63 at sP, 64-127 at sP + TILE
+  __shared__ __align__(8) uint64_t bar_q, r_full[NSL], r_empty[NSL], s_full, s_empty, p_full,
+      o_done;
   __shared__ uint32_t tmem_base_sh;
   constexpr int MAXN = G8<D>::MAXN;
   __shared__ int s_item[MAXN];   // (kb << 3) | kind of the j-th live slot
@@ -121,10 +123,8 @@ __global__ void __launch_bounds__(G8_THREADS, G8<D>::MINB)
     s_n = n;
     mbar_init(&bar_q, 1);
     for (int s = 0; s < NSL; ++s) {
-      mbar_init(&k_full[s], 1);
-      mbar_init(&k_empty[s], 1);
-      mbar_init(&v_full[s], 1);
-      mbar_init(&v_empty[s], 1);
+      mbar_init(&r_full[s], 1);
+      mbar_init(&r_empty[s], 1);
     }
     mbar_init(&s_full, 1);
     mbar_init(&s_empty, 8);  // one arrive per softmax warp
@@ -142,23 +142,23 @@ __global__ void __launch_bounds__(G8_THREADS, G8<D>::MINB)
   const uint32_t tmem = tmem_base_sh;
   const int nsteps = s_n;
 
-  // Chunk sequence of each ring: step j's chunks c = 0 .. NCH-1, in step order;
-  // chunk number n = j * NCH + c uses slot n % NSL.  The producer issues the K
-  // chunks of step j + 1 before the V chunks of step j.
+  // Ring sequence: K chunks of step 0, then per step j the K chunks of step
+  // j + 1 (if any) and the V chunks of step j; item number n uses slot n % NSL.
+  // Producer and MMA issuer walk the same sequence with their own counters.
   if (warp == G8_WPROD) {
     // ================= TMA producer
     if (lane == 0) {
       mbar_expect_tx(&bar_q, NCH * G8_TILE);
       for (int c = 0; c < NCH; ++c)
         tma_load_rhb(sQ + c * G8_TILE, &tq, &bar_q, perm_q, 64 * c, qi * p.bs, h, b);
+      int n = 0;
       auto load = [&](bool isv, int j) {
-        for (int c = 0; c < NCH; ++c) {
-          const int n = j * NCH + c, sl = n % NSL;
-          uint64_t *full = isv ? &v_full[sl] : &k_full[sl];
-          uint64_t *empty = isv ? &v_empty[sl] : &k_empty[sl];
-          if (n >= NSL && !mbar_wait(empty, ((n / NSL) - 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
-          mbar_expect_tx(full, G8_TILE);
-          tma_load_rhb((isv ? sV : sK) + sl * G8_TILE, isv ? &tv : &tk, full, isv ? perm_v : perm_k,
+        for (int c = 0; c < NCH; ++c, ++n) {
+          const int sl = n % NSL;
+          if (n >= NSL && !mbar_wait(&r_empty[sl], ((n / NSL) - 1) & 1))
+            report(p.status, BSA_DEVERR_TIMEOUT);
+          mbar_expect_tx(&r_full[sl], G8_TILE);
+          tma_load_rhb(sR + sl * G8_TILE, isv ? &tv : &tk, &r_full[sl], isv ? perm_v : perm_k,
                        64 * c, (s_item[j] >> 3) * p.bs, hk, b);
         }
       };
@@ -173,19 +173,20 @@ __global__ void __launch_bounds__(G8_THREADS, G8<D>::MINB)
     if (lane == 0) {
       if (!mbar_wait(&bar_q, 0)) report(p.status, BSA_DEVERR_TIMEOUT);
       const uint64_t dq = tc05::sdesc(smem_u32(sQ), 16, 1024);
+      int n = 0;
       auto issue_s = [&](int js) {
         if (js >= 1 && !mbar_wait(&s_empty, (js - 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
-        for (int c = 0; c < NCH; ++c) {
-          const int n = js * NCH + c, sl = n % NSL;
-          if (!mbar_wait(&k_full[sl], (n / NSL) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
+        for (int c = 0; c < NCH; ++c, ++n) {
+          const int sl = n % NSL;
+          if (!mbar_wait(&r_full[sl], (n / NSL) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
           tc05::fence_after();
-          const uint64_t dk = tc05::sdesc(smem_u32(sK + sl * G8_TILE), 16, 1024);
+          const uint64_t dk = tc05::sdesc(smem_u32(sR + sl * G8_TILE), 16, 1024);
           const uint64_t dqc = dq + c * (G8_TILE >> 4);
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks)
             tc05::mma_f16(tc05::taddr(tmem, 0, G8_SCOL), dqc + 2 * ks, dk + 2 * ks, IDESC_S,
                           (c > 0 || ks > 0) ? 1u : 0u);
-          tc05::commit(&k_empty[sl]);
+          tc05::commit(&r_empty[sl]);
         }
         tc05::commit(&s_full);
       };
@@ -194,17 +195,17 @@ __global__ void __launch_bounds__(G8_THREADS, G8<D>::MINB)
         if (jp + 1 < nsteps) issue_s(jp + 1);
         if (!mbar_wait(&p_full, jp & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
         const uint64_t dp = tc05::sdesc(smem_u32(sP), 16, 1024);
-        for (int c = 0; c < NCH; ++c) {
-          const int n = jp * NCH + c, sl = n % NSL;
-          if (!mbar_wait(&v_full[sl], (n / NSL) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
+        for (int c = 0; c < NCH; ++c, ++n) {
+          const int sl = n % NSL;
+          if (!mbar_wait(&r_full[sl], (n / NSL) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
           tc05::fence_after();
-          const uint64_t dv = tc05::sdesc(smem_u32(sV + sl * G8_TILE), G8_TILE, 1024);
+          const uint64_t dv = tc05::sdesc(smem_u32(sR + sl * G8_TILE), G8_TILE, 1024);
 #pragma unroll
           for (int ks = 0; ks < G8_BS / 16; ++ks)  // keys 16*ks: P region ks/4, +32 B per 16 keys
             tc05::mma_f16(tc05::taddr(tmem, 0, G8_OCOL + 64 * c),
                           dp + (ks >> 2) * (G8_TILE >> 4) + 2 * (ks & 3), dv + 128 * ks, IDESC_PV,
                           (jp > 0 || ks > 0) ? 1u : 0u);
-          tc05::commit(&v_empty[sl]);
+          tc05::commit(&r_empty[sl]);
         }
         tc05::commit(&o_done);
       }
