@@ -16,10 +16,11 @@
 //   warps 0-7  softmax: warp w reads rows 32*(w&3).. and key columns
 //              64*(w>>2)..+63; the two warps of a row quarter exchange their
 //              half-row maxima through shared memory (named barrier 1 + (w&3));
-//              exponentials use the maximum in use and are redone (rarely)
-//              when the block raises it by more than 2^8 (lazy rescaling; O is
-//              rescaled in TMEM); P is written 128B-swizzled K-major in two
-//              64-key regions; final O / l.
+//              the maximum in use is raised only when the block exceeds it by
+//              more than 2^8 (lazy rescaling; O is then rescaled in TMEM); the
+//              exponentials go to registers while PV_{j-1} may still run, and P
+//              is written 128B-swizzled K-major in two 64-key regions once
+//              PV_{j-1} has released the buffer; final O / l.
 //   warp 8     TMA producer (one thread): Q once, then the K and V chunks into
 //              ONE ring of 64-column slots, in the order the MMAs consume them
 //              (K of step 0; then K of step j + 1 and V of step j for each j),
@@ -79,7 +80,7 @@ __global__ void __launch_bounds__(G8_THREADS, G8<D>::MINB)
   __shared__ int s_item[MAXN];   // (kb << 3) | kind of the j-th live slot
   __shared__ int s_islot[MAXN];
   __shared__ int s_n;
-  __shared__ float s_xch[2][4][2][32];  // half-row maxima (by step parity), then sums
+  __shared__ float s_xch[3][4][2][32];  // half-row maxima (by step parity), row sums
 
   long long id = blockIdx.x;
   const int gi = (int)(id % p.grp);
@@ -240,38 +241,15 @@ __global__ void __launch_bounds__(G8_THREADS, G8<D>::MINB)
           if (((kind & KIND_TRIU) && cb + c > r) || ((kind & KIND_PAD) && kb * p.bs + cb + c >= p.L))
             s[c] = -INFINITY;
       }
-      // PV_{j-1} must be complete before P is overwritten (and before O is rescaled)
-      if (j >= 1) {
-        if (!mbar_wait(&o_done, (j - 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
-        tc05::fence_after();
-      }
-      // exponentials with the maximum in use, written to P 8 columns at a time,
-      // the block maximum formed alongside
-      float sum8[8], m8[8];
+      // block row maximum (both halves of the row, through shared memory), then
+      // the exponentials into registers while PV_{j-1} may still be running
+      float m8[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) sum8[i] = 0.f, m8[i] = -INFINITY;
-      auto write_p = [&](float off, bool track) {
+      for (int i = 0; i < 8; ++i) m8[i] = fmaxf(s[i], s[i + 8]);
 #pragma unroll
-        for (int c8 = 0; c8 < 8; ++c8) {
-          uint32_t w4[4];
+      for (int c = 16; c < 64; c += 8)
 #pragma unroll
-          for (int e = 0; e < 8; e += 2) {
-            const int c = c8 * 8 + e;
-            const float p0 = ex2(fmaf(s[c], p.scale2, off)), p1 = ex2(fmaf(s[c + 1], p.scale2, off));
-            if (track) {
-              m8[e] = fmaxf(m8[e], s[c]);
-              m8[e + 1] = fmaxf(m8[e + 1], s[c + 1]);
-            }
-            sum8[e] += p0;
-            sum8[e + 1] += p1;
-            w4[e >> 1] = Mma<T>::pack(p0, p1);
-          }
-          asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(swz(pbase, 128, r, c8 * 8)),
-                       "r"(w4[0]), "r"(w4[1]), "r"(w4[2]), "r"(w4[3])
-                       : "memory");
-        }
-      };
-      write_p(g2 - (m_used == -INFINITY ? 0.f : m_used), true);
+        for (int i = 0; i < 8; ++i) m8[i] = fmaxf(m8[i], s[c + i]);
       const float mh = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
                              fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
       s_xch[j & 1][quad][hf][lane] = mh;
@@ -281,16 +259,29 @@ __global__ void __launch_bounds__(G8_THREADS, G8<D>::MINB)
       bool need = false;
       float alpha = 1.f;
       if (mx > -INFINITY && (m_used == -INFINITY || mx > m_used + G8_RESCALE)) {
-        // rare: the block raised the maximum past the slack; redo P with it
         alpha = m_used == -INFINITY ? 0.f : ex2(m_used - mx);
         m_used = mx;
         l *= alpha;
         need = true;
+      }
+      const float off = g2 - (m_used == -INFINITY ? 0.f : m_used);
+      uint32_t w[32];
+      float sum8[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) sum8[i] = 0.f;
-        write_p(g2 - m_used, false);
+      for (int i = 0; i < 8; ++i) sum8[i] = 0.f;
+#pragma unroll
+      for (int c = 0; c < 64; c += 2) {
+        const float p0 = ex2(fmaf(s[c], p.scale2, off)), p1 = ex2(fmaf(s[c + 1], p.scale2, off));
+        sum8[c & 7] += p0;
+        sum8[(c & 7) + 1] += p1;
+        w[c >> 1] = Mma<T>::pack(p0, p1);
       }
       l += ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
+      // PV_{j-1} must be complete before P is overwritten (and before O is rescaled)
+      if (j >= 1) {
+        if (!mbar_wait(&o_done, (j - 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
+        tc05::fence_after();
+      }
       if (__any_sync(0xffffffffu, need) && j >= 1) {
         // O columns [hf * D/2, +D/2) of this warp's rows, 32 at a time
 #pragma unroll 1
@@ -305,15 +296,20 @@ __global__ void __launch_bounds__(G8_THREADS, G8<D>::MINB)
         }
         tc05::wait_st();
       }
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8)
+        asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(swz(pbase, 128, r, c8 * 8)),
+                     "r"(w[4 * c8]), "r"(w[4 * c8 + 1]), "r"(w[4 * c8 + 2]), "r"(w[4 * c8 + 3])
+                     : "memory");
       fence_proxy_async_smem();
       tc05::fence_before();
       __syncwarp();
       if (lane == 0) tc05::mbar_arrive(&p_full);
     }
     // ---- epilogue: O / l, l summed over the two halves of the row
-    s_xch[0][quad][hf][lane] = l;
+    s_xch[2][quad][hf][lane] = l;
     named_bar_sync(1 + quad, 64);
-    const float lt = l + s_xch[0][quad][hf ^ 1][lane];
+    const float lt = l + s_xch[2][quad][hf ^ 1][lane];
     if (nsteps > 0) {
       if (!mbar_wait(&o_done, (nsteps - 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
       tc05::fence_after();
