@@ -44,6 +44,7 @@ struct BwdPlan {
   const int32_t *col;      // entries qblk*kk + slot
   const unsigned long long *plan;  // nbins + 1: (chunk_off << 32) | part_off (exclusive)
   const int32_t *chunk_bin;        // chunk -> bin
+  const int32_t *chunk_ord;        // processing order of the chunks (largest first); may be null
   float *part;             // partial dK/dV tiles
   long long npart;         // capacity of part, in tiles (per KV head of a bin group)
   int ncol;                // capacity of col

@@ -146,6 +146,25 @@ __global__ void chunk_bin_kernel(const unsigned long long *plan, int nbins, int3
   }
 }
 
+// Sort keys of the chunks for the tcgen05 dK/dV kernel: C - entries (largest
+// first), slots past the chunk count last.  Pairing chunks of equal size keeps
+// both tiles of a work unit busy on every step.
+__global__ void chunk_key_kernel(const unsigned long long *plan, const int32_t *row_ptr,
+                                 const int32_t *chunk_bin, int nbins, int C, int ncap,
+                                 int32_t *key, int32_t *val) {
+  const unsigned total = (unsigned)(plan[nbins] >> 32);
+  for (int x = blockIdx.x * blockDim.x + threadIdx.x; x < ncap; x += gridDim.x * blockDim.x) {
+    int k = C + 1;
+    if ((unsigned)x < total) {
+      const int bin = chunk_bin[x];
+      const int cidx = x - (int)(plan[bin] >> 32);
+      const int e0 = row_ptr[bin] + cidx * C;
+      k = C - (min(row_ptr[bin + 1], e0 + C) - e0);
+    }
+    key[x] = k;
+    val[x] = x;
+  }
+}
 
 // ------------------------------------------------------------------ dQ (tensor cores)
 template <int BS, int D>
@@ -933,6 +952,9 @@ struct BwdWs {
   int32_t *row_ptr, *col;
   unsigned long long *plan_in, *plan;
   int32_t *chunk_bin;
+  int32_t *ord_key_in, *ord_key_out, *ord_in, *ord;
+  void *sort_tmp;
+  size_t sort_bytes;
   void *csr_ws;
   size_t csr_bytes;
   void *scan_tmp;
@@ -988,7 +1010,17 @@ static size_t bwd_layout(const bsa_attn_args *a, BwdWs *w, uint8_t *base) {
   w->col = (int32_t *)take(E * 4);
   w->plan_in = (unsigned long long *)take((nbins + 1) * 8);
   w->plan = (unsigned long long *)take((nbins + 1) * 8);
-  w->chunk_bin = (int32_t *)take((nbins + (E + kChunkEntries - 1) / kChunkEntries + 1) * 4);
+  const long long ncap = nbins + (E + kChunkEntries - 1) / kChunkEntries + 1;
+  w->chunk_bin = (int32_t *)take(ncap * 4);
+  size_t sort_bytes = 0;
+  cub::DeviceRadixSort::SortPairs(nullptr, sort_bytes, (int32_t *)nullptr, (int32_t *)nullptr,
+                                  (int32_t *)nullptr, (int32_t *)nullptr, (int)ncap, 0, 6);
+  w->ord_key_in = (int32_t *)take(ncap * 4);
+  w->ord_key_out = (int32_t *)take(ncap * 4);
+  w->ord_in = (int32_t *)take(ncap * 4);
+  w->ord = (int32_t *)take(ncap * 4);
+  w->sort_bytes = sort_bytes;
+  w->sort_tmp = take(sort_bytes);
   w->csr_bytes = sel_csr_workspace(&c);
   w->csr_ws = take(w->csr_bytes);
   w->scan_bytes = scan_bytes;
@@ -1140,11 +1172,24 @@ bsa_status run_attn_bwd(const bsa_attn_args *a, void *ws, size_t ws_bytes, cudaS
   pl.col = w.col;
   pl.plan = w.plan;
   pl.chunk_bin = w.chunk_bin;
+  pl.chunk_ord = nullptr;
   pl.part = w.part;
   const long long E = (long long)a->B * c.Hs * attn_nq(a) * a->kk;
   pl.npart = 2 * ((E + kChunkEntries - 1) / kChunkEntries) + 1;
   pl.ncol = (int)E;
   const long long dkv_grid = nbins + (E + kChunkEntries - 1) / kChunkEntries;
+  if (a->dtype != BSA_F32 && dkdv_sm100_applicable(a->dtype, a->bs, a->D) &&
+      !getenv("BSA_DKDV_NOSORT")) {
+    const int ncap = (int)(dkv_grid + 1);
+    chunk_key_kernel<<<(ncap + 255) / 256, 256, 0, st>>>(w.plan, w.row_ptr, w.chunk_bin, nbins,
+                                                        kChunkEntries, ncap, w.ord_key_in, w.ord_in);
+    if ((s = check_launch("chunk_key"))) return s;
+    size_t sb = w.sort_bytes;
+    if (cub::DeviceRadixSort::SortPairs(w.sort_tmp, sb, w.ord_key_in, w.ord_key_out, w.ord_in,
+                                        w.ord, ncap, 0, 6, st) != cudaSuccess)
+      return fail(BSA_ERR_LAUNCH, "attn_bwd: chunk order sort failed");
+    pl.chunk_ord = w.ord;
+  }
 
   if (a->dtype == BSA_F32) {
 #define BSA_BF32(BS_, D_) \

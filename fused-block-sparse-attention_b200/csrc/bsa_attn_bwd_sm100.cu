@@ -71,12 +71,13 @@ __device__ __forceinline__ void b5_unit(const BwdPlan &pl, const AttnParams &p, 
   const int y = u % pl.Y;
 #pragma unroll
   for (int t = 0; t < 2; ++t) {
-    const unsigned x = x0 + t;
-    w.valid[t] = x < total;
+    const unsigned xs = x0 + t;
+    w.valid[t] = xs < total;
     w.n[t] = 0;
     w.kb[t] = w.b[t] = w.hk[t] = w.ebeg[t] = w.cidx[t] = w.poff[t] = 0;
     w.nch[t] = 1;
     if (!w.valid[t]) continue;
+    const unsigned x = pl.chunk_ord ? (unsigned)pl.chunk_ord[xs] : xs;
     const int bin = pl.chunk_bin[x];
     const unsigned coff = (unsigned)(pl.plan[bin] >> 32);
     w.poff[t] = (int)(pl.plan[bin] & 0xffffffffu);
