@@ -374,41 +374,54 @@ __global__ void __launch_bounds__(320, 1)
         if (!mbar_wait(&r_full[st], (gs / B5_NST) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
         if (tid == 0) B5_TRACE(3, gs);
         tc05::fence_after();
-        float sv[32], dp[32];
-        tc05::ld32(tmem + lane_base + B5_SCOL + 64 * bb + 32 * hf, sv);
-        tc05::ld32(tmem + lane_base + B5_DPCOL + 64 * bb + 32 * hf, dp);
-        tc05::wait_ld();
-        if (tid == 0) B5_TRACE(6, gs);
-        tc05::fence_before();
-        tc05::mbar_arrive(&s_empty[bb]);
+        // two 16-column halves (keeps the live registers low): loads of half 1
+        // overlap the arithmetic of half 0
         uint32_t wp[16], wd[16];
         const bool active = j < nmine;
-        if (active) {
-          const int qblk = s_meta[st][t][0], slot = s_meta[st][t][1];
-          // qblk is the local query block; kb is global
-          const bool triu = p.causal && ((p.mask_mode == BSA_MASK_SLOT) ? slot == 0 : kb == p.q0 + qblk);
-          const float g2 = s_g2[st][t];
-          const float *lsep = sRow + (st * 2 + t) * 2 * B5_BS + 32 * hf;
-          const long long q0 = (long long)qblk * p.bs + 32 * hf;
-          if (triu || !key_ok || q0 + 32 > p.Lq) {  // diagonal / padded steps: explicit masks
+        const int qblk = s_meta[st][t][0], slot = s_meta[st][t][1];
+        // qblk is the local query block; kb is global
+        const bool triu = p.causal && ((p.mask_mode == BSA_MASK_SLOT) ? slot == 0 : kb == p.q0 + qblk);
+        const float g2 = s_g2[st][t];
+        const float *lsep = sRow + (st * 2 + t) * 2 * B5_BS + 32 * hf;
+        const long long q0 = (long long)qblk * p.bs + 32 * hf;
+        const bool edge = triu || !key_ok || q0 + 32 > p.Lq;
+        float sv[2][16], dp[2][16];
+        tc05::ld16(tmem + lane_base + B5_SCOL + 64 * bb + 32 * hf, sv[0]);
+        tc05::ld16(tmem + lane_base + B5_DPCOL + 64 * bb + 32 * hf, dp[0]);
+        tc05::wait_ld();
+        tc05::ld16(tmem + lane_base + B5_SCOL + 64 * bb + 32 * hf + 16, sv[1]);
+        tc05::ld16(tmem + lane_base + B5_DPCOL + 64 * bb + 32 * hf + 16, dp[1]);
 #pragma unroll
-            for (int c = 0; c < 32; ++c) {
-              const int qc = 32 * hf + c;
-              if (!key_ok || (triu && kr > qc) || q0 + c >= p.Lq) sv[c] = -INFINITY;
-            }
+        for (int h2 = 0; h2 < 2; ++h2) {
+          if (h2 == 1) {
+            tc05::wait_ld();
+            if (tid == 0) B5_TRACE(6, gs);
+            tc05::fence_before();
+            tc05::mbar_arrive(&s_empty[bb]);
           }
+          if (active) {
+            if (edge) {  // diagonal / padded steps: explicit masks
 #pragma unroll
-          for (int c = 0; c < 32; c += 4) {
-            const float4 a4 = *reinterpret_cast<const float4 *>(lsep + c);
-            const float4 d4 = *reinterpret_cast<const float4 *>(lsep + B5_BS + c);
-            const float p0 = ex2(fmaf(sv[c], p.scale2, g2 - a4.x));
-            const float p1 = ex2(fmaf(sv[c + 1], p.scale2, g2 - a4.y));
-            const float p2 = ex2(fmaf(sv[c + 2], p.scale2, g2 - a4.z));
-            const float p3 = ex2(fmaf(sv[c + 3], p.scale2, g2 - a4.w));
-            wp[c >> 1] = Mma<T>::pack(p0, p1);
-            wp[(c >> 1) + 1] = Mma<T>::pack(p2, p3);
-            wd[c >> 1] = Mma<T>::pack(p0 * (dp[c] - d4.x), p1 * (dp[c + 1] - d4.y));
-            wd[(c >> 1) + 1] = Mma<T>::pack(p2 * (dp[c + 2] - d4.z), p3 * (dp[c + 3] - d4.w));
+              for (int c = 0; c < 16; ++c) {
+                const int qc = 32 * hf + 16 * h2 + c;
+                if (!key_ok || (triu && kr > qc) || q0 + 16 * h2 + c >= p.Lq) sv[h2][c] = -INFINITY;
+              }
+            }
+#pragma unroll
+            for (int c = 0; c < 16; c += 4) {
+              const float4 a4 = *reinterpret_cast<const float4 *>(lsep + 16 * h2 + c);
+              const float4 d4 = *reinterpret_cast<const float4 *>(lsep + B5_BS + 16 * h2 + c);
+              const float *x = sv[h2], *y = dp[h2];
+              const float p0 = ex2(fmaf(x[c], p.scale2, g2 - a4.x));
+              const float p1 = ex2(fmaf(x[c + 1], p.scale2, g2 - a4.y));
+              const float p2 = ex2(fmaf(x[c + 2], p.scale2, g2 - a4.z));
+              const float p3 = ex2(fmaf(x[c + 3], p.scale2, g2 - a4.w));
+              const int o = 8 * h2 + (c >> 1);
+              wp[o] = Mma<T>::pack(p0, p1);
+              wp[o + 1] = Mma<T>::pack(p2, p3);
+              wd[o] = Mma<T>::pack(p0 * (y[c] - d4.x), p1 * (y[c + 1] - d4.y));
+              wd[o + 1] = Mma<T>::pack(p2 * (y[c + 2] - d4.z), p3 * (y[c + 3] - d4.w));
+            }
           }
         }
         if (tid == 0) B5_TRACE(5, gs);
@@ -435,60 +448,63 @@ __global__ void __launch_bounds__(320, 1)
         if (tid == 0) B5_TRACE(4, gs);
         tc05::mbar_arrive(&p_full[gs % NPD]);
       }
-      // ---- dK (scaled) and dV of this unit: this thread's row, columns [32*hf, +32)
-      float dkv[32], dvv[32];
+      // ---- dK (scaled) and dV of this unit: this thread's row, columns [32*hf, +32),
+      // one accumulator at a time (32 registers)
+      const int ab = ne & 1;
       if (ns > 0) {
         const int gl = gs - 1;  // last step of this unit
         if (!mbar_wait(&g_done[gl % NPD], (gl / NPD) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
         tc05::fence_after();
-        const int ab = ne & 1;
-        tc05::ld32(tmem + lane_base + B5_DKCOL + 128 * ab + 32 * hf, dkv);
-        tc05::ld32(tmem + lane_base + B5_DVCOL + 128 * ab + 32 * hf, dvv);
-        tc05::wait_ld();
-        tc05::fence_before();
-        tc05::mbar_arrive(&acc_empty[ab]);
-        ++ne;
       }
-      if (!w.valid[t]) continue;
-      if (nmine == 0) {
-#pragma unroll
-        for (int c = 0; c < 32; ++c) dkv[c] = dvv[c] = 0.f;
-      }
-      if (w.nch[t] == 1) {
-        const long long g = (long long)kb * p.bs + kr;
-        if (g < p.L) {
-          T *dkp = reinterpret_cast<T *>(p.dk) + b * p.dk_sb + hk * p.dk_sh + g * p.dk_sl + 32 * hf;
-          T *dvp = reinterpret_cast<T *>(p.dv) + b * p.dv_sb + hk * p.dv_sh + g * p.dv_sl + 32 * hf;
-#pragma unroll
-          for (int c = 0; c < 32; c += 8) {
-            uint4 a4, v4;
-            a4.x = Mma<T>::pack(dkv[c] * p.scale, dkv[c + 1] * p.scale);
-            a4.y = Mma<T>::pack(dkv[c + 2] * p.scale, dkv[c + 3] * p.scale);
-            a4.z = Mma<T>::pack(dkv[c + 4] * p.scale, dkv[c + 5] * p.scale);
-            a4.w = Mma<T>::pack(dkv[c + 6] * p.scale, dkv[c + 7] * p.scale);
-            v4.x = Mma<T>::pack(dvv[c], dvv[c + 1]);
-            v4.y = Mma<T>::pack(dvv[c + 2], dvv[c + 3]);
-            v4.z = Mma<T>::pack(dvv[c + 4], dvv[c + 5]);
-            v4.w = Mma<T>::pack(dvv[c + 6], dvv[c + 7]);
-            *reinterpret_cast<uint4 *>(dkp + c) = a4;
-            *reinterpret_cast<uint4 *>(dvp + c) = v4;
-          }
-        }
-      } else {
-        const long long pidx = (long long)(w.poff[t] + w.cidx[t]) * pl.Y + (u % pl.Y);
+      long long pidx = -1;
+      if (w.valid[t] && w.nch[t] > 1) {
+        pidx = (long long)(w.poff[t] + w.cidx[t]) * pl.Y + (u % pl.Y);
         if (pidx < 0 || pidx >= pl.npart * pl.Y) {  // self-check: partial tile in range
           report(p.status, BSA_DEVERR_INDEX);
-          continue;
-        }
-        float *part = pl.part + pidx * (2LL * B5_BS * B5_D);
-#pragma unroll
-        for (int c = 0; c < 32; c += 4) {
-          *reinterpret_cast<float4 *>(part + kr * B5_D + 32 * hf + c) =
-              make_float4(dkv[c], dkv[c + 1], dkv[c + 2], dkv[c + 3]);
-          *reinterpret_cast<float4 *>(part + B5_BS * B5_D + kr * B5_D + 32 * hf + c) =
-              make_float4(dvv[c], dvv[c + 1], dvv[c + 2], dvv[c + 3]);
+          pidx = -2;
         }
       }
+#pragma unroll 1
+      for (int m = 0; m < 2; ++m) {  // 0: dK, 1: dV
+        float acc[32];
+        if (ns > 0) {
+          tc05::ld32(tmem + lane_base + (m ? B5_DVCOL : B5_DKCOL) + 128 * ab + 32 * hf, acc);
+          tc05::wait_ld();
+          if (m == 1) {
+            tc05::fence_before();
+            tc05::mbar_arrive(&acc_empty[ab]);
+          }
+        }
+        if (!w.valid[t]) continue;
+        if (nmine == 0) {
+#pragma unroll
+          for (int c = 0; c < 32; ++c) acc[c] = 0.f;
+        }
+        if (w.nch[t] == 1) {
+          const long long g = (long long)kb * p.bs + kr;
+          if (g < p.L) {
+            const float sc = m ? 1.f : p.scale;
+            T *dst = m ? reinterpret_cast<T *>(p.dv) + b * p.dv_sb + hk * p.dv_sh + g * p.dv_sl
+                       : reinterpret_cast<T *>(p.dk) + b * p.dk_sb + hk * p.dk_sh + g * p.dk_sl;
+#pragma unroll
+            for (int c = 0; c < 32; c += 8) {
+              uint4 a4;
+              a4.x = Mma<T>::pack(acc[c] * sc, acc[c + 1] * sc);
+              a4.y = Mma<T>::pack(acc[c + 2] * sc, acc[c + 3] * sc);
+              a4.z = Mma<T>::pack(acc[c + 4] * sc, acc[c + 5] * sc);
+              a4.w = Mma<T>::pack(acc[c + 6] * sc, acc[c + 7] * sc);
+              *reinterpret_cast<uint4 *>(dst + 32 * hf + c) = a4;
+            }
+          }
+        } else if (pidx >= 0) {
+          float *part = pl.part + pidx * (2LL * B5_BS * B5_D) + m * (B5_BS * B5_D);
+#pragma unroll
+          for (int c = 0; c < 32; c += 4)
+            *reinterpret_cast<float4 *>(part + kr * B5_D + 32 * hf + c) =
+                make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
+        }
+      }
+      if (ns > 0) ++ne;
     }
   }
   tc05::fence_before();
