@@ -204,6 +204,7 @@ __global__ void __launch_bounds__(320, 1)
       if (ne >= NKV && !mbar_wait(&kv_empty[kvb], ((ne / NKV) - 1) & 1))
         report(p.status, BSA_DEVERR_TIMEOUT);
       mbar_expect_tx(&kv_full[kvb], ((w.n[0] > 0) + (w.n[1] > 0)) * 2 * B5_TILE);
+      #pragma unroll
       for (int t = 0; t < 2; ++t) {
         if (w.n[t] == 0) continue;
         uint8_t *dst = sKV + (kvb * 2 + t) * 2 * B5_TILE;
@@ -224,6 +225,7 @@ __global__ void __launch_bounds__(320, 1)
           B5_TRACE(0, gs);
           const int act = (j < w.n[0]) + (j < w.n[1]);
           int mq[2], mh[2];
+          #pragma unroll
           for (int t = 0; t < 2; ++t) {
             if (j >= w.n[t]) continue;
             const int en = j / p.grp;
@@ -237,6 +239,7 @@ __global__ void __launch_bounds__(320, 1)
           }
           // the arrive below releases the metadata stores to the r_full waiters
           mbar_expect_tx(&r_full[st], act * (2 * B5_TILE + 2 * B5_ROWB));
+          #pragma unroll
           for (int t = 0; t < 2; ++t) {
             if (j >= w.n[t]) continue;
             const int qblk = mq[t], h = mh[t];
@@ -283,6 +286,7 @@ __global__ void __launch_bounds__(320, 1)
           const int st = gsg % B5_NST, ab = neg & 1;
           B5_TRACE(2, gsg);
           tc05::fence_after();
+          #pragma unroll
           for (int t = 0; t < 2; ++t) {
             if (jg >= wg.n[t]) continue;
             const uint32_t q_addr = smem_u32(sR + (st * 2 + t) * 2 * B5_TILE);
@@ -317,6 +321,7 @@ __global__ void __launch_bounds__(320, 1)
           const int st = gss % B5_NST, bb = gss & 1;
           B5_TRACE(1, gss);
           tc05::fence_after();
+          #pragma unroll
           for (int t = 0; t < 2; ++t) {
             if (js >= ws.n[t]) continue;
             const uint32_t q_addr = smem_u32(sR + (st * 2 + t) * 2 * B5_TILE);
@@ -365,7 +370,12 @@ __global__ void __launch_bounds__(320, 1)
       B5Unit w;
       b5_unit(pl, p, total, u, w);
       const int ns = max(w.n[0], w.n[1]);
-      const int nmine = w.n[t], kb = w.kb[t], b = w.b[t], hk = w.hk[t];
+      // this thread's tile by selects (a runtime index would put the unit in local memory)
+      const int nmine = t ? w.n[1] : w.n[0], kb = t ? w.kb[1] : w.kb[0];
+      const int b = t ? w.b[1] : w.b[0], hk = t ? w.hk[1] : w.hk[0];
+      const bool wvalid = t ? w.valid[1] : w.valid[0];
+      const int wnch = t ? w.nch[1] : w.nch[0];
+      const int wpc = t ? w.poff[1] + w.cidx[1] : w.poff[0] + w.cidx[0];
       const bool key_ok = (long long)kb * p.bs + kr < p.L;
       for (int j = 0; j < ns; ++j, ++gs) {
         const int bb = gs & 1, st = gs % B5_NST;
@@ -374,8 +384,8 @@ __global__ void __launch_bounds__(320, 1)
         if (!mbar_wait(&r_full[st], (gs / B5_NST) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
         if (tid == 0) B5_TRACE(3, gs);
         tc05::fence_after();
-        // two 16-column halves (keeps the live registers low): loads of half 1
-        // overlap the arithmetic of half 0
+        // two 16-column halves, loaded one after the other (keeps the live
+        // registers under the 168 a 10-warp CTA allows)
         uint32_t wp[16], wd[16];
         const bool active = j < nmine;
         const int qblk = s_meta[st][t][0], slot = s_meta[st][t][1];
@@ -389,11 +399,11 @@ __global__ void __launch_bounds__(320, 1)
         tc05::ld16(tmem + lane_base + B5_SCOL + 64 * bb + 32 * hf, sv[0]);
         tc05::ld16(tmem + lane_base + B5_DPCOL + 64 * bb + 32 * hf, dp[0]);
         tc05::wait_ld();
-        tc05::ld16(tmem + lane_base + B5_SCOL + 64 * bb + 32 * hf + 16, sv[1]);
-        tc05::ld16(tmem + lane_base + B5_DPCOL + 64 * bb + 32 * hf + 16, dp[1]);
 #pragma unroll
         for (int h2 = 0; h2 < 2; ++h2) {
           if (h2 == 1) {
+            tc05::ld16(tmem + lane_base + B5_SCOL + 64 * bb + 32 * hf + 16, sv[1]);
+            tc05::ld16(tmem + lane_base + B5_DPCOL + 64 * bb + 32 * hf + 16, dp[1]);
             tc05::wait_ld();
             if (tid == 0) B5_TRACE(6, gs);
             tc05::fence_before();
@@ -457,8 +467,8 @@ __global__ void __launch_bounds__(320, 1)
         tc05::fence_after();
       }
       long long pidx = -1;
-      if (w.valid[t] && w.nch[t] > 1) {
-        pidx = (long long)(w.poff[t] + w.cidx[t]) * pl.Y + (u % pl.Y);
+      if (wvalid && wnch > 1) {
+        pidx = (long long)wpc * pl.Y + (u % pl.Y);
         if (pidx < 0 || pidx >= pl.npart * pl.Y) {  // self-check: partial tile in range
           report(p.status, BSA_DEVERR_INDEX);
           pidx = -2;
@@ -475,12 +485,12 @@ __global__ void __launch_bounds__(320, 1)
             tc05::mbar_arrive(&acc_empty[ab]);
           }
         }
-        if (!w.valid[t]) continue;
+        if (!wvalid) continue;
         if (nmine == 0) {
 #pragma unroll
           for (int c = 0; c < 32; ++c) acc[c] = 0.f;
         }
-        if (w.nch[t] == 1) {
+        if (wnch == 1) {
           const long long g = (long long)kb * p.bs + kr;
           if (g < p.L) {
             const float sc = m ? 1.f : p.scale;
