@@ -37,7 +37,7 @@ import torch  # noqa: E402
 METRIC = "fwd+bwd tokens/s at 262k tok (selection+forward+backward)"
 # DRAM bytes per launch of each phase at N=262144, from the ncu launch list in
 # profiles/launches_bench262k.md (attn_bwd = dK/dV + dQ + reduce + CSR kernels).
-TRAFFIC_262K = {"attn_bwd": 5.41e9, "attn_fwd": 1.164e9, "select": 0.29e9}
+TRAFFIC_262K = {"attn_bwd": 9.07e9, "attn_fwd": 1.164e9, "select": 0.564e9}
 UNIT = "tokens/s"
 
 
