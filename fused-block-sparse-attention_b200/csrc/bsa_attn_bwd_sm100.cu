@@ -257,6 +257,11 @@ __global__ void __launch_bounds__(320, 1)
   } else if (warp == 9) {
     // ================= MMA issuer: S/dP queue and dV/dK queue, polled
     if (lane == 0) {
+      // descriptors built once; per MMA only a 64-bit add
+      const uint64_t dkv0 = tc05::sdesc(smem_u32(sKV), 16, 1024);          // K, V (A, K-major)
+      const uint64_t drk0 = tc05::sdesc(smem_u32(sR), 16, 1024);           // Q, dO as K-major B
+      const uint64_t drm0 = tc05::sdesc(smem_u32(sR), B5_BS * 128, 1024);  // Q, dO as MN-major B
+      const uint64_t dpd0 = tc05::sdesc(smem_u32(sPD), 16, 1024);          // P^T, dS^T (A)
       // S queue state
       int us = blockIdx.x, js = 0, gss = 0, nes = -1;
       B5Unit ws;
@@ -289,19 +294,17 @@ __global__ void __launch_bounds__(320, 1)
           #pragma unroll
           for (int t = 0; t < 2; ++t) {
             if (jg >= wg.n[t]) continue;
-            const uint32_t q_addr = smem_u32(sR + (st * 2 + t) * 2 * B5_TILE);
-            const uint32_t do_addr = q_addr + B5_TILE;
-            const uint32_t p_addr = smem_u32(sPD + ((gsg % NPD) * 2 + t) * 2 * B5_TILE);
-            const uint32_t ds_addr = p_addr + B5_TILE;
+            const uint32_t roff = (st * 2 + t) * 2 * B5_TILE;        // Q; dO at + TILE
+            const uint32_t poff = ((gsg % NPD) * 2 + t) * 2 * B5_TILE;  // P^T; dS^T at + TILE
+            const uint64_t ap = tc05::dadd(dpd0, poff), ads = tc05::dadd(dpd0, poff + B5_TILE);
+            const uint64_t bdo = tc05::dadd(drm0, roff + B5_TILE), bq = tc05::dadd(drm0, roff);
             const uint32_t dv = tc05::taddr(tmem, 16 * t, B5_DVCOL + 128 * ab);
             const uint32_t dk = tc05::taddr(tmem, 16 * t, B5_DKCOL + 128 * ab);
 #pragma unroll
             for (int ks = 0; ks < B5_BS / 16; ++ks) {
               const uint32_t acc = (jg > 0 || ks > 0) ? 1u : 0u;
-              tc05::mma_f16(dv, tc05::sdesc(p_addr + ks * 32, 16, 1024),
-                            tc05::sdesc(do_addr + ks * 2048, B5_BS * 128, 1024), IDESC_KM, acc);
-              tc05::mma_f16(dk, tc05::sdesc(ds_addr + ks * 32, 16, 1024),
-                            tc05::sdesc(q_addr + ks * 2048, B5_BS * 128, 1024), IDESC_KM, acc);
+              tc05::mma_f16(dv, tc05::dadd(ap, ks * 32), tc05::dadd(bdo, ks * 2048), IDESC_KM, acc);
+              tc05::mma_f16(dk, tc05::dadd(ads, ks * 32), tc05::dadd(bq, ks * 2048), IDESC_KM, acc);
             }
           }
           tc05::commit(&r_empty[st]);
@@ -324,18 +327,16 @@ __global__ void __launch_bounds__(320, 1)
           #pragma unroll
           for (int t = 0; t < 2; ++t) {
             if (js >= ws.n[t]) continue;
-            const uint32_t q_addr = smem_u32(sR + (st * 2 + t) * 2 * B5_TILE);
-            const uint32_t do_addr = q_addr + B5_TILE;
-            const uint32_t k_addr = smem_u32(sKV + ((nes % NKV) * 2 + t) * 2 * B5_TILE);
-            const uint32_t v_addr = k_addr + B5_TILE;
+            const uint32_t roff = (st * 2 + t) * 2 * B5_TILE;          // Q; dO at + TILE
+            const uint32_t koff = ((nes % NKV) * 2 + t) * 2 * B5_TILE;  // K; V at + TILE
+            const uint64_t ak = tc05::dadd(dkv0, koff), av = tc05::dadd(dkv0, koff + B5_TILE);
+            const uint64_t bq = tc05::dadd(drk0, roff), bdo = tc05::dadd(drk0, roff + B5_TILE);
             const uint32_t ds = tc05::taddr(tmem, 16 * t, B5_SCOL + 64 * bb);
             const uint32_t ddp = tc05::taddr(tmem, 16 * t, B5_DPCOL + 64 * bb);
 #pragma unroll
             for (int ks = 0; ks < B5_D / 16; ++ks) {
-              tc05::mma_f16(ds, tc05::sdesc(k_addr + ks * 32, 16, 1024),
-                            tc05::sdesc(q_addr + ks * 32, 16, 1024), IDESC_KK, ks > 0);
-              tc05::mma_f16(ddp, tc05::sdesc(v_addr + ks * 32, 16, 1024),
-                            tc05::sdesc(do_addr + ks * 32, 16, 1024), IDESC_KK, ks > 0);
+              tc05::mma_f16(ds, tc05::dadd(ak, ks * 32), tc05::dadd(bq, ks * 32), IDESC_KK, ks > 0);
+              tc05::mma_f16(ddp, tc05::dadd(av, ks * 32), tc05::dadd(bdo, ks * 32), IDESC_KK, ks > 0);
             }
           }
           tc05::commit(&s_full[bb]);

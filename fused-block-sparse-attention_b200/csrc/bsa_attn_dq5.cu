@@ -173,7 +173,13 @@ __global__ void __launch_bounds__(192, 2)
     // ================= MMA issuer: S/dP queue and dQ queue, polled
     if (lane == 0) {
       if (!mbar_wait(&bar_q, 0)) report(p.status, BSA_DEVERR_TIMEOUT);
-      const uint32_t q_addr = smem_u32(sQ), do_addr = smem_u32(sDO), ds_addr = smem_u32(sS);
+      // descriptors built once; per MMA only a 64-bit add
+      const uint64_t dq0 = tc05::sdesc(smem_u32(sQ), 16, 1024);
+      const uint64_t ddo0 = tc05::sdesc(smem_u32(sDO), 16, 1024);
+      const uint64_t dds0 = tc05::sdesc(smem_u32(sS), 16, 1024);
+      const uint64_t dk0 = tc05::sdesc(smem_u32(sK), 16, 1024);
+      const uint64_t dkm0 = tc05::sdesc(smem_u32(sK), D5_BS * 128, 1024);  // K as MN-major B
+      const uint64_t dv0 = tc05::sdesc(smem_u32(sV), 16, 1024);
       int js = 0, jg = 0;
       uint32_t idle = 0;
       while (jg < nsteps) {
@@ -184,13 +190,13 @@ __global__ void __launch_bounds__(192, 2)
           tc05::fence_after();
           for (int t = 0; t < 2; ++t) {
             if (jg >= (t ? nB : nA)) continue;
-            const uint32_t k_addr = smem_u32(sK + (st * 2 + t) * D5_TILE);
+            const uint64_t da = tc05::dadd(dds0, t * D5_TILE);
+            const uint64_t db = tc05::dadd(dkm0, (st * 2 + t) * D5_TILE);
             const uint32_t d = tc05::taddr(tmem, 16 * t, D5_DQCOL);
             // a tile's first live step starts its accumulator
 #pragma unroll
             for (int ks = 0; ks < D5_BS / 16; ++ks)
-              tc05::mma_f16(d, tc05::sdesc(ds_addr + t * D5_TILE + ks * 32, 16, 1024),
-                            tc05::sdesc(k_addr + ks * 2048, D5_BS * 128, 1024), IDESC_DQ,
+              tc05::mma_f16(d, tc05::dadd(da, ks * 32), tc05::dadd(db, ks * 2048), IDESC_DQ,
                             (jg > 0 || ks > 0) ? 1u : 0u);
           }
           tc05::commit(&k_empty[st]);
@@ -205,16 +211,14 @@ __global__ void __launch_bounds__(192, 2)
           tc05::fence_after();
           for (int t = 0; t < 2; ++t) {
             if (js >= (t ? nB : nA)) continue;
-            const uint32_t k_addr = smem_u32(sK + (st * 2 + t) * D5_TILE);
-            const uint32_t v_addr = smem_u32(sV + t * D5_TILE);
+            const uint64_t aq = tc05::dadd(dq0, t * D5_TILE), ado = tc05::dadd(ddo0, t * D5_TILE);
+            const uint64_t bk = tc05::dadd(dk0, (st * 2 + t) * D5_TILE), bv = tc05::dadd(dv0, t * D5_TILE);
             const uint32_t ds = tc05::taddr(tmem, 16 * t, D5_SCOL);
             const uint32_t ddp = tc05::taddr(tmem, 16 * t, D5_DPCOL);
 #pragma unroll
             for (int ks = 0; ks < D5_D / 16; ++ks) {
-              tc05::mma_f16(ds, tc05::sdesc(q_addr + t * D5_TILE + ks * 32, 16, 1024),
-                            tc05::sdesc(k_addr + ks * 32, 16, 1024), IDESC_S, ks > 0);
-              tc05::mma_f16(ddp, tc05::sdesc(do_addr + t * D5_TILE + ks * 32, 16, 1024),
-                            tc05::sdesc(v_addr + ks * 32, 16, 1024), IDESC_S, ks > 0);
+              tc05::mma_f16(ds, tc05::dadd(aq, ks * 32), tc05::dadd(bk, ks * 32), IDESC_S, ks > 0);
+              tc05::mma_f16(ddp, tc05::dadd(ado, ks * 32), tc05::dadd(bv, ks * 32), IDESC_S, ks > 0);
             }
           }
           tc05::commit(&sd_full);

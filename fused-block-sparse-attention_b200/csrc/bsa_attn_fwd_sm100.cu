@@ -214,7 +214,12 @@ __global__ void __launch_bounds__(192, 1)
     // ================= MMA issuer (S and PV queues, polled)
     if (lane == 0) {
       if (!mbar_wait(&bar_q, 0)) report(p.status, BSA_DEVERR_TIMEOUT);
-      const uint32_t q_addr = smem_u32(sQ), p_addr = smem_u32(sP);
+      // descriptors built once; per MMA only a 64-bit add (the issuing thread's
+      // scalar work is on the critical path of every step)
+      const uint64_t dq0 = tc05::sdesc(smem_u32(sQ), 16, 1024);
+      const uint64_t dp0 = tc05::sdesc(smem_u32(sP), 16, 1024);
+      const uint64_t dk0 = tc05::sdesc(smem_u32(sK), 16, 1024);
+      const uint64_t dv0 = tc05::sdesc(smem_u32(sV), F5_BS * 128, 1024);
       int js = 0, jp = 0;
       uint32_t idle = 0;
       while (js < nsteps || jp < nsteps) {
@@ -226,12 +231,12 @@ __global__ void __launch_bounds__(192, 1)
           tc05::fence_after();
           for (int t = 0; t < 2; ++t) {
             if (jp >= (t ? nB : nA)) continue;
-            const uint32_t v_addr = smem_u32(sV + (st * 2 + t) * F5_TILE);
+            const uint64_t da = tc05::dadd(dp0, t * F5_TILE);
+            const uint64_t db = tc05::dadd(dv0, (st * 2 + t) * F5_TILE);
             const uint32_t d = tc05::taddr(tmem, 16 * t, F5_OCOL);
 #pragma unroll
             for (int ks = 0; ks < F5_BS / 16; ++ks)
-              tc05::mma_f16(d, tc05::sdesc(p_addr + t * F5_TILE + ks * 32, 16, 1024),
-                            tc05::sdesc(v_addr + ks * 2048, F5_BS * 128, 1024), IDESC_PV,
+              tc05::mma_f16(d, tc05::dadd(da, ks * 32), tc05::dadd(db, ks * 2048), IDESC_PV,
                             (jp > 0 || ks > 0) ? 1u : 0u);
           }
           tc05::commit(&v_empty[st]);
@@ -246,12 +251,12 @@ __global__ void __launch_bounds__(192, 1)
           tc05::fence_after();
           for (int t = 0; t < 2; ++t) {
             if (js >= (t ? nB : nA)) continue;
-            const uint32_t k_addr = smem_u32(sK + (st * 2 + t) * F5_TILE);
+            const uint64_t da = tc05::dadd(dq0, t * F5_TILE);
+            const uint64_t db = tc05::dadd(dk0, (st * 2 + t) * F5_TILE);
             const uint32_t d = tc05::taddr(tmem, 16 * t, F5_SCOL0 + 64 * bb);
 #pragma unroll
             for (int ks = 0; ks < F5_D / 16; ++ks)
-              tc05::mma_f16(d, tc05::sdesc(q_addr + t * F5_TILE + ks * 32, 16, 1024),
-                            tc05::sdesc(k_addr + ks * 32, 16, 1024), IDESC_S, ks > 0);
+              tc05::mma_f16(d, tc05::dadd(da, ks * 32), tc05::dadd(db, ks * 32), IDESC_S, ks > 0);
           }
           tc05::commit(&s_full[bb]);
           tc05::commit(&k_empty[st]);

@@ -67,6 +67,13 @@ __device__ __forceinline__ uint64_t sdesc(uint32_t saddr, uint32_t lbo, uint32_t
   return d;
 }
 
+// Descriptor of the same layout `bytes` further on (16-byte aligned offsets whose
+// start address stays inside shared memory, so the 14-bit address field cannot
+// carry into the next field): one 64-bit add instead of rebuilding the fields.
+__device__ __forceinline__ uint64_t dadd(uint64_t desc, uint32_t bytes) {
+  return desc + (uint64_t)(bytes >> 4);
+}
+
 // Instruction descriptor, kind::f16 with fp32 accumulation.  A is K-major;
 // B is K-major (b_mn = false) or MN-major (b_mn = true).
 __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N, bool b_mn) {
