@@ -92,7 +92,9 @@ __device__ __forceinline__ void b5_unit(const BwdPlan &pl, const AttnParams &p, 
   }
 }
 
-template <typename T, int B5_NST, int NPD, int NKV>
+// GATE: a gate tensor is present (without one the exponent's offset is -lse, which
+// folds into the FMA)
+template <typename T, int B5_NST, int NPD, int NKV, bool GATE>
 __global__ void __launch_bounds__(320, 1)
     attn_dkdv_sm100_kernel(const __grid_constant__ CUtensorMap tq,
                            const __grid_constant__ CUtensorMap tdo,
@@ -392,7 +394,7 @@ __global__ void __launch_bounds__(320, 1)
         const int qblk = s_meta[st][t][0], slot = s_meta[st][t][1];
         // qblk is the local query block; kb is global
         const bool triu = p.causal && ((p.mask_mode == BSA_MASK_SLOT) ? slot == 0 : kb == p.q0 + qblk);
-        const float g2 = s_g2[st][t];
+        const float g2 = GATE ? s_g2[st][t] : 0.f;
         const float *lsep = sRow + (st * 2 + t) * 2 * B5_BS + 32 * hf;
         const long long q0 = (long long)qblk * p.bs + 32 * hf;
         const bool edge = triu || !key_ok || q0 + 32 > p.Lq;
@@ -552,14 +554,14 @@ bsa_status launch_dkdv_sm100(int dtype, const CUtensorMap &mq, const CUtensorMap
   const int variant = cfg ? atoi(cfg) : 41;
 #define BSA_B5_LAUNCH(T_, N_, P_, KV_)                                                      \
   {                                                                                         \
-    auto kern = attn_dkdv_sm100_kernel<T_, N_, P_, KV_>;                                    \
+    auto kern = p.gate ? attn_dkdv_sm100_kernel<T_, N_, P_, KV_, true>                      \
+                       : attn_dkdv_sm100_kernel<T_, N_, P_, KV_, false>;                    \
     constexpr int sm = b5_smem(N_, P_, KV_);                                                \
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);            \
     kern<<<grid, 320, sm, st>>>(mq, mdo, mk, mv, pq, pdo, pk, pv, p, pl);                   \
   }
 #define BSA_B5_PICK(T_)                                      \
   if (variant == 32) BSA_B5_LAUNCH(T_, 3, 2, 1)              \
-  else if (variant == 312) BSA_B5_LAUNCH(T_, 3, 1, 2)        \
   else BSA_B5_LAUNCH(T_, 4, 1, 1)
   if (dtype == BSA_BF16) {
     BSA_B5_PICK(__nv_bfloat16)

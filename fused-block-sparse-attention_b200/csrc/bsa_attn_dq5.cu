@@ -265,6 +265,7 @@ __global__ void __launch_bounds__(192, 2)
         kb = item >> 3;
         g2 = gaterow ? __ldg(gaterow + s_islot[t][j]) * kLog2e : 0.f;
       }
+      const float off = g2 - lse;  // exponent offset of this row and step
       uint32_t w[32];
       float dgs = 0.f;
 #pragma unroll
@@ -281,7 +282,7 @@ __global__ void __launch_bounds__(192, 2)
             const int col = 32 * hf + c + e;
             const bool masked = !active || ((kind & KIND_TRIU) && col > r) ||
                                 ((kind & KIND_PAD) && kb * p.bs + col >= p.L);
-            const float pr = masked ? 0.f : ex2(fmaf(s[c + e], p.scale2, g2) - lse);
+            const float pr = masked ? 0.f : ex2(fmaf(s[c + e], p.scale2, off));
             d2[e] = pr * (dp[c + e] - dv);
             dgs += d2[e];
           }
