@@ -274,19 +274,30 @@ __global__ void __launch_bounds__(192, 2)
         tc05::ld32(tmem + lane_base + D5_SCOL + 32 * hf, s);
         tc05::ld32(tmem + lane_base + D5_DPCOL + 32 * hf, dp);
         tc05::wait_ld();
+        if (active && !(kind & (KIND_TRIU | KIND_PAD))) {  // common case: no masks
 #pragma unroll
-        for (int c = 0; c < 32; c += 2) {
-          float d2[2];
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int col = 32 * hf + c + e;
-            const bool masked = !active || ((kind & KIND_TRIU) && col > r) ||
-                                ((kind & KIND_PAD) && kb * p.bs + col >= p.L);
-            const float pr = masked ? 0.f : ex2(fmaf(s[c + e], p.scale2, off));
-            d2[e] = pr * (dp[c + e] - dv);
-            dgs += d2[e];
+          for (int c = 0; c < 32; c += 2) {
+            const float d0 = ex2(fmaf(s[c], p.scale2, off)) * (dp[c] - dv);
+            const float d1 = ex2(fmaf(s[c + 1], p.scale2, off)) * (dp[c + 1] - dv);
+            dgs += d0;
+            dgs += d1;
+            w[16 * hf + (c >> 1)] = Mma<T>::pack(d0, d1);
           }
-          w[16 * hf + (c >> 1)] = Mma<T>::pack(d2[0], d2[1]);
+        } else {  // diagonal / padded block, or an idle tile (its TMEM is stale)
+#pragma unroll
+          for (int c = 0; c < 32; c += 2) {
+            float d2[2];
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int col = 32 * hf + c + e;
+              const bool masked = !active || ((kind & KIND_TRIU) && col > r) ||
+                                  ((kind & KIND_PAD) && kb * p.bs + col >= p.L);
+              const float pr = masked ? 0.f : ex2(fmaf(s[c + e], p.scale2, off));
+              d2[e] = pr * (dp[c + e] - dv);
+              dgs += d2[e];
+            }
+            w[16 * hf + (c >> 1)] = Mma<T>::pack(d2[0], d2[1]);
+          }
         }
       }
       tc05::fence_before();
