@@ -31,7 +31,6 @@ struct AttnParams {
   float *dgate;
   float *dvec;  // (B,Hq,Lp) rowsum(dO * O)
   int32_t *status;
-  unsigned long long *trace;  // pipeline timestamps (builds with -DBSA_TRACE only)
 };
 
 // Backward CSR / chunk plan (device pointers into the workspace).

@@ -103,7 +103,10 @@ bsa_status run_sel_csr(const bsa_csr_args *a, void *ws, size_t ws_bytes, cudaStr
   csr_layout(a, &w, reinterpret_cast<uint8_t *>(ws));
   const long long nbins = (long long)a->B * a->Hs * a->nblk;
   const long long n = (long long)a->B * a->Hs * csr_nq(a) * a->kk;
-  cudaMemsetAsync(w.cnt, 0, (nbins + 1) * 4, st);
+  // the counts must start at zero (the allocation-free entry point reuses its
+  // scratch across calls, so this clear is what keeps a call from seeing the last one's)
+  if (cudaMemsetAsync(w.cnt, 0, (nbins + 1) * 4, st) != cudaSuccess)
+    return fail(BSA_ERR_LAUNCH, "sel_csr: clearing the bin counts failed");
   const int threads = 256;
   const long long blocks = std::min<long long>((n + threads - 1) / threads, 148LL * 64);
   csr_count_kernel<<<(unsigned)std::max<long long>(blocks, 1), threads, 0, st>>>(

@@ -33,17 +33,6 @@
 
 namespace bsa {
 
-#ifdef BSA_TRACE
-#define B5_TRACE(ev, j)                                                                  \
-  do {                                                                                   \
-    if (b5_tr && (j) < 127) p.trace[(ev) * 128 + (j)] = clock64();                  \
-  } while (0)
-#else
-#define B5_TRACE(ev, j) \
-  do {                  \
-  } while (0)
-#endif
-
 namespace {
 constexpr int B5_BS = 64, B5_D = 64;
 constexpr int B5_TILE = B5_BS * B5_D * 2;            // 8 KB
@@ -126,9 +115,6 @@ __global__ void __launch_bounds__(320, 1)
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const unsigned total = (unsigned)(pl.plan[pl.nbins] >> 32);
-#ifdef BSA_TRACE
-  const bool b5_tr = p.trace && blockIdx.x == p.trace[1023];
-#endif
   const int nunits = (int)((total + 1) / 2) * pl.Y;
 
   if (tid == 0) {
@@ -224,7 +210,6 @@ __global__ void __launch_bounds__(320, 1)
             __nanosleep(32);
           }
           idle = 0;
-          B5_TRACE(0, gs);
           const int act = (j < w.n[0]) + (j < w.n[1]);
           int mq[2], mh[2];
           #pragma unroll
@@ -291,7 +276,6 @@ __global__ void __launch_bounds__(320, 1)
         if (gsg < gss && mbar_test(&p_full[gsg % NPD], (gsg / NPD) & 1) &&
             (jg > 0 || neg < 2 || mbar_test(&acc_empty[neg & 1], ((neg >> 1) - 1) & 1))) {
           const int st = gsg % B5_NST, ab = neg & 1;
-          B5_TRACE(2, gsg);
           tc05::fence_after();
           #pragma unroll
           for (int t = 0; t < 2; ++t) {
@@ -324,7 +308,6 @@ __global__ void __launch_bounds__(320, 1)
             (gss < 2 || mbar_test(&s_empty[gss & 1], ((gss >> 1) - 1) & 1)) &&
             (js > 0 || mbar_test(&kv_full[nes % NKV], (nes / NKV) & 1))) {
           const int st = gss % B5_NST, bb = gss & 1;
-          B5_TRACE(1, gss);
           tc05::fence_after();
           #pragma unroll
           for (int t = 0; t < 2; ++t) {
@@ -385,7 +368,6 @@ __global__ void __launch_bounds__(320, 1)
         if (!mbar_wait(&s_full[bb], (gs >> 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
         // acquire the stage's TMA / bulk data and the producer's metadata
         if (!mbar_wait(&r_full[st], (gs / B5_NST) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
-        if (tid == 0) B5_TRACE(3, gs);
         tc05::fence_after();
         // two 16-column halves, loaded one after the other (keeps the live
         // registers under the 168 a 10-warp CTA allows)
@@ -408,7 +390,6 @@ __global__ void __launch_bounds__(320, 1)
             tc05::ld16(tmem + lane_base + B5_SCOL + 64 * bb + 32 * hf + 16, sv[1]);
             tc05::ld16(tmem + lane_base + B5_DPCOL + 64 * bb + 32 * hf + 16, dp[1]);
             tc05::wait_ld();
-            if (tid == 0) B5_TRACE(6, gs);
             tc05::fence_before();
             tc05::mbar_arrive(&s_empty[bb]);
           }
@@ -437,12 +418,10 @@ __global__ void __launch_bounds__(320, 1)
             }
           }
         }
-        if (tid == 0) B5_TRACE(5, gs);
         if (gs >= NPD) {  // dV/dK of step gs-NPD read P / dS buffer gs % NPD
           if (!mbar_wait(&g_done[gs % NPD], ((gs / NPD) - 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
           tc05::fence_after();
         }
-        if (tid == 0) B5_TRACE(7, gs);
         if (active) {
           const uint32_t pa = smem_u32(sPD + ((gs % NPD) * 2 + t) * 2 * B5_TILE);
 #pragma unroll
@@ -458,7 +437,6 @@ __global__ void __launch_bounds__(320, 1)
         }
         fence_proxy_async_smem();
         tc05::fence_before();
-        if (tid == 0) B5_TRACE(4, gs);
         tc05::mbar_arrive(&p_full[gs % NPD]);
       }
       // ---- dK (scaled) and dV of this unit: this thread's row, columns [32*hf, +32),
@@ -543,11 +521,6 @@ bsa_status launch_dkdv_sm100(int dtype, const CUtensorMap &mq, const CUtensorMap
   cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
   const long long units_max = ((dkv_grid + 1) / 2) * pl.Y;
   const unsigned grid = (unsigned)std::max<long long>(1, std::min<long long>(nsm, units_max));
-#ifdef BSA_TRACE
-  AttnParams pt = p;
-  if (const char *tp = getenv("BSA_TRACE_PTR")) pt.trace = (unsigned long long *)strtoull(tp, nullptr, 0);
-#define p pt
-#endif
   // ring stages / P-dS buffers: 4/1 by default (the deeper ring hides more of
   // the Q/dO load latency than a second P/dS buffer saves); BSA_DKDV_CFG=32 for 3/2
   const char *cfg = getenv("BSA_DKDV_CFG");
@@ -570,9 +543,6 @@ bsa_status launch_dkdv_sm100(int dtype, const CUtensorMap &mq, const CUtensorMap
   }
 #undef BSA_B5_PICK
 #undef BSA_B5_LAUNCH
-#ifdef BSA_TRACE
-#undef p
-#endif
   return check_launch("attn_dkdv_sm100");
 }
 

@@ -33,31 +33,7 @@
 
 namespace bsa {
 
-// Optional pipeline trace of CTA 0 (compile with -DBSA_TRACE): slot
-// [event * 64 + step] receives clock64() at that event.
-#ifdef BSA_TRACE
-#define F5_TRACE(ev, j)                                                           \
-  do {                                                                            \
-    if (p.trace && blockIdx.x == p.trace[1023] && (j) < 64) p.trace[(ev) * 64 + (j)] = clock64(); \
-  } while (0)
-#else
-#define F5_TRACE(ev, j) \
-  do {                  \
-  } while (0)
-#endif
 
-#ifdef BSA_TRACE
-__device__ __forceinline__ unsigned long long f5_gtime() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
-__device__ __forceinline__ unsigned f5_smid() {
-  unsigned r;
-  asm volatile("mov.u32 %0, %smid;" : "=r"(r));
-  return r;
-}
-#endif
 
 namespace {
 constexpr int F5_BS = 64, F5_D = 64;
@@ -107,12 +83,6 @@ __global__ void __launch_bounds__(192, 1)
   const int qb0 = 2 * pair;  // local index of tile A's query block
   const bool validB = qb0 + 1 < p.nq;
 
-#ifdef BSA_TRACE
-  if (p.trace && tid == 0) {
-    p.trace[1024 + 3 * blockIdx.x] = f5_smid();
-    p.trace[1024 + 3 * blockIdx.x + 1] = f5_gtime();
-  }
-#endif
   // ---- live-slot lists of both tiles (one thread per tile)
   if (tid == 0 || tid == 32) {
     const int t = tid >> 5;
@@ -190,7 +160,6 @@ __global__ void __launch_bounds__(192, 1)
         bool progress = false;
         if (jk < nsteps &&
             (jk < F5_NST || mbar_test(&k_empty[jk % F5_NST], ((jk / F5_NST) - 1) & 1))) {
-          F5_TRACE(0, jk);
           issue(false, jk++);
           progress = true;
         }
@@ -227,7 +196,6 @@ __global__ void __launch_bounds__(192, 1)
         if (jp < js && mbar_test(&p_full, jp & 1) &&
             mbar_test(&v_full[jp % F5_NST], (jp / F5_NST) & 1)) {
           const int st = jp % F5_NST;
-          F5_TRACE(3, jp);
           tc05::fence_after();
           for (int t = 0; t < 2; ++t) {
             if (jp >= (t ? nB : nA)) continue;
@@ -247,7 +215,6 @@ __global__ void __launch_bounds__(192, 1)
         if (js < nsteps && mbar_test(&k_full[js % F5_NST], (js / F5_NST) & 1) &&
             (js < 2 || mbar_test(&s_empty[js & 1], ((js >> 1) - 1) & 1))) {
           const int st = js % F5_NST, bb = js & 1;
-          F5_TRACE(2, js);
           tc05::fence_after();
           for (int t = 0; t < 2; ++t) {
             if (js >= (t ? nB : nA)) continue;
@@ -290,7 +257,6 @@ __global__ void __launch_bounds__(192, 1)
     for (int j = 0; j < nsteps; ++j) {
       const int bb = j & 1;
       if (!mbar_wait(&s_full[bb], (j >> 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
-      if (lane == 0) F5_TRACE(4 + warp, j);
       tc05::fence_after();
       tc05::ld32(tmem + lane_base + F5_SCOL0 + 64 * bb, s);
       tc05::ld32(tmem + lane_base + F5_SCOL0 + 64 * bb + 32, s + 32);
@@ -373,7 +339,6 @@ __global__ void __launch_bounds__(192, 1)
       }
       fence_proxy_async_smem();
       tc05::fence_before();
-      if (lane == 0) F5_TRACE(8 + warp, j);
       tc05::mbar_arrive(&p_full);
     }
     // ---- epilogue: O / l
@@ -410,9 +375,6 @@ __global__ void __launch_bounds__(192, 1)
   }
   tc05::fence_before();
   __syncthreads();
-#ifdef BSA_TRACE
-  if (p.trace && tid == 0) p.trace[1024 + 3 * blockIdx.x + 2] = f5_gtime();
-#endif
   if (warp == 5) {
     tc05::fence_after();
     tc05::dealloc(tmem, F5_TMEM_COLS);
@@ -436,11 +398,6 @@ bsa_status launch_fwd_sm100(const bsa_attn_args *a, const AttnParams &p, cudaStr
     return s;
   auto pk = [](const TensorMap4 &m) { return m.perm[0] | (m.perm[1] << 2) | (m.perm[2] << 4); };
   const long long grid = (long long)a->B * a->Hq * ((p.nq + 1) / 2);
-#ifdef BSA_TRACE
-  AttnParams pt = p;
-  if (const char *tp = getenv("BSA_TRACE_PTR")) pt.trace = (unsigned long long *)strtoull(tp, nullptr, 0);
-#define p pt
-#endif
   const char *env = getenv("BSA_FWD_STAGES");
   const bool three = env && env[0] == '3';
 #define BSA_F5_LAUNCH(T_, N_)                                                                   \
@@ -456,9 +413,6 @@ bsa_status launch_fwd_sm100(const bsa_attn_args *a, const AttnParams &p, cudaStr
     if (three) BSA_F5_LAUNCH(__half, 3) else BSA_F5_LAUNCH(__half, 2)
   }
 #undef BSA_F5_LAUNCH
-#ifdef BSA_TRACE
-#undef p
-#endif
   return check_launch("attn_fwd_sm100");
 }
 

@@ -14,7 +14,8 @@
 // Rules of use:
 //  - The first call on a device looks up the array's device address
 //    (cudaGetSymbolAddress) with that device current; make that first call
-//    before any stream capture.
+//    before any stream capture.  The address is cached for the life of the
+//    process: it does not survive cudaDeviceReset of that device.
 //  - All calls on a device share the array, which keeps the previous call's
 //    contents; the counts that must start at zero are cleared by every call.
 //    Calls whose work overlaps on the GPU (different streams, or different host

@@ -3,6 +3,7 @@ sm_100a: same entry points and argument meaning, backed by libbsa_b200.so.
 
   bsattn_forward(q, k, v, sel, gate_bias=None, causal=False) -> o      (:184-207)
   bsattn_backward(q, k, v, sel, o, do, gate_bias=None, causal=False)   (:210-234)
+      (+ keyword lse= from bsattn_forward_lse: skips the recomputing forward)
   BSAttnFunction.apply(q, k, v, sel, gate_bias, causal)                (:237-254)
   bsattn(q, k, v, sel, gate_bias=None, causal=False)                   (:257-259)
 
@@ -21,7 +22,7 @@ import torch
 
 import _bsa
 
-__all__ = ["bsattn_forward", "bsattn_backward", "BSAttnFunction", "bsattn"]
+__all__ = ["bsattn_forward", "bsattn_backward", "BSAttnFunction", "bsattn", "bsattn_forward_lse"]
 
 
 def _geometry(q, sel):
@@ -44,15 +45,26 @@ def _forward_lse(q, k, v, sel, gate_bias, causal):
     return _bsa.attn_fwd(q, k, v, sel, gate_bias, bs=bs, causal=causal, want_lse=True)
 
 
-def bsattn_backward(q, k, v, sel, o, do, gate_bias=None, causal=False):
-    """(dQ, dK, dV) of the block-sparse attention.  The row log-sum-exp is
-    recomputed by a forward pass (the autograd path reuses the saved one)."""
+def bsattn_backward(q, k, v, sel, o, do, gate_bias=None, causal=False, *, lse=None):
+    """(dQ, dK, dV) of the block-sparse attention.
+
+    Without `lse` the row log-sum-exp is recomputed by a forward pass, as the
+    reference recomputes it (src/triton_kernel.py:106-129), and `o` is not read
+    (the reference ignores it too; the recomputed output keeps rowsum(dO * O)
+    consistent with the recomputed lse).  With `lse` (an extension: the fp32
+    (B, H, L) tensor that `bsattn_forward_lse` returns beside `o`) the backward
+    uses the given `o` and `lse` and runs no forward."""
     bs = _geometry(q, sel)
-    o2, lse = _forward_lse(q, k, v, sel, gate_bias, causal)
-    # `o` is accepted for signature parity (the reference ignores it too); the
-    # recomputed output keeps rowsum(dO * O) consistent with the recomputed lse.
-    dq, dk, dv, _ = _bsa.attn_bwd(q, k, v, o2, do, sel, lse, gate_bias, bs=bs, causal=causal)
+    if lse is None:
+        o, lse = _forward_lse(q, k, v, sel, gate_bias, causal)
+    dq, dk, dv, _ = _bsa.attn_bwd(q, k, v, o, do, sel, lse, gate_bias, bs=bs, causal=causal)
     return dq, dk, dv
+
+
+def bsattn_forward_lse(q, k, v, sel, gate_bias=None, causal=False):
+    """(o, lse): the forward output and its fp32 row log-sum-exp (log2 domain,
+    scale folded in), for callers that run bsattn_backward(..., lse=lse) later."""
+    return _forward_lse(q, k, v, sel, gate_bias, causal)
 
 
 class BSAttnFunction(torch.autograd.Function):

@@ -296,8 +296,10 @@ bsa_status bsa_sel_csr(const bsa_csr_args *a, void *workspace, size_t workspace_
  * reference.  Its scratch is a fixed 16 MiB device array inside the library
  * (held by every GPU that loads it until exit); selections needing more are
  * rejected with BSA_ERR_UNSUPPORTED.  The first call on a device resolves the
- * array's address and should precede any stream capture; calls share the array,
- * so calls that overlap on the GPU race.  Allocates nothing. */
+ * array's address and should precede any stream capture; the address is kept
+ * for the life of the process, so it does not survive cudaDeviceReset (do not
+ * call this entry point after resetting a device in the same process).  Calls
+ * share the array, so calls that overlap on the GPU race.  Allocates nothing. */
 bsa_status bsa_sel_csr_noalloc(const bsa_csr_args *a, bsa_stream_t stream);
 
 /* Partial rotary embedding with the arithmetic of transformers'

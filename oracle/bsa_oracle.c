@@ -39,7 +39,7 @@
  *                    masks of src/triton_kernel.py:57-61 (SLOT) or
  *                    src/qwen_blocksparse.py:67-72 (TOKEN).
  *
- * Build: oracle/build.sh (gcc -O2 -ffp-contract=off -fPIC -shared).
+ * Build: oracle/build.sh (gcc -O2 -ffp-contract=off -fopenmp -fPIC -shared).
  */
 #include <math.h>
 #include <stdint.h>
@@ -112,74 +112,101 @@ static int cmp_int(const void *p, const void *q) {
   return (a > b) - (a < b);
 }
 
-/* a, b1, b2: (G, nblk, dim) fp32.  sel: (G, nblk, W).  score/gate optional (SSA). */
+/* One selection row: query block i of group g.  ls/li/tmp: scratch of T, T, W+1. */
+static void select_row(const float *a, const float *b1, const float *b2, int g, int i, int nblk,
+                       int dim, int kind, int layout, int causal, int topk, int sink,
+                       int32_t *sel, float *score_out, float *gate_out, float *ls, int *li,
+                       int *tmp) {
+  const int W = oracle_select_width(layout, nblk, topk, sink);
+  const int T = layout == 0 ? W - 1 : (layout == 2 ? W : W - 1 - (sink ? 1 : 0));
+  const float *A = a + (int64_t)g * nblk * dim;
+  const float *B1 = b1 + (int64_t)g * nblk * dim;
+  const float *B2 = b2 ? b2 + (int64_t)g * nblk * dim : NULL;
+  int n = 0; /* list length */
+  for (int j = 0; j < nblk && T > 0; ++j) {
+    int ok;
+    if (layout == 0)
+      ok = j != i && (!causal || j < i);
+    else
+      ok = j <= i;
+    if (!ok) continue;
+    const float s = score_of(kind, A + (int64_t)i * dim, B1 + (int64_t)j * dim,
+                             B2 ? B2 + (int64_t)j * dim : NULL, dim);
+    if (!(s > -INFINITY)) continue; /* -inf / NaN never rank */
+    if (n == T && !better(s, j, ls[T - 1], li[T - 1])) continue;
+    int pos = n < T ? n : T - 1;
+    while (pos > 0 && better(s, j, ls[pos - 1], li[pos - 1])) {
+      ls[pos] = ls[pos - 1];
+      li[pos] = li[pos - 1];
+      --pos;
+    }
+    ls[pos] = s;
+    li[pos] = j;
+    if (n < T) ++n;
+  }
+  int32_t *out = sel + ((int64_t)g * nblk + i) * W;
+  if (layout == 0) {
+    const float own = score_of(kind, A + (int64_t)i * dim, B1 + (int64_t)i * dim,
+                               B2 ? B2 + (int64_t)i * dim : NULL, dim);
+    const int64_t ob = ((int64_t)g * nblk + i) * W;
+    out[0] = i;
+    if (score_out) score_out[ob] = own;
+    if (gate_out) gate_out[ob] = logsigmoidf_(own);
+    for (int l = 0; l < T; ++l) {
+      const int valid = l < n;
+      out[1 + l] = valid ? li[l] : i;
+      const float sc = valid ? ls[l] : own;
+      if (score_out) score_out[ob + 1 + l] = sc;
+      if (gate_out) gate_out[ob + 1 + l] = logsigmoidf_(sc);
+    }
+  } else if (layout == 2) {
+    for (int l = 0; l < T; ++l) out[l] = l < n ? li[l] : -1;
+  } else {
+    for (int l = 0; l < T; ++l) tmp[l] = l < n ? li[l] : i;
+    tmp[T] = i;
+    if (sink) tmp[T + 1] = 0;
+    qsort(tmp, W, sizeof(int), cmp_int);
+    for (int l = 0; l < W; ++l) out[l] = tmp[l];
+  }
+}
+
+/* a, b1, b2: (G, nblk, dim) fp32.  sel: (G, nblk, W).  score/gate optional (SSA).
+ * rows: optional list of nrows query blocks (each computed for every group; the
+ * other rows of sel are left untouched); NULL = every row.  Rows are independent
+ * and run in parallel (OpenMP) with identical arithmetic per row. */
+void oracle_select_rows(const float *a, const float *b1, const float *b2, int G, int nblk, int dim,
+                        int kind, int layout, int causal, int topk, int sink, const int32_t *rows,
+                        int nrows, int32_t *sel, float *score_out, float *gate_out) {
+  const int W = oracle_select_width(layout, nblk, topk, sink);
+  const int T = layout == 0 ? W - 1 : (layout == 2 ? W : W - 1 - (sink ? 1 : 0));
+  const int R = rows ? nrows : nblk;
+  const int64_t total = (int64_t)G * R;
+#pragma omp parallel
+  {
+    float *ls = (float *)malloc(sizeof(float) * (T > 0 ? T : 1));
+    int *li = (int *)malloc(sizeof(int) * (T > 0 ? T : 1));
+    int *tmp = (int *)malloc(sizeof(int) * (W + 1));
+#pragma omp for schedule(dynamic, 16)
+    for (int64_t t = 0; t < total; ++t) {
+      const int g = (int)(t / R);
+      const int r = (int)(t % R);
+      const int i = rows ? rows[r] : r;
+      select_row(a, b1, b2, g, i, nblk, dim, kind, layout, causal, topk, sink, sel, score_out,
+                 gate_out, ls, li, tmp);
+    }
+    free(ls);
+    free(li);
+    free(tmp);
+  }
+}
+
 void oracle_select(const float *a, const float *b1, const float *b2, int G, int nblk, int dim,
                    int kind, int layout, int causal, int topk, int sink, int32_t *sel,
                    float *score_out, float *gate_out) {
-  const int W = oracle_select_width(layout, nblk, topk, sink);
-  const int T = layout == 0 ? W - 1 : (layout == 2 ? W : W - 1 - (sink ? 1 : 0));
-  float *ls = (float *)malloc(sizeof(float) * (T > 0 ? T : 1));
-  int *li = (int *)malloc(sizeof(int) * (T > 0 ? T : 1));
-  int *tmp = (int *)malloc(sizeof(int) * (W + 1));
-  for (int g = 0; g < G; ++g) {
-    const float *A = a + (int64_t)g * nblk * dim;
-    const float *B1 = b1 + (int64_t)g * nblk * dim;
-    const float *B2 = b2 ? b2 + (int64_t)g * nblk * dim : NULL;
-    for (int i = 0; i < nblk; ++i) {
-      int n = 0; /* list length */
-      for (int j = 0; j < nblk && T > 0; ++j) {
-        int ok;
-        if (layout == 0)
-          ok = j != i && (!causal || j < i);
-        else
-          ok = j <= i;
-        if (!ok) continue;
-        const float s = score_of(kind, A + (int64_t)i * dim, B1 + (int64_t)j * dim,
-                                 B2 ? B2 + (int64_t)j * dim : NULL, dim);
-        if (!(s > -INFINITY)) continue; /* -inf / NaN never rank */
-        if (n == T && !better(s, j, ls[T - 1], li[T - 1])) continue;
-        int pos = n < T ? n : T - 1;
-        while (pos > 0 && better(s, j, ls[pos - 1], li[pos - 1])) {
-          ls[pos] = ls[pos - 1];
-          li[pos] = li[pos - 1];
-          --pos;
-        }
-        ls[pos] = s;
-        li[pos] = j;
-        if (n < T) ++n;
-      }
-      int32_t *out = sel + ((int64_t)g * nblk + i) * W;
-      if (layout == 0) {
-        const float own = score_of(kind, A + (int64_t)i * dim, B1 + (int64_t)i * dim,
-                                   B2 ? B2 + (int64_t)i * dim : NULL, dim);
-        const int64_t ob = ((int64_t)g * nblk + i) * W;
-        out[0] = i;
-        if (score_out) score_out[ob] = own;
-        if (gate_out) gate_out[ob] = logsigmoidf_(own);
-        for (int l = 0; l < T; ++l) {
-          const int valid = l < n;
-          out[1 + l] = valid ? li[l] : i;
-          const float sc = valid ? ls[l] : own;
-          if (score_out) score_out[ob + 1 + l] = sc;
-          if (gate_out) gate_out[ob + 1 + l] = logsigmoidf_(sc);
-        }
-      } else if (layout == 2) {
-        for (int l = 0; l < T; ++l) out[l] = l < n ? li[l] : -1;
-      } else {
-        for (int l = 0; l < T; ++l) tmp[l] = l < n ? li[l] : i;
-        tmp[T] = i;
-        if (sink) tmp[T + 1] = 0;
-        qsort(tmp, W, sizeof(int), cmp_int);
-        for (int l = 0; l < W; ++l) out[l] = tmp[l];
-      }
-    }
-  }
-  free(ls);
-  free(li);
-  free(tmp);
+  oracle_select_rows(a, b1, b2, G, nblk, dim, kind, layout, causal, topk, sink, NULL, 0, sel,
+                     score_out, gate_out);
 }
 
-/* 1 when slot `slot` of `row` is attended under the mask rules, else 0. */
 static int slot_active(const int32_t *row, int slot, int qblk, int nblk, int mask_mode, int causal) {
   const int kb = row[slot];
   if (kb < 0 || kb >= nblk) return 0;

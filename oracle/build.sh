@@ -3,5 +3,5 @@
 set -e
 HERE=$(cd "$(dirname "$0")" && pwd)
 mkdir -p "$HERE/_build"
-gcc -O2 -ffp-contract=off -fPIC -shared -o "$HERE/_build/libbsa_oracle.so" "$HERE/bsa_oracle.c" -lm
+gcc -O2 -ffp-contract=off -fopenmp -fPIC -shared -o "$HERE/_build/libbsa_oracle.so" "$HERE/bsa_oracle.c" -lm
 echo "$HERE/_build/libbsa_oracle.so"

@@ -145,6 +145,19 @@ def test_backward_is_deterministic_with_hub_blocks(cuda):
     _cmp(r1[2], rv, torch.bfloat16, "dv")
 
 
+def test_backward_with_saved_lse_equals_recompute(cuda):
+    """bsattn_backward(..., lse=) with the (o, lse) of bsattn_forward_lse gives the
+    same gradients, bit for bit, as the recomputing form."""
+    import triton_kernel as tk
+    q, k, v, do, sel, gate = _random_case(1, 2, 2048, 64, 64, 7, torch.bfloat16, cuda, 12)
+    o, lse = tk.bsattn_forward_lse(q, k, v, sel, gate, causal=True)
+    a = tk.bsattn_backward(q, k, v, sel, o, do, gate, causal=True, lse=lse)
+    b = tk.bsattn_backward(q, k, v, sel, None, do, gate, causal=True)
+    assert torch.equal(o, tk.bsattn_forward(q, k, v, sel, gate, causal=True))
+    for x, y in zip(a, b):
+        assert torch.equal(x, y)
+
+
 def test_strided_inputs_read_in_place(cuda):
     """q/k/v as transposed views of a (B, L, 3, H, D) projection (no copies)."""
     import triton_kernel as tk
