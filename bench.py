@@ -13,6 +13,15 @@ per second, timed on the device as the max over ranks.
     python bench.py --config {2,3b,4,5} [--n N]     the other BASELINE configurations
                                                    (one JSON line each, not the driver line)
 
+The driver line also carries two sub-objects timed in the same run (max over
+ranks, strong scaling):
+  qsharded_262k  the same 262k step with the sequence split by query blocks
+                 (NCCL all-gathers of K, V, the pooled summaries and the
+                 selection rows; fp32 reduce-scatter of dK/dV);
+  long_fwd       BASELINE config 3b at 16M tokens (block 128, forward only),
+                 query-block sharded, with the peak allocation beside the size an
+                 nblk x nblk score matrix would take.
+
 --impl reference times the CPU restatement of the reference's gather path
 (oracle/, the reference is Python and cannot be installed on the GPU box) on
 a bounded sample of the same workload, with all host threads.
@@ -35,9 +44,13 @@ for _p in (ROOT, PKG):
 import torch  # noqa: E402
 
 METRIC = "fwd+bwd tokens/s at 262k tok (selection+forward+backward)"
-# DRAM bytes per launch of each phase at N=262144, from the ncu launch list in
-# profiles/launches_bench262k.md (attn_bwd = dK/dV + dQ + reduce + CSR kernels).
-TRAFFIC_262K = {"attn_bwd": 9.07e9, "attn_fwd": 1.164e9, "select": 0.564e9}
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per step of each phase
+# at N=262144, summed over the phase's kernels in one ncu launch-list capture of
+# this bench (cold cache), and the source revision that capture was taken at.
+# A recorded figure, not measured by this run: it is printed with its revision so
+# that a stale figure is visible.
+TRAFFIC_262K = {"attn_bwd": None, "attn_fwd": None, "select": None}
+TRAFFIC_REV = None
 UNIT = "tokens/s"
 
 
@@ -55,6 +68,16 @@ def workload(a):
     cfg["nblk"] = cfg["N"] // cfg["bs"]
     cfg["kk"] = cfg["topk"] + 1
     return cfg
+
+
+def config_dict(cfg, world):
+    """The `config` object of the driver line (identical in both arms)."""
+    return {"workload": "BASELINE config 3a: selection+fwd+bwd, B1 H8 N%d D64 block64 top16 (+own) "
+                        "causal" % cfg["N"],
+            "B": cfg["B"], "H": cfg["H"], "N": cfg["N"], "D": cfg["D"], "block": cfg["bs"],
+            "kk": cfg["kk"], "parallelism": "heads sharded %d/rank" % (cfg["H"] // world),
+            "l2": "256 MB buffer written between timed steps; inputs %.0f MB per rank"
+                  % (4 * cfg["B"] * (cfg["H"] // world) * cfg["N"] * cfg["D"] * 2 / 1e6)}
 
 
 def flops(cfg, heads):
@@ -289,24 +312,28 @@ def run_ours(a):
         dom = max(phases, key=lambda n: phases[n]["ms"])
         dom_fl = {"select": f_sel, "attn_fwd": f_fwd, "attn_bwd": f_bwd}[dom]
         achieved = dom_fl / (phases[dom]["ms"] * 1e-3) / 1e12
+        # a phase of a few ms runs at full clocks: the burst figure is its peak
+        peak, peak_name = (tf_burst, "bf16_tflops") if phases[dom]["ms"] < 10 else \
+            (tf_sus, "bf16_tflops_sustained")
+        for name in phases:
+            phases[name]["frac_tensor"] = round(phases[name]["tflops"] / peak, 4)
         line = {
             "metric": METRIC, "value": round(tokens / (ms_step * 1e-3), 1), "unit": UNIT,
             "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": round(ms_step, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic N(0,1), seeded",
-            "config": {"workload": "BASELINE config 3a: selection+fwd+bwd, B1 H8 N%d D64 block64 "
-                                   "top16 (+own) causal" % cfg["N"],
-                       "B": cfg["B"], "H": cfg["H"], "N": cfg["N"], "D": cfg["D"], "block": cfg["bs"],
-                       "kk": cfg["kk"], "parallelism": "heads sharded %d/rank" % heads,
-                       "l2": "256 MB buffer written between timed steps; inputs %.0f MB per rank"
-                             % (4 * q.numel() * 2 / 1e6)},
+            "config": config_dict(cfg, world),
             "roofline": {"kernel": dom, "bound": "tensor", "achieved": round(achieved, 2),
-                         "peak": tf_sus, "unit": "TFLOP/s", "frac": round(achieved / tf_sus, 4),
-                         "peak_source": "%s bf16_tflops_sustained" % src,
+                         "peak": peak, "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                         "peak_source": "%s %s (phase of %.2f ms: %s)" % (
+                             src, peak_name, phases[dom]["ms"],
+                             "burst figure, under 10 ms" if peak_name == "bf16_tflops"
+                             else "sustained figure"),
                          "traffic": TRAFFIC_262K.get(dom) if cfg["N"] == 262144 else None,
-                         "traffic_source": "ncu dram__bytes_read+write summed over the phase's "
-                                           "kernels, one capture, cold cache "
-                                           "(profiles/launches_bench262k.md)"},
+                         "traffic_source": ("ncu dram__bytes_read+write summed over the phase's "
+                                            "kernels, one launch-list capture of this bench at "
+                                            "revision %s" % TRAFFIC_REV) if TRAFFIC_REV else
+                                           "not captured for this revision"},
             "phases": phases,
             "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 1), "unit": UNIT,
                     "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d * world,
@@ -315,11 +342,136 @@ def run_ours(a):
             "launches_per_step": nlaunch,
             "clocks": clk.summary(),
         }
+    del q, k, v, do
+    torch.cuda.empty_cache()
+    extra = {}
+    if not a.no_qsharded:
+        extra["qsharded_262k"] = run_qsharded(a, dist, world, rank, dev, flush)
+    if not a.no_long:
+        extra["long_fwd"] = run_long_fwd(a, dist, world, rank, dev, flush)
+    if rank == 0:
+        line.update(extra)
         if world == 1 and not a.no_cpu:
             line["cpu_baseline"] = cpu_baseline(cfg, a.cpu_sample)
         print(json.dumps(line), flush=True)
     if dist:
         dist.destroy_process_group()
+
+
+def _phase_loop(fn, nph, steps, warmup, flush, dist, dev):
+    """Runs fn(events) warmup + steps times (fn records nph + 1 events), flushing L2
+    before every timed step; returns the mean ms per phase, max over ranks."""
+    for _ in range(warmup):
+        fn(None)
+    torch.cuda.synchronize()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(nph + 1)] for _ in range(steps)]
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    for i in range(steps):
+        flush.zero_()
+        fn(evs[i])
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    ms = [statistics.mean(e[j].elapsed_time(e[j + 1]) for e in evs) for j in range(nph)]
+    vals = torch.tensor([sum(ms)] + ms, device=dev)
+    if dist:
+        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
+    return vals.tolist()
+
+
+def run_qsharded(a, dist, world, rank, dev, flush):
+    """The north-star step with the sequence split by query blocks (the layout of
+    sequence-parallel training): rank r holds the Q, K, V, dO rows of its
+    contiguous query blocks.  One step = NCCL all-gather of K, V + selection
+    (pooled-summary all-gathers, equal-area selection rows, row exchange) +
+    forward over the local query blocks + backward + the fp32 reduce-scatter of
+    the dK/dV partials.  Same total work at every N (strong scaling)."""
+    import sharded
+    import _bsa
+    B, H, N, D, bs, topk = 1, 8, a.n, 64, 64, 16
+    if N % (world * bs):
+        return {"skipped": "N not divisible by world * block"}
+    Ls = N // world
+    g = torch.Generator(device=dev).manual_seed(900 + rank)
+    q, k, v, do = (torch.randn(B, H, Ls, D, generator=g, device=dev).to(torch.bfloat16)
+                   for _ in range(4))
+    m = sharded.ShardedBlockSparse(bs=bs, topk=topk, causal=True)
+    a0 = rank * (Ls // bs)
+
+    def fn(ev):
+        if ev:
+            ev[0].record()
+        kf, vf = m.gather_kv(k, v)
+        sel = m.select(q, k)
+        if ev:
+            ev[1].record()
+        o, lse = _bsa.attn_fwd(q, kf, vf, sel, None, bs=bs, causal=True, q_blk0=a0)
+        if ev:
+            ev[2].record()
+        m.backward(q, o, do, (kf, vf, sel, lse))
+        if ev:
+            ev[3].record()
+    ms, ms_sel, ms_fwd, ms_bwd = _phase_loop(fn, 3, a.steps_sub, max(3, a.warmup // 2), flush, dist,
+                                             dev)
+    return {"N": N, "ms_per_step": round(ms, 4), "tokens_per_s": round(B * N / (ms * 1e-3), 1),
+            "phases_ms_max_over_ranks": {"gather_kv+select": round(ms_sel, 4),
+                                         "attn_fwd": round(ms_fwd, 4),
+                                         "attn_bwd+reduce_scatter": round(ms_bwd, 4)},
+            "parallelism": "query blocks sharded %d/rank (NCCL all-gather K, V, pooled summaries, "
+                           "selection rows; reduce-scatter dK/dV fp32)" % (N // bs // world),
+            "scaling": "strong", "steps": a.steps_sub}
+
+
+def run_long_fwd(a, dist, world, rank, dev, flush):
+    """BASELINE config 3b at N = --long-n (16M by default): forward only, block 128,
+    top-16 + own, query blocks sharded over the ranks (one NCCL all-gather of K and
+    V, all-gathers of the pooled summaries and of the selection rows), the causal
+    top-k streamed through the tensor-core selector so that no nblk x nblk score
+    matrix is ever stored.  Same total work at every N (strong scaling)."""
+    import sharded
+    import _bsa
+    B, H, N, D, bs, topk = 1, 8, a.long_n, 64, 128, 16
+    if N % (world * bs):
+        return {"skipped": "N not divisible by world * block"}
+    Ls = N // world
+    nblk = N // bs
+    g = torch.Generator(device=dev).manual_seed(700 + rank)
+    q, k, v = (torch.randn(B, H, Ls, D, generator=g, device=dev).to(torch.bfloat16)
+               for _ in range(3))
+    m = sharded.ShardedBlockSparse(bs=bs, topk=topk, causal=True)
+    a0 = rank * (Ls // bs)
+    torch.cuda.synchronize()
+    base = torch.cuda.memory_allocated(dev)
+    torch.cuda.reset_peak_memory_stats(dev)
+
+    def fn(ev):
+        if ev:
+            ev[0].record()
+        kf, vf = m.gather_kv(k, v)
+        if ev:
+            ev[1].record()
+        sel = m.select(q, k)
+        if ev:
+            ev[2].record()
+        _bsa.attn_fwd(q, kf, vf, sel, None, bs=bs, causal=True, want_lse=False, q_blk0=a0)
+        if ev:
+            ev[3].record()
+    ms, ms_kv, ms_sel, ms_fwd = _phase_loop(fn, 3, a.steps_long, 3, flush, dist, dev)
+    peak = torch.cuda.max_memory_allocated(dev) - base
+    fwd_flops = 4.0 * B * H * N * (topk + 1) * bs * D
+    score_bytes = 4.0 * nblk * nblk * H / world
+    return {"N": N, "ms_per_step": round(ms, 3), "tokens_per_s": round(B * N / (ms * 1e-3), 1),
+            "phases_ms_max_over_ranks": {"gather_kv": round(ms_kv, 3), "select": round(ms_sel, 3),
+                                         "attn_fwd": round(ms_fwd, 3)},
+            "attn_fwd_tflops_per_gpu": round(fwd_flops / world / (ms_fwd * 1e-3) / 1e12, 1),
+            "peak_extra_alloc_bytes_per_rank": int(peak),
+            "score_matrix_bytes_per_rank_if_stored": int(score_bytes),
+            "score_matrix_stored": bool(peak >= score_bytes),
+            "parallelism": "query blocks sharded %d/rank" % (nblk // world),
+            "config": "B1 H8 D64 block128 top16 (+own) causal bf16, forward only",
+            "scaling": "strong", "steps": a.steps_long}
 
 
 # ---------------------------------------------------------------- CPU baseline
@@ -391,18 +543,23 @@ def run_reference(a):
     t = statistics.mean(ts)
     value = smp.tokens() / t
     cores = torch.get_num_threads()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    frac = smp.S / cfg["nblk"]
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 1), "unit": UNIT,
-        "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": a.steps, "warmup": a.warmup,
-        "ms_per_step": round(cfg["B"] * cfg["N"] / value * 1e3, 2), "higher_is_better": True,
+        "n_gpus": world, "steps": a.steps, "warmup": a.warmup,
+        "ms_per_step": round(t * 1e3, 2), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32 (bf16-rounded inputs)",
         "data": "synthetic N(0,1), seeded",
-        "config": {"workload": "BASELINE config 3a: selection+fwd+bwd, B1 H8 N%d D64 block64 "
-                               "top16 (+own) causal" % cfg["N"], "N": cfg["N"], "block": cfg["bs"],
-                   "kk": cfg["kk"]},
+        "config": config_dict(cfg, world),
+        "sample_fraction": round(frac, 6),
+        "sample": "each step = the last %d of %d query blocks of all %d heads (%d tokens) through "
+                  "selection + gather fwd + autograd bwd; ms_per_step is that sample's measured "
+                  "time, value = its tokens / time (the per-block cost does not depend on the "
+                  "position)" % (smp.S, cfg["nblk"], cfg["H"], smp.tokens()),
         "cpu_baseline": {"value": round(value, 1), "unit": UNIT, "cores": cores, "kind": "port",
                          "sample": "%d query blocks x %d heads per step (%d tokens), mean of %d "
-                                   "steps" % (a.ref_sample, cfg["H"], smp.tokens(), a.steps)},
+                                   "steps" % (smp.S, cfg["H"], smp.tokens(), a.steps)},
         "e2e": {"value": round(value, 1), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
@@ -437,6 +594,10 @@ def _line(metric, value, unit, ms, a, world, scaling, dtype, config, roofline, c
 
 
 def _roof(name, fl, ms, peak, src):
+    """peak: the sustained figure; phases under 10 ms are rated against the burst one."""
+    _, tf_burst, _, kind = load_peaks()
+    if ms < 10:
+        peak, src = tf_burst, "%s bf16_tflops (burst figure: phase of %.2f ms)" % (kind, ms)
     ach = fl / (ms * 1e-3) / 1e12
     return {"kernel": name, "bound": "tensor", "achieved": round(ach, 2), "peak": peak,
             "unit": "TFLOP/s", "frac": round(ach / peak, 4), "peak_source": src, "traffic": None}
@@ -612,6 +773,11 @@ def main():
     ap.add_argument("--ref-sample", type=int, default=256,
                     help="query blocks per step of the --impl reference arm")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    ap.add_argument("--no-long", action="store_true", help="skip the long_fwd (16M) sub-object")
+    ap.add_argument("--no-qsharded", action="store_true", help="skip the qsharded_262k sub-object")
+    ap.add_argument("--long-n", type=int, default=1 << 24, help="tokens of the long_fwd sub-object")
+    ap.add_argument("--steps-long", type=int, default=5, help="timed steps of long_fwd")
+    ap.add_argument("--steps-sub", type=int, default=10, help="timed steps of qsharded_262k")
     ap.add_argument("--config", default="3a", choices=["3a", "2", "3b", "4", "5"],
                     help="BASELINE configuration (3a = the driver line)")
     a = ap.parse_args()

@@ -84,6 +84,27 @@ bsa_status make_tmap(TensorMap4 *out, const void *ptr, int dtype, int B, int H, 
   return BSA_OK;
 }
 
+bsa_status make_tmap_f32_rows(CUtensorMap *out, const float *ptr, int G, int rows, int dim,
+                              int box_rows, const char *name) {
+  if (reinterpret_cast<uintptr_t>(ptr) % 16 || dim % 4)
+    return fail(BSA_ERR_STRIDE, std::string(name) + ": needs a 16-byte aligned base and dim % 4 == 0");
+  auto enc = get_encode();
+  if (!enc) return fail(BSA_ERR_LAUNCH, "cuTensorMapEncodeTiled unavailable");
+  cuuint64_t gdim[3] = {(cuuint64_t)dim, (cuuint64_t)rows, (cuuint64_t)G};
+  cuuint64_t gstride[2] = {(cuuint64_t)dim * 4, (cuuint64_t)dim * 4 * (cuuint64_t)rows};
+  cuuint32_t box[3] = {32u, (cuuint32_t)box_rows, 1u};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float *>(ptr), gdim, gstride,
+                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[160];
+    snprintf(buf, sizeof buf, "%s: cuTensorMapEncodeTiled failed (%d)", name, (int)r);
+    return fail(BSA_ERR_STRIDE, buf);
+  }
+  return BSA_OK;
+}
+
 }  // namespace bsa
 
 extern "C" const char *bsa_last_error(void) { return bsa::g_last_error.c_str(); }

@@ -32,4 +32,10 @@ struct TensorMap4 {
 bsa_status make_tmap(TensorMap4 *out, const void *ptr, int dtype, int B, int H, int L, int D,
                      int64_t sb, int64_t sh, int64_t sl, int rows, const char *name);
 
+// Encodes a 3-D tiled tensor map over a contiguous fp32 (G, rows, dim) array
+// with a box of 32 columns (128 bytes) x `box_rows` rows x 1 and 128-byte
+// swizzle; rows past `rows` read as zero.  dim must be a multiple of 4.
+bsa_status make_tmap_f32_rows(CUtensorMap *out, const float *ptr, int G, int rows, int dim,
+                              int box_rows, const char *name);
+
 }  // namespace bsa

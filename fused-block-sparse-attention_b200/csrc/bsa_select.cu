@@ -333,9 +333,8 @@ __global__ void __launch_bounds__(256) select_kernel(const bsa_select_args a, in
   }
 }
 
-bool select_tc_applicable(const bsa_select_args *a, int T);
-size_t select_tc_workspace(const bsa_select_args *a);
-bsa_status run_select_tc(const bsa_select_args *a, int T, int W, void *ws, cudaStream_t st);
+bool select_tc5_applicable(const bsa_select_args *a, int T);
+bsa_status run_select_tc5(const bsa_select_args *a, int T, int W, cudaStream_t st);
 
 int32_t select_width(const bsa_select_args *a) {
   if (a->layout == BSA_SEL_SSA) return 1 + std::max(0, std::min(a->topk, a->nblk - 1));
@@ -361,17 +360,9 @@ bsa_status run_select(const bsa_select_args *a, cudaStream_t st) {
   const int nq = a->nq > 0 ? a->nq : a->nblk;
   if (a->q_blk0 < 0 || a->nq < 0 || (long long)a->q_blk0 + nq > a->nblk)
     return fail(BSA_ERR_SHAPE, "select: query range outside [0, nblk)");
-  if (select_tc_applicable(a, T)) {
-    // tensor-core scoring with exact certification; its scratch (a few bytes per
-    // query row) comes from the stream-ordered pool and is released on the stream
-    void *ws = nullptr;
-    const size_t bytes = select_tc_workspace(a);
-    if (cudaMallocAsync(&ws, bytes, st) != cudaSuccess)
-      return fail(BSA_ERR_LAUNCH, "select: scratch allocation failed");
-    const bsa_status s = run_select_tc(a, T, W, ws, st);
-    cudaFreeAsync(ws, st);
-    return s;
-  }
+  // large DOT selections: tcgen05 approximate scores + exact re-scoring
+  // (bsa_select_tc5.cu), bit-identical to the kernel below
+  if (select_tc5_applicable(a, T)) return run_select_tc5(a, T, W, st);
   const int ntiles = (nq + kTile - 1) / kTile;
   const size_t smem = (size_t)(a->dim * kLdA + 2 * kDC * kLdA + kTile * 65) * 4;
   dim3 grid(ntiles, a->G);

@@ -8,15 +8,26 @@ produces them).
 
   forward   1. all-gather K and V into local HBM (sequence-major buffers, so the
                gathered tensor is a strided (B, H, L, D) view with no copy);
-            2. pool this rank's K blocks (mean, fp32) and all-gather the pooled
-               summaries (nblk x D per head, small);
-            3. select: this rank's pooled queries against every key block,
-               causal top-k with the own block first (bsa_select with a query
-               range);
-            4. attention over the local query blocks (bsa_attn_fwd with q_blk0).
+            2. pool this rank's Q and K blocks (mean, fp32) and all-gather both
+               pooled summaries (nblk x D per head, small);
+            3. select: causal selection costs grow with the query position, so
+               the selection rows are split by equal causal area instead
+               (select_ranges: rank r scores query blocks [s_r, e_r) against
+               every earlier key block, one tcgen05 selection call with a query
+               range), and the rows are returned to their owners by one
+               all-gather of the int32 selection (a few bytes per row);
+            4. attention over the local query blocks (bsa_attn_fwd with q_blk0);
+               with kk blocks per query block the attention itself is balanced.
   backward  dQ stays local; dK/dV are this rank's contributions over the whole
             sequence, summed across ranks and returned to their owners by one
-            reduce_scatter (fp32 accumulation).
+            reduce_scatter.  The per-rank partials come out of the backward in
+            the input dtype (bf16): each is rounded once (relative 2^-9) before
+            the fp32 sum, so the summed dK/dV carry at most that rounding of
+            each rank's share, the same order as the single-GPU result's own
+            final rounding to bf16.
+
+A process group is optional: without an initialised torch.distributed (one
+GPU) every collective is the identity and the ranges cover the whole sequence.
 
 No kernel reads another GPU's memory: every collective lands in local HBM
 before a kernel touches it.  The reference has no multi-GPU path; this is the
@@ -31,7 +42,7 @@ import torch.distributed as dist
 
 import _bsa
 
-__all__ = ["block_ranges", "CudaOps", "ShardedBlockSparse"]
+__all__ = ["block_ranges", "select_ranges", "CudaOps", "ShardedBlockSparse"]
 
 
 def block_ranges(nblk, world):
@@ -40,6 +51,32 @@ def block_ranges(nblk, world):
         raise ValueError("nblk (%d) must be a multiple of the world size (%d)" % (nblk, world))
     n = nblk // world
     return [(r * n, (r + 1) * n) for r in range(world)]
+
+
+def select_ranges(nblk, world, causal=True, align=128):
+    """Query-block ranges [(s_r, e_r)] for the selection step.  Causal row i scores
+    i key blocks, so the ranges split the triangle sum_{i<e} (i + 1) into equal
+    areas (boundaries rounded to multiples of `align` blocks, the selection
+    kernel's query tile, when that keeps every range non-empty); non-causal rows
+    cost the same and the ranges are the contiguous block_ranges."""
+    if not causal or world == 1:
+        return block_ranges(nblk, world)
+    total = nblk * (nblk + 1) / 2.0
+    cuts = [0]
+    for r in range(1, world):
+        # e with e (e + 1) / 2 = r / world * total
+        e = int(round(((1 + 8.0 * total * r / world) ** 0.5 - 1) / 2))
+        if align > 1 and nblk >= 16 * align * world:
+            e = int(round(e / align)) * align
+        cuts.append(min(max(e, cuts[-1] + 1), nblk - (world - r)))
+    cuts.append(nblk)
+    return [(cuts[r], cuts[r + 1]) for r in range(world)]
+
+
+def _world(group):
+    if not dist.is_available() or not dist.is_initialized():
+        return 1, 0
+    return dist.get_world_size(group), dist.get_rank(group)
 
 
 class CudaOps:
@@ -69,7 +106,9 @@ class CudaOps:
 def _gather_rows(x, group):
     """x: (n, ...) this rank's rows -> (world * n, ...) in rank order, in a new
     contiguous buffer (one all_gather_into_tensor)."""
-    world = dist.get_world_size(group)
+    world, _ = _world(group)
+    if world == 1:
+        return x.contiguous()
     out = torch.empty((world * x.shape[0],) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
     dist.all_gather_into_tensor(out, x.contiguous(), group=group)
     return out
@@ -78,7 +117,9 @@ def _gather_rows(x, group):
 def _reduce_scatter_rows(x, group):
     """x: (world * n, ...) per-rank partial sums -> this rank's (n, ...) slice of
     the sum over ranks (one reduce_scatter_tensor)."""
-    world = dist.get_world_size(group)
+    world, _ = _world(group)
+    if world == 1:
+        return x.contiguous()
     out = torch.empty((x.shape[0] // world,) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
     dist.reduce_scatter_tensor(out, x.contiguous(), group=group)
     return out
@@ -104,8 +145,7 @@ class ShardedBlockSparse:
         self.ops = ops if ops is not None else CudaOps()
 
     def _geometry(self, q):
-        world = dist.get_world_size(self.group)
-        rank = dist.get_rank(self.group)
+        world, rank = _world(self.group)
         Ls = q.shape[2]
         if Ls % self.bs:
             raise ValueError("shard length (%d) must be a multiple of the block size" % Ls)
@@ -119,12 +159,27 @@ class ShardedBlockSparse:
             _bhld(_gather_rows(_seq_major(v), self.group))
 
     def select(self, q, k):
-        """This rank's selection rows (B, H, nq, 1 + min(topk, nblk-1)), int32."""
+        """This rank's selection rows (B, H, nq, 1 + min(topk, nblk-1)), int32,
+        computed over the equal-area ranges of select_ranges and exchanged."""
         world, rank, nblk, a = self._geometry(q)
-        qp = self.ops.pool(q, self.bs)                        # (B, H, nq, D) fp32
+        nq = q.shape[2] // self.bs
+        qp_local = self.ops.pool(q, self.bs)                  # (B, H, nq, D) fp32
         kp_local = self.ops.pool(k, self.bs)
         kp = _bhld(_gather_rows(_seq_major(kp_local), self.group)).contiguous()
-        return self.ops.select(qp, kp, topk=self.topk, causal=self.causal, q_blk0=a)
+        if world == 1 or not self.causal:
+            return self.ops.select(qp_local, kp, topk=self.topk, causal=self.causal, q_blk0=a)
+        qp = _bhld(_gather_rows(_seq_major(qp_local), self.group))
+        ranges = select_ranges(nblk, world, self.causal)
+        s0, s1 = ranges[rank]
+        mine = self.ops.select(qp[:, :, s0:s1].contiguous(), kp, topk=self.topk,
+                               causal=self.causal, q_blk0=s0)     # (B, H, s1 - s0, W)
+        width = max(e - b for b, e in ranges)
+        pad = torch.zeros(mine.shape[0], mine.shape[1], width, mine.shape[3], dtype=mine.dtype,
+                          device=mine.device)
+        pad[:, :, :s1 - s0] = mine
+        every = _gather_rows(_seq_major(pad), self.group)      # (world * width, B, H, W)
+        rows = torch.cat([every[r * width:r * width + (e - b)] for r, (b, e) in enumerate(ranges)])
+        return _bhld(rows[a:a + nq]).contiguous()
 
     def forward(self, q, k, v):
         """Returns (o, ctx): o is this rank's (B, H, Ls, D) output; ctx carries what

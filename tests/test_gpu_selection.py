@@ -297,30 +297,59 @@ def test_other_selectors_golden(cuda):
     assert np.array_equal(r.cpu().numpy(), O.select_scores(draws.cpu(), topk=topk))
 
 
-@pytest.mark.parametrize("layout,causal,topk,dim", [(O.SEL_SSA, True, 16, 64), (O.SEL_SSA, False, 8, 128),
-                                                    (O.SEL_FINISH, True, 12, 64), (O.SEL_RAW, True, 16, 128)])
-def test_select_tensor_core_path_exact_with_ties(cuda, monkeypatch, layout, causal, topk, dim):
-    """The tf32 tensor-core scoring path (opt-in, BSA_SELECT_TC=1) must give the exact
-    fp32 selection: checked against the oracle and against the SIMT kernel, on data
-    with many exactly tied scores (repeated key summaries) that force the exact
-    fallback."""
+@pytest.mark.parametrize("layout,causal,topk,dim,nblk", [(O.SEL_SSA, True, 16, 64, 700),
+                                                         (O.SEL_SSA, False, 8, 64, 600),
+                                                         (O.SEL_SSA, True, 32, 32, 1100),
+                                                         (O.SEL_FINISH, True, 12, 64, 700),
+                                                         (O.SEL_RAW, True, 16, 32, 520),
+                                                         (O.SEL_SSA, True, 1, 64, 2000)])
+def test_select_tensor_core_path_exact_with_ties(cuda, monkeypatch, layout, causal, topk, dim, nblk):
+    """The tcgen05 tf32 scoring path (default for DOT scores at nblk >= 512) must give
+    the exact fp32 selection: checked against the oracle and against the SIMT kernel
+    (BSA_SELECT_SIMT=1), on data with many exactly tied scores (repeated key
+    summaries) and a group of huge-norm summaries, at every key-split width."""
     import _bsa
-    gen = torch.Generator().manual_seed(topk + dim)
-    G, nblk = 4, 700
+    gen = torch.Generator().manual_seed(topk + dim + nblk)
+    G = 5
     a = torch.randn(G, nblk, dim, generator=gen)
     b = torch.randn(G, nblk, dim, generator=gen)
     b[1] = b[1, :1]                       # group 1: every key summary identical (all ties)
     b[2, ::3] = b[2, 5]                   # group 2: a third of the keys identical
-    args = dict(kind=_bsa.SCORE_DOT, layout=layout, causal=causal, topk=topk, want_score=layout == 0)
-    s_simt, sc_simt, _ = _bsa.select(a.to(cuda), b.to(cuda), **args)
-    monkeypatch.setenv("BSA_SELECT_TC", "1")
-    s_tc, sc_tc, _ = _bsa.select(a.to(cuda), b.to(cuda), **args)
-    o_sel, o_sc, _ = O.select(a, b, kind=O.SCORE_DOT, layout=layout, causal=causal, topk=topk,
-                              want_score=layout == 0)
-    assert np.array_equal(s_tc.cpu().numpy(), o_sel)
-    assert torch.equal(s_tc, s_simt)
-    if layout == 0:
-        assert np.array_equal(sc_tc.cpu().numpy(), o_sc)
+    a[3] *= 1e4                           # group 3: large scores, small relative gaps
+    b[3] = b[3] * 1e-3 + 1.0
+    args = dict(kind=_bsa.SCORE_DOT, layout=layout, causal=causal, topk=topk, want_score=layout == 0,
+                want_gate=layout == 0)
+    o_sel, o_sc, o_gt = O.select(a, b, kind=O.SCORE_DOT, layout=layout, causal=causal, topk=topk,
+                                 want_score=layout == 0, want_gate=layout == 0)
+    monkeypatch.setenv("BSA_SELECT_SIMT", "1")
+    s_simt, _, _ = _bsa.select(a.to(cuda), b.to(cuda), **args)
+    monkeypatch.delenv("BSA_SELECT_SIMT")
+    monkeypatch.setenv("BSA_SELECT_TC5", "1")
+    assert np.array_equal(s_simt.cpu().numpy(), o_sel)
+    for split in ("", "1", "2", "8"):
+        if split:
+            monkeypatch.setenv("BSA_SELECT_SPLIT", split)
+        s_tc, sc_tc, gt_tc = _bsa.select(a.to(cuda), b.to(cuda), **args)
+        _bsa.check_status(cuda)
+        assert np.array_equal(s_tc.cpu().numpy(), o_sel), "split %s" % split
+        if layout == 0:
+            assert np.array_equal(sc_tc.cpu().numpy(), o_sc)
+            assert np.allclose(gt_tc.cpu().numpy(), o_gt, atol=1e-6, rtol=1e-6)
+
+
+def test_select_tensor_core_path_query_range(cuda, monkeypatch):
+    """The tcgen05 selection on a query-block range (the sharded layout) equals the
+    rows of the whole-sequence selection."""
+    import _bsa
+    monkeypatch.setenv("BSA_SELECT_TC5", "1")
+    gen = torch.Generator().manual_seed(77)
+    nblk, dim = 3000, 64
+    a = torch.randn(2, nblk, dim, generator=gen).to(cuda)
+    b = torch.randn(2, nblk, dim, generator=gen).to(cuda)
+    full, _, _ = _bsa.select(a, b, topk=16)
+    for q0, nq in ((0, 1000), (1000, 1000), (2000, 1000), (1234, 777)):
+        part, _, _ = _bsa.select(a[:, q0:q0 + nq].contiguous(), b, topk=16, q_blk0=q0)
+        assert torch.equal(part, full[:, q0:q0 + nq])
 
 
 def test_centroid_module_matches_oracle_attention(cuda, monkeypatch):
