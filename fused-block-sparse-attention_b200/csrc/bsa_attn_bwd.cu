@@ -149,20 +149,25 @@ __global__ void chunk_bin_kernel(const unsigned long long *plan, int nbins, int3
   }
 }
 
-// Sort keys of the chunks for the tcgen05 dK/dV kernel: C - entries (largest
-// first), slots past the chunk count last.  Pairing chunks of equal size keeps
-// both tiles of a work unit busy on every step.
+// Sort keys of the chunks for the tcgen05 dK/dV kernel: (head group, then
+// C - entries), slots past the chunk count last.  Within one (batch, selection
+// head) group the chunks run largest first, so the two chunks of a work unit
+// have equal size and both tiles stay busy on every step; the groups run one
+// after another, so the query rows that the concurrently running units gather
+// (Q, dO, lse, Dvec of one head: 64 MB at 262k tokens) stay in L2 instead of
+// spanning every head at once.
 __global__ void chunk_key_kernel(const unsigned long long *plan, const int32_t *row_ptr,
-                                 const int32_t *chunk_bin, int nbins, int C, int ncap,
+                                 const int32_t *chunk_bin, int nbins, int nblk, int C, int ncap,
                                  int32_t *key, int32_t *val) {
   const unsigned total = (unsigned)(plan[nbins] >> 32);
+  const int ngroups = nbins / nblk;
   for (int x = blockIdx.x * blockDim.x + threadIdx.x; x < ncap; x += gridDim.x * blockDim.x) {
-    int k = C + 1;
+    int k = ngroups * (C + 2);
     if ((unsigned)x < total) {
       const int bin = chunk_bin[x];
       const int cidx = x - (int)(plan[bin] >> 32);
       const int e0 = row_ptr[bin] + cidx * C;
-      k = C - (min(row_ptr[bin + 1], e0 + C) - e0);
+      k = (bin / nblk) * (C + 2) + C - (min(row_ptr[bin + 1], e0 + C) - e0);
     }
     key[x] = k;
     val[x] = x;
@@ -1017,7 +1022,8 @@ static size_t bwd_layout(const bsa_attn_args *a, BwdWs *w, uint8_t *base) {
   w->chunk_bin = (int32_t *)take(ncap * 4);
   size_t sort_bytes = 0;
   cub::DeviceRadixSort::SortPairs(nullptr, sort_bytes, (int32_t *)nullptr, (int32_t *)nullptr,
-                                  (int32_t *)nullptr, (int32_t *)nullptr, (int)ncap, 0, 6);
+                                  (int32_t *)nullptr, (int32_t *)nullptr, (int)ncap, 0,
+                                  bits_for((long long)(nbins / a->nblk + 1) * (kChunkEntries + 2)));
   w->ord_key_in = (int32_t *)take(ncap * 4);
   w->ord_key_out = (int32_t *)take(ncap * 4);
   w->ord_in = (int32_t *)take(ncap * 4);
@@ -1185,11 +1191,13 @@ bsa_status run_attn_bwd(const bsa_attn_args *a, void *ws, size_t ws_bytes, cudaS
       !getenv("BSA_DKDV_NOSORT")) {
     const int ncap = (int)(dkv_grid + 1);
     chunk_key_kernel<<<(ncap + 255) / 256, 256, 0, st>>>(w.plan, w.row_ptr, w.chunk_bin, nbins,
-                                                        kChunkEntries, ncap, w.ord_key_in, w.ord_in);
+                                                        a->nblk, kChunkEntries, ncap, w.ord_key_in,
+                                                        w.ord_in);
     if ((s = check_launch("chunk_key"))) return s;
     size_t sb = w.sort_bytes;
+    const int key_bits = bits_for((long long)(nbins / a->nblk + 1) * (kChunkEntries + 2));
     if (cub::DeviceRadixSort::SortPairs(w.sort_tmp, sb, w.ord_key_in, w.ord_key_out, w.ord_in,
-                                        w.ord, ncap, 0, 6, st) != cudaSuccess)
+                                        w.ord, ncap, 0, key_bits, st) != cudaSuccess)
       return fail(BSA_ERR_LAUNCH, "attn_bwd: chunk order sort failed");
     pl.chunk_ord = w.ord;
   }

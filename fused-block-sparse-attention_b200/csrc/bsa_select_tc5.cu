@@ -10,7 +10,7 @@
 //     (operands are the fp32 summaries, TMA-loaded with 128-byte swizzle; the
 //     tensor core reads them as tf32), accumulated in TMEM (two buffers).
 //  2. Per query row (one epilogue thread per TMEM lane) a sorted list of the
-//     best T exact scores so far.  A key block can only enter the list when its
+//     best KT >= T exact scores so far, in registers (KT = 8, 16 or 32).  A key block can only enter the list when its
 //     exact score s >= thr (the T-th exact score, ties to the lower block id).
 //     Since |S~ - s| <= eps = 2^-7 * |a| * |b| (tf32 operand rounding of at most
 //     2^-10 relative per factor, fp32 accumulation, and the fp32 rounding of the
@@ -19,7 +19,9 @@
 //     without changing the result.
 //  3. Keys that pass are re-scored with the exact fp32 chain
 //     s = fma(a_d, b_d, s), d = 0..dim-1 (operands read back from the same
-//     shared-memory tiles) and inserted by (score desc, block id asc).
+//     shared-memory tiles), cooperatively: the passing (row, key) pairs of a
+//     warp are queued and scored one per lane, then every row inserts its own
+//     results by (score desc, block id asc) with a fixed compare-exchange sweep.
 //  After the first few tiles the threshold is high and almost every key is
 //  rejected by one add and one compare, so the exact work is a small multiple
 //  of T per row instead of one dot product per causal block pair; the
@@ -49,6 +51,7 @@ constexpr int kN = 128;          // key blocks per tile (TMEM columns per buffer
 constexpr int kTmemCols = 256;   // two accumulator buffers
 constexpr int kMaxT = 32;
 constexpr int kThreads = 192;
+constexpr int kQueue = 1024;     // candidates of one 32-column chunk of one warp (32 x 32)
 
 __host__ __device__ constexpr int chunks(int dim) { return dim / 32; }          // 128-byte K chunks
 __host__ __device__ constexpr int tile_bytes(int dim) { return kM * dim * 4; }  // A or one B stage
@@ -56,7 +59,7 @@ __host__ __device__ constexpr int stages(int dim) { return dim <= 32 ? 6 : (dim 
 
 struct Smem {
   // offsets (bytes) from the 1024-aligned dynamic shared memory base
-  int a, b, ls, li, nb, bars, total;
+  int a, b, ls, li, nb, q, bars, total;
 };
 __host__ __device__ constexpr Smem layout(int dim) {
   Smem s{};
@@ -65,7 +68,8 @@ __host__ __device__ constexpr Smem layout(int dim) {
   s.ls = s.b + stages(dim) * tile_bytes(dim);
   s.li = s.ls + kMaxT * kM * 4;
   s.nb = s.li + kMaxT * kM * 4;
-  s.bars = s.nb + kM * 4 + kM * 4;  // column norms + per-row list lengths
+  s.q = s.nb + kM * 4 + kM * 4;     // column norms + per-row list lengths
+  s.bars = s.q + 4 * kQueue * (2 + 4);  // per-warp candidate queues (u16 entry + fp32 score)
   s.total = s.bars + 8 * (1 + 2 * 6 + 2 * 2) + 16;
   return s;
 }
@@ -134,7 +138,7 @@ __device__ __forceinline__ int ld_dsmem_s32(uint32_t addr) {
   return v;
 }
 
-template <int DIM>
+template <int DIM, int KT>
 __global__ void __launch_bounds__(kThreads, 1)
     select_tc5_kernel(const __grid_constant__ CUtensorMap map_a,
                       const __grid_constant__ CUtensorMap map_b, const bsa_select_args a, int T,
@@ -149,6 +153,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   int *li = reinterpret_cast<int *>(sm + L.li);
   float *nbs = reinterpret_cast<float *>(sm + L.nb);
   int *cnt = reinterpret_cast<int *>(sm + L.nb + kM * 4);
+  uint16_t *qent = reinterpret_cast<uint16_t *>(sm + L.q);                  // [4][kQueue]
+  float *qres = reinterpret_cast<float *>(sm + L.q + 4 * kQueue * 2);       // [4][kQueue]
   uint64_t *bars = reinterpret_cast<uint64_t *>(sm + L.bars);
   uint64_t *a_full = bars;
   uint64_t *b_full = bars + 1;         // [NS]
@@ -267,8 +273,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (!live) jend = 0;
     const uint8_t *As = sm + L.a;
     float na = 0.f;
-    int n = 0;
-    float thr = -INFINITY;  // T-th exact score once the list is full
+    // this row's best KT (the power of two >= T) exact scores so far, sorted by
+    // (score desc, id asc), in registers; empty entries are (-inf, INT_MAX).  A
+    // key that does not beat the last entry cannot be among the best T.
+    float Ls[KT];
+    int Li[KT];
+#pragma unroll
+    for (int l = 0; l < KT; ++l) {
+      Ls[l] = -INFINITY;
+      Li[l] = INT_MAX;
+    }
     bool ok = ntile == 0 || mbar_wait(a_full, 0);
     if (live && ok) {
 #pragma unroll 4
@@ -319,37 +333,86 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // candidates of this 32-column chunk against the current threshold (it
         // only rises while they are processed, so the mask is a superset)
-        unsigned m = 0;
+        // candidate mask, branch-free: valid columns of this chunk, and the
+        // approximate score against the current threshold
+        const int lim = min(max(cend - cc, 0), 32);
+        unsigned m = lim >= 32 ? 0xffffffffu : ((1u << lim) - 1u);
+        if (jskip >= k0 + cc && jskip < k0 + cc + 32) m &= ~(1u << (jskip - k0 - cc));
+        {
+          const float thr = Ls[KT - 1];
+          unsigned pass = 0;
+          const float4 *nb4 = reinterpret_cast<const float4 *>(nbs + cc);
 #pragma unroll
-        for (int c = 0; c < 32; ++c)
-          if (cc + c < cend && v[c] + ka * nbs[cc + c] >= thr) m |= 1u << c;
-        while (m) {
-          const int col = cc + __ffs(m) - 1;
-          m &= m - 1;
-          const int j = k0 + col;
-          if (j == jskip) continue;
-          float e = 0.f;
+          for (int c4 = 0; c4 < 8; ++c4) {
+            const float4 nb = nb4[c4];
+            pass |= (unsigned)(fmaf(ka, nb.x, v[4 * c4 + 0]) >= thr) << (4 * c4 + 0);
+            pass |= (unsigned)(fmaf(ka, nb.y, v[4 * c4 + 1]) >= thr) << (4 * c4 + 1);
+            pass |= (unsigned)(fmaf(ka, nb.z, v[4 * c4 + 2]) >= thr) << (4 * c4 + 2);
+            pass |= (unsigned)(fmaf(ka, nb.w, v[4 * c4 + 3]) >= thr) << (4 * c4 + 3);
+          }
+          m &= pass;
+        }
+        // The candidates of the whole warp are re-scored cooperatively (one per
+        // lane, so the exact dot products never run with idle lanes): each lane
+        // queues its (row, column) pairs at its exclusive prefix, the warp scores
+        // the queue 32 at a time, then every lane inserts its own results.
+        const int nc = __popc(m);
+        int pre = nc;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int y = __shfl_up_sync(0xffffffffu, pre, o);
+          if (lane >= o) pre += y;
+        }
+        const int total = __shfl_sync(0xffffffffu, pre, 31);
+        if (total == 0) continue;
+        pre -= nc;
+        uint16_t *wq = qent + warp * kQueue;
+        float *wr = qres + warp * kQueue;
+        {
+          unsigned mm = m;
+          int p = pre;
+          while (mm) {
+            wq[p++] = (uint16_t)((lane << 5) | (__ffs(mm) - 1));
+            mm &= mm - 1;
+          }
+        }
+        __syncwarp();
+        for (int base = 0; base < total; base += 32) {
+          const int idx = base + lane;
+          if (idx < total) {
+            const int ent = wq[idx];
+            const int r = warp * 32 + (ent >> 5), col = cc + (ent & 31);
+            float e = 0.f;
 #pragma unroll 4
-          for (int d = 0; d < DIM; d += 4) {
-            const float4 x = *reinterpret_cast<const float4 *>(As + off(row, d));
-            const float4 y = *reinterpret_cast<const float4 *>(Bs + off(col, d));
-            e = fmaf(x.x, y.x, e);
-            e = fmaf(x.y, y.y, e);
-            e = fmaf(x.z, y.z, e);
-            e = fmaf(x.w, y.w, e);
+            for (int d = 0; d < DIM; d += 4) {
+              const float4 x = *reinterpret_cast<const float4 *>(As + off(r, d));
+              const float4 y = *reinterpret_cast<const float4 *>(Bs + off(col, d));
+              e = fmaf(x.x, y.x, e);
+              e = fmaf(x.y, y.y, e);
+              e = fmaf(x.z, y.z, e);
+              e = fmaf(x.w, y.w, e);
+            }
+            wr[idx] = e;
           }
-          if (!(e > -INFINITY)) continue;  // -inf / NaN never rank
-          if (n == T && !better(e, j, ls[(T - 1) * kM + row], li[(T - 1) * kM + row])) continue;
-          int pos = n < T ? n : T - 1;
-          while (pos > 0 && better(e, j, ls[(pos - 1) * kM + row], li[(pos - 1) * kM + row])) {
-            ls[pos * kM + row] = ls[(pos - 1) * kM + row];
-            li[pos * kM + row] = li[(pos - 1) * kM + row];
-            --pos;
+        }
+        __syncwarp();
+        for (int x = pre; x < pre + nc; ++x) {
+          const int j = k0 + cc + (wq[x] & 31);
+          float cs = wr[x];
+          if (!(cs > -INFINITY)) continue;  // -inf / NaN never rank
+          if (!better(cs, j, Ls[KT - 1], Li[KT - 1])) continue;
+          int ci = j;
+          // insertion by a fixed compare-exchange sweep (no data-dependent indexing)
+#pragma unroll
+          for (int l = 0; l < KT; ++l) {
+            const bool bt = better(cs, ci, Ls[l], Li[l]);
+            const float ts = Ls[l];
+            const int ti = Li[l];
+            Ls[l] = bt ? cs : ts;
+            Li[l] = bt ? ci : ti;
+            cs = bt ? ts : cs;
+            ci = bt ? ti : ci;
           }
-          ls[pos * kM + row] = e;
-          li[pos * kM + row] = j;
-          if (n < T) ++n;
-          if (n == T) thr = ls[(T - 1) * kM + row];
         }
       }
       named_bar_sync(1, 128);  // nbs is rewritten by the next tile
@@ -358,7 +421,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (tid == 0 && e_err) atomicOr(&s_err, 1);
     if (tid == 0 && e_err) report(a.status, BSA_DEVERR_TIMEOUT);
-    cnt[row] = n;
+    int n = 0;
+#pragma unroll
+    for (int l = 0; l < KT; ++l) {
+      ls[l * kM + row] = Ls[l];
+      li[l * kM + row] = Li[l];
+      n += Li[l] != INT_MAX;
+    }
+    cnt[row] = min(n, T);
   }
 
   // ---------------------------------------------------------------- merge + write
@@ -457,9 +527,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // Used by run_select: the tensor-core path serves DOT scores with dim 32 or 64, 1 <= T <= 32, and enough key blocks for the tensor cores to pay off.
 bool select_tc5_applicable(const bsa_select_args *a, int T) {
-  if (getenv("BSA_SELECT_SIMT") || !getenv("BSA_SELECT_TC5")) return false;
+  if (getenv("BSA_SELECT_SIMT")) return false;
+  // measured crossover with the fp32 SIMT kernel: about 4096 key blocks (equal
+  // there); BSA_SELECT_TC5=1 forces this path from 512 key blocks up
+  const int min_nblk = getenv("BSA_SELECT_TC5") ? 512 : 8192;
   return a->score_kind == BSA_SCORE_DOT && (a->dim == 32 || a->dim == 64) &&
-         T >= 1 && T <= s5::kMaxT && a->nblk >= 512 &&
+         T >= 1 && T <= s5::kMaxT && a->nblk >= min_nblk &&
          reinterpret_cast<uintptr_t>(a->a) % 16 == 0 && reinterpret_cast<uintptr_t>(a->b1) % 16 == 0;
 }
 
@@ -480,10 +553,16 @@ bsa_status run_select_tc5(const bsa_select_args *a, int T, int W, cudaStream_t s
   if (const char *e = getenv("BSA_SELECT_SPLIT")) C = std::max(1, std::min(8, atoi(e)));
   const int smem = layout(a->dim).total + 1024;
   void (*kern)(const CUtensorMap, const CUtensorMap, const bsa_select_args, int, int, int) = nullptr;
-  if (a->dim == 32)
-    kern = select_tc5_kernel<32>;
-  else
-    kern = select_tc5_kernel<64>;
+  const int kt = T <= 8 ? 8 : (T <= 16 ? 16 : 32);
+#define BSA_S5_PICK(D_)                                        \
+  kern = kt == 8 ? select_tc5_kernel<D_, 8>                    \
+                 : (kt == 16 ? select_tc5_kernel<D_, 16> : select_tc5_kernel<D_, 32>);
+  if (a->dim == 32) {
+    BSA_S5_PICK(32)
+  } else {
+    BSA_S5_PICK(64)
+  }
+#undef BSA_S5_PICK
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(nqt * C), (unsigned)a->G, 1);

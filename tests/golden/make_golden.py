@@ -26,6 +26,13 @@ Fixtures (npz, fp32 / int32):
   selectors.npz       SelectOracle (random mass), SelectRandom (its CPU draws), SelectLastTok,
                       SelectMaxQMax and SelectTwoStage (src/qwen_blocksparse.py:124-299) on
                       one seeded GQA input with a padded last block.
+  module_*.npz        whole modules through their reference (CPU gather / SDPA) path:
+                      BlockSparseSSA (causal + gate with a padded L, non-causal),
+                      LSHBucketSSA (causal, gate) and CentroidSSA (plain routing and
+                      the refine step) with seeded weights: the input, the upstream
+                      gradient, every parameter, the output and the gradients of
+                      sum(out * dout) w.r.t. the input and every parameter, plus the
+                      selection the module attended with (BlockSparseSSA).
   rope.npz            transformers' apply_rotary_pos_emb (qwen3_5_moe) on bf16 inputs, and
                       the cos/sin of Qwen3_5MoeTextRotaryEmbedding for text positions.
 """
@@ -237,6 +244,40 @@ def centroid_case(name, B, L, d, h, bs, C, cpq, cap, refine, seed):
          refine=torch.tensor(refine if refine is not None else -1))
 
 
+def module_case(name, cls, kwargs, B, L, seed):
+    import json
+
+    import ssa_model
+    torch.manual_seed(seed)
+    m = getattr(ssa_model, cls)(**kwargs)
+    d = kwargs["d"]
+    x = torch.randn(B, L, d, requires_grad=True)
+    cap_ = {}
+    orig = ssa_model._gather_and_attend
+
+    def spy(q, k, v, sel, *a, **kw):
+        cap_["sel"] = sel.clone()
+        return orig(q, k, v, sel, *a, **kw)
+
+    ssa_model._gather_and_attend = spy
+    try:
+        out = m(x)
+    finally:
+        ssa_model._gather_and_attend = orig
+    dout = torch.randn_like(out)
+    (out * dout).sum().backward()
+    arrs = dict(x=x, dout=dout, out=out, dx=x.grad, cls=np.array(cls),
+                kwargs=np.array(json.dumps(kwargs)), meta=np.array([B, L, d, seed], np.int32))
+    for n, prm in m.named_parameters():
+        arrs["p:" + n] = prm
+        arrs["g:" + n] = prm.grad if prm.grad is not None else torch.zeros_like(prm)
+    for n, buf in m.named_buffers():
+        arrs["b:" + n] = buf
+    if "sel" in cap_:
+        arrs["sel"] = cap_["sel"]
+    save(name, **arrs)
+
+
 def selectors_case(name, B, Hq, Hkv, L, d, bs, topk, seed):
     import qwen_blocksparse as qb
     torch.manual_seed(seed)
@@ -279,6 +320,19 @@ def main():
         ("selectors.npz", selectors_case, (1, 4, 2, 600, 16, 32, 3, 12)),
         ("centroid_plain.npz", centroid_case, (2, 2048, 64, 2, 32, 8, 2, 6, None, 13)),
         ("centroid_refine.npz", centroid_case, (1, 2048, 64, 2, 32, 8, 3, 8, 5, 14)),
+        ("module_ssa_causal_gate.npz", module_case,
+         ("BlockSparseSSA", dict(d=64, h=2, block=64, topk=4, causal=True, gate=True), 2, 1000, 15)),
+        ("module_ssa_noncausal.npz", module_case,
+         ("BlockSparseSSA", dict(d=128, h=4, block=32, topk=3, causal=False, gate=False), 1, 512, 16)),
+        ("module_lsh_causal_gate.npz", module_case,
+         ("LSHBucketSSA", dict(d=64, h=2, block=32, topk=4, n_rounds=3, n_buckets=6, cap=4,
+                               causal=True, gate=True), 1, 1024, 17)),
+        ("module_centroid.npz", module_case,
+         ("CentroidSSA", dict(d=64, h=2, block=32, n_centroids=6, cpq=2, cap=3, gate=True), 1, 1024,
+          18)),
+        ("module_centroid_refine.npz", module_case,
+         ("CentroidSSA", dict(d=64, h=2, block=32, n_centroids=6, cpq=2, cap=3, refine_topk=3),
+          1, 1024, 19)),
     ]
     for name, fn, args in cases:
         if name.startswith(a.only):
