@@ -528,9 +528,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Used by run_select: the tensor-core path serves DOT scores with dim 32 or 64, 1 <= T <= 32, and enough key blocks for the tensor cores to pay off.
 bool select_tc5_applicable(const bsa_select_args *a, int T) {
   if (getenv("BSA_SELECT_SIMT")) return false;
-  // measured crossover with the fp32 SIMT kernel: about 4096 key blocks (equal
-  // there); BSA_SELECT_TC5=1 forces this path from 512 key blocks up
-  const int min_nblk = getenv("BSA_SELECT_TC5") ? 512 : 8192;
+  // measured against the fp32 SIMT kernel: ahead from 4096 key blocks (262k
+  // tokens of block 64: 0.18 against 0.45 ms for one head, 0.67 against 0.72 for
+  // eight); BSA_SELECT_TC5=1 forces this path from 512 key blocks up
+  const int min_nblk = getenv("BSA_SELECT_TC5") ? 512 : 4096;
   return a->score_kind == BSA_SCORE_DOT && (a->dim == 32 || a->dim == 64) &&
          T >= 1 && T <= s5::kMaxT && a->nblk >= min_nblk &&
          reinterpret_cast<uintptr_t>(a->a) % 16 == 0 && reinterpret_cast<uintptr_t>(a->b1) % 16 == 0;
@@ -547,9 +548,10 @@ bsa_status run_select_tc5(const bsa_select_args *a, int T, int W, cudaStream_t s
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
   // split the key tiles of a query tile over C CTAs when there are too few
-  // query tiles to fill the SMs (one resident CTA per SM)
+  // query tiles to fill the SMs (one resident CTA per SM); measured on B200:
+  // clusters of 4 fill best, clusters of 8 schedule worse than 4
   int C = 1;
-  while (C < 8 && (long long)nqt * a->G * C < 2LL * nsm && C * 2 <= std::max(1, nkt / 2)) C *= 2;
+  while (C < 4 && (long long)nqt * a->G * C * 2 <= 2LL * nsm && C * 2 <= std::max(1, nkt / 2)) C *= 2;
   if (const char *e = getenv("BSA_SELECT_SPLIT")) C = std::max(1, std::min(8, atoi(e)));
   const int smem = layout(a->dim).total + 1024;
   void (*kern)(const CUtensorMap, const CUtensorMap, const bsa_select_args, int, int, int) = nullptr;
