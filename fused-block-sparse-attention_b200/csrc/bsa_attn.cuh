@@ -30,6 +30,10 @@ struct AttnParams {
   int64_t dq_sb, dq_sh, dq_sl, dk_sb, dk_sh, dk_sl, dv_sb, dv_sh, dv_sl;
   float *dgate;
   float *dvec;  // (B,Hq,Lp) rowsum(dO * O)
+  // dS tiles of the active (query block, slot) entries, written by the dK/dV
+  // kernel and read back by the dQ kernel that consumes them (null: dQ
+  // recomputes S and dP itself): bf16/f16 [B][Hq][nq][kk][64 keys][64 rows]
+  void *ds;
   int32_t *status;
 };
 

@@ -968,6 +968,7 @@ struct BwdWs {
   void *scan_tmp;
   size_t scan_bytes;
   float *part;
+  void *ds;  // dS tiles for the stored-dS dQ pass (null when it does not apply)
   size_t total;
 };
 
@@ -995,6 +996,10 @@ static void csr_args_from(const bsa_attn_args *a, bsa_csr_args *c) {
   c->q_blk0 = a->q_blk0;
   c->nq = attn_nq(a);
 }
+
+size_t dq_ds_bytes(const bsa_attn_args *a, int nq);
+bsa_status launch_dq_ds(int dtype, const CUtensorMap &mk, int pk, const AttnParams &p,
+                        cudaStream_t st);
 
 static size_t bwd_layout(const bsa_attn_args *a, BwdWs *w, uint8_t *base) {
   bsa_csr_args c;
@@ -1035,6 +1040,8 @@ static size_t bwd_layout(const bsa_attn_args *a, BwdWs *w, uint8_t *base) {
   w->scan_bytes = scan_bytes;
   w->scan_tmp = take(scan_bytes);
   w->part = (float *)take((size_t)pmax * Y * 2 * a->bs * a->D * 4);
+  const size_t ds_bytes = dq_ds_bytes(a, attn_nq(a));
+  w->ds = ds_bytes ? take(ds_bytes) : nullptr;
   w->total = off;
   return off;
 }
@@ -1093,6 +1100,16 @@ static bsa_status launch_bwd_tc(const bsa_attn_args *a, const AttnParams &p, con
                      "v")))
     return s;
   auto pk = [](const TensorMap4 &m) { return m.perm[0] | (m.perm[1] << 2) | (m.perm[2] << 4); };
+  if (BS == 64 && D == 64 && p.ds && dkdv_sm100_applicable(a->dtype, BS, D)) {
+    // dK/dV first (it stores the dS tiles), then dQ from the stored tiles
+    if ((s = launch_dvec(a->dtype, p, D, st))) return s;
+    if ((s = launch_dkdv_sm100(a->dtype, mqc.map, mdoc.map, mk.map, mv.map, pk(mqc), pk(mdoc),
+                               pk(mk), pk(mv), p, pl, dkv_grid, st)))
+      return s;
+    if ((s = launch_dq_ds(a->dtype, mk.map, pk(mk), p, st))) return s;
+    dkdv_reduce_kernel<T><<<dim3(pl.nbins, pl.Y), 256, 0, st>>>(p, pl, BS, D);
+    return check_launch("dkdv_reduce");
+  }
   if (BS == 64 && D == 64 && dq_f5_applicable(p, a->dtype, D)) {
     if ((s = launch_dvec(a->dtype, p, D, st))) return s;
     if ((s = launch_dq_f5(a->dtype, mq.map, mdo.map, mk.map, mv.map, pk(mq), pk(mdo), pk(mk),
@@ -1157,6 +1174,7 @@ bsa_status run_attn_bwd(const bsa_attn_args *a, void *ws, size_t ws_bytes, cudaS
   if (reinterpret_cast<uintptr_t>(ws) % 256) return fail(BSA_ERR_WORKSPACE, "attn_bwd: workspace not 256-byte aligned");
   bwd_layout(a, &w, reinterpret_cast<uint8_t *>(ws));
   p.dvec = w.dvec;
+  p.ds = w.ds;
 
   bsa_csr_args c;
   csr_args_from(a, &c);

@@ -418,6 +418,17 @@ __global__ void __launch_bounds__(320, 1)
             }
           }
         }
+        if (p.ds && active) {
+          // dS^T row of this key for the dQ pass: 32 query columns, 64 bytes
+          const int hq = s_meta[st][t][2];
+          T *dst = reinterpret_cast<T *>(p.ds) +
+                   (((((long long)b * p.Hq + hq) * p.nq + qblk) * p.kk + slot) * B5_BS + kr) * B5_BS +
+                   32 * hf;
+#pragma unroll
+          for (int c8 = 0; c8 < 4; ++c8)
+            *reinterpret_cast<uint4 *>(dst + 8 * c8) =
+                make_uint4(wd[4 * c8], wd[4 * c8 + 1], wd[4 * c8 + 2], wd[4 * c8 + 3]);
+        }
         if (gs >= NPD) {  // dV/dK of step gs-NPD read P / dS buffer gs % NPD
           if (!mbar_wait(&g_done[gs % NPD], ((gs / NPD) - 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
           tc05::fence_after();

@@ -322,3 +322,49 @@ def test_tcgen05_forward_d256_identity_selection(cuda, monkeypatch):
     ref = O.attention(q, k, v, ident, None, bs=bs, causal=True, mask_mode=1)
     _cmp(o5, ref, torch.bfloat16, "o tcgen05")
     _cmp(o1, ref, torch.bfloat16, "o mma.sync")
+
+
+@pytest.mark.parametrize("Hq,Hkv,shared,hub,L,mode", [(2, 2, False, False, 4096, 0),
+                                                   (4, 4, True, True, 4096, 0),
+                                                   (4, 2, False, False, 4096 - 37, 0),
+                                                   (2, 1, True, True, 3072 + 64, 1)])
+def test_stored_ds_dq_matches_recomputing_dq(cuda, monkeypatch, Hq, Hkv, shared, hub, L, mode):
+    """Without a gate gradient the block-64 backward takes dQ from the dS tiles the
+    dK/dV kernel stores (bsa_attn_dq_ds.cu); the recomputing dQ kernel
+    (BSA_DQ_DS=0) must agree closely, dK/dV bit for bit, and both match the oracle
+    (GQA, hub blocks, a ragged last block, TOKEN masks with repeated ids)."""
+    import _bsa
+    B, D, bs, kk = 1, 64, 64, 9
+    gen = torch.Generator().manual_seed(Hq * 7 + Hkv + hub + L)
+    nblk = (L + bs - 1) // bs
+    q, do = (torch.randn(B, Hq, L, D, generator=gen).to(torch.bfloat16) for _ in range(2))
+    k, v = (torch.randn(B, Hkv, L, D, generator=gen).to(torch.bfloat16) for _ in range(2))
+    shape = (B, nblk, kk) if shared else (B, Hkv, nblk, kk)
+    sel = torch.randint(0, nblk, shape, generator=gen)
+    sel[..., 0] = torch.arange(nblk).view(*([1] * (len(shape) - 2)), nblk)
+    if hub:
+        sel[..., 1] = 0
+        sel[..., 2] = 3
+    if mode == 1:
+        sel[..., 5] = sel[..., 4]
+    gate = torch.randn(shape, generator=gen) * 0.3
+    dev = [t.to(cuda) for t in (q, k, v, do)]
+    sd, gd = sel.to(cuda, torch.int32), gate.to(cuda)
+    o, lse = _bsa.attn_fwd(dev[0], dev[1], dev[2], sd, gd, bs=bs, causal=True, mask_mode=mode)
+
+    def run():
+        return _bsa.attn_bwd(dev[0], dev[1], dev[2], o, dev[3], sd, lse, gd, bs=bs, causal=True,
+                             mask_mode=mode)
+    r_ds = run()
+    r_ds2 = run()
+    monkeypatch.setenv("BSA_DQ_DS", "0")
+    r_re = run()
+    _bsa.check_status(cuda)
+    for x, y in zip(r_ds[:3], r_ds2[:3]):
+        assert torch.equal(x, y)                          # deterministic
+    assert torch.equal(r_ds[1], r_re[1]) and torch.equal(r_ds[2], r_re[2])
+    assert (r_ds[0].float() - r_re[0].float()).abs().max().item() < 2e-2
+    rq, rk, rv, _ = O.attention_grads(q, k, v, sel, do, gate, bs=bs, causal=True, mask_mode=mode)
+    _cmp(r_ds[0], rq, torch.bfloat16, "dq (stored dS)")
+    _cmp(r_ds[1], rk, torch.bfloat16, "dk")
+    _cmp(r_ds[2], rv, torch.bfloat16, "dv")
