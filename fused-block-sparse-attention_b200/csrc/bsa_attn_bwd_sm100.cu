@@ -352,6 +352,8 @@ __global__ void __launch_bounds__(320, 1)
     const int kr = quad * 16 + (lane & 15);  // key row within the block
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
     int gs = 0, ne = 0;
+    uint64_t evict_first;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(evict_first));
     for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
       B5Unit w;
       b5_unit(pl, p, total, u, w);
@@ -418,17 +420,6 @@ __global__ void __launch_bounds__(320, 1)
             }
           }
         }
-        if (p.ds && active) {
-          // dS^T row of this key for the dQ pass: 32 query columns, 64 bytes
-          const int hq = s_meta[st][t][2];
-          T *dst = reinterpret_cast<T *>(p.ds) +
-                   (((((long long)b * p.Hq + hq) * p.nq + qblk) * p.kk + slot) * B5_BS + kr) * B5_BS +
-                   32 * hf;
-#pragma unroll
-          for (int c8 = 0; c8 < 4; ++c8)
-            *reinterpret_cast<uint4 *>(dst + 8 * c8) =
-                make_uint4(wd[4 * c8], wd[4 * c8 + 1], wd[4 * c8 + 2], wd[4 * c8 + 3]);
-        }
         if (gs >= NPD) {  // dV/dK of step gs-NPD read P / dS buffer gs % NPD
           if (!mbar_wait(&g_done[gs % NPD], ((gs / NPD) - 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
           tc05::fence_after();
@@ -449,6 +440,21 @@ __global__ void __launch_bounds__(320, 1)
         fence_proxy_async_smem();
         tc05::fence_before();
         tc05::mbar_arrive(&p_full[gs % NPD]);
+        if (p.ds && active) {
+          // dS^T row of this key for the dQ pass (32 query columns, 64 bytes),
+          // after the MMA hand-off; evict-first so that the stream of dS tiles
+          // does not push the gathered Q / dO rows out of L2
+          const int hq = s_meta[st][t][2];
+          T *dst = reinterpret_cast<T *>(p.ds) +
+                   (((((long long)b * p.Hq + hq) * p.nq + qblk) * p.kk + slot) * B5_BS + kr) * B5_BS +
+                   32 * hf;
+#pragma unroll
+          for (int c8 = 0; c8 < 4; ++c8)
+            asm volatile("st.global.L2::cache_hint.v4.b32 [%0], {%1,%2,%3,%4}, %5;" ::"l"(dst + 8 * c8),
+                         "r"(wd[4 * c8]), "r"(wd[4 * c8 + 1]), "r"(wd[4 * c8 + 2]),
+                         "r"(wd[4 * c8 + 3]), "l"(evict_first)
+                         : "memory");
+        }
       }
       // ---- dK (scaled) and dV of this unit: this thread's row, columns [32*hf, +32),
       // one accumulator at a time (32 registers)
