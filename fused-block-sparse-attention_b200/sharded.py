@@ -155,6 +155,8 @@ class ShardedBlockSparse:
 
     def gather_kv(self, k, v):
         """All-gathers the K, V shards -> (B, H, L, D) strided views of local buffers."""
+        if _world(self.group)[0] == 1:
+            return k, v
         return _bhld(_gather_rows(_seq_major(k), self.group)), \
             _bhld(_gather_rows(_seq_major(v), self.group))
 
@@ -198,6 +200,8 @@ class ShardedBlockSparse:
         _, _, _, a = self._geometry(q)
         dq, dk, dv = self.ops.attn_bwd(q, kf, vf, o, do, sel, lse, bs=self.bs, causal=self.causal,
                                        q_blk0=a)
+        if _world(self.group)[0] == 1:
+            return dq, dk, dv
         dk_s = _reduce_scatter_rows(_seq_major(dk.float()), self.group)
         dv_s = _reduce_scatter_rows(_seq_major(dv.float()), self.group)
         return dq, _bhld(dk_s).to(dk.dtype).contiguous(), _bhld(dv_s).to(dv.dtype).contiguous()
