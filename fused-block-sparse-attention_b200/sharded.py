@@ -6,8 +6,9 @@ dO rows, their selection rows, O and dQ.  K and V arrive sharded the same way
 (each rank holds the rows of its own blocks, as a sequence-parallel model
 produces them).
 
-  forward   1. all-gather K and V into local HBM (sequence-major buffers, so the
-               gathered tensor is a strided (B, H, L, D) view with no copy);
+  forward   1. all-gather K and V into local HBM (one collective per (batch,
+               head) slice, so the gathered (B, H, L, D) tensor is contiguous and
+               neither side needs a layout copy);
             2. pool this rank's Q and K blocks (mean, fp32) and all-gather both
                pooled summaries (nblk x D per head, small);
             3. select: causal selection costs grow with the query position, so
@@ -103,36 +104,35 @@ class CudaOps:
         return dq, dk, dv
 
 
-def _gather_rows(x, group):
-    """x: (n, ...) this rank's rows -> (world * n, ...) in rank order, in a new
-    contiguous buffer (one all_gather_into_tensor)."""
+def _gather_seq(x, group):
+    """x: (B, H, n, ...) this rank's rows along dim 2 -> (B, H, world * n, ...) in rank
+    order, contiguous: one all_gather_into_tensor per (b, h) slice, each slice
+    contiguous on both sides, so no layout copy is needed on either end."""
     world, _ = _world(group)
     if world == 1:
-        return x.contiguous()
-    out = torch.empty((world * x.shape[0],) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
-    dist.all_gather_into_tensor(out, x.contiguous(), group=group)
+        return x
+    x = x.contiguous()
+    B, H, n = x.shape[:3]
+    out = torch.empty((B, H, world * n) + tuple(x.shape[3:]), dtype=x.dtype, device=x.device)
+    for b in range(B):
+        for h in range(H):
+            dist.all_gather_into_tensor(out[b, h], x[b, h], group=group)
     return out
 
 
-def _reduce_scatter_rows(x, group):
-    """x: (world * n, ...) per-rank partial sums -> this rank's (n, ...) slice of
-    the sum over ranks (one reduce_scatter_tensor)."""
+def _reduce_scatter_seq(x, group):
+    """x: (B, H, world * n, ...) per-rank partial sums -> this rank's (B, H, n, ...)
+    slice of the sum over ranks (one reduce_scatter_tensor per (b, h) slice)."""
     world, _ = _world(group)
     if world == 1:
-        return x.contiguous()
-    out = torch.empty((x.shape[0] // world,) + tuple(x.shape[1:]), dtype=x.dtype, device=x.device)
-    dist.reduce_scatter_tensor(out, x.contiguous(), group=group)
+        return x
+    x = x.contiguous()
+    B, H, L = x.shape[:3]
+    out = torch.empty((B, H, L // world) + tuple(x.shape[3:]), dtype=x.dtype, device=x.device)
+    for b in range(B):
+        for h in range(H):
+            dist.reduce_scatter_tensor(out[b, h], x[b, h], group=group)
     return out
-
-
-def _seq_major(x):
-    """(B, H, n, D) -> contiguous (n, B, H, D)."""
-    return x.permute(2, 0, 1, 3).contiguous()
-
-
-def _bhld(x):
-    """(L, B, H, D) buffer -> its (B, H, L, D) strided view."""
-    return x.permute(1, 2, 0, 3)
 
 
 class ShardedBlockSparse:
@@ -154,11 +154,8 @@ class ShardedBlockSparse:
         return world, rank, nblk, a
 
     def gather_kv(self, k, v):
-        """All-gathers the K, V shards -> (B, H, L, D) strided views of local buffers."""
-        if _world(self.group)[0] == 1:
-            return k, v
-        return _bhld(_gather_rows(_seq_major(k), self.group)), \
-            _bhld(_gather_rows(_seq_major(v), self.group))
+        """All-gathers the K, V shards -> (B, H, L, D) contiguous local buffers."""
+        return _gather_seq(k, self.group), _gather_seq(v, self.group)
 
     def select(self, q, k):
         """This rank's selection rows (B, H, nq, 1 + min(topk, nblk-1)), int32,
@@ -166,11 +163,10 @@ class ShardedBlockSparse:
         world, rank, nblk, a = self._geometry(q)
         nq = q.shape[2] // self.bs
         qp_local = self.ops.pool(q, self.bs)                  # (B, H, nq, D) fp32
-        kp_local = self.ops.pool(k, self.bs)
-        kp = _bhld(_gather_rows(_seq_major(kp_local), self.group)).contiguous()
+        kp = _gather_seq(self.ops.pool(k, self.bs), self.group)
         if world == 1 or not self.causal:
             return self.ops.select(qp_local, kp, topk=self.topk, causal=self.causal, q_blk0=a)
-        qp = _bhld(_gather_rows(_seq_major(qp_local), self.group))
+        qp = _gather_seq(qp_local, self.group)
         ranges = select_ranges(nblk, world, self.causal)
         s0, s1 = ranges[rank]
         mine = self.ops.select(qp[:, :, s0:s1].contiguous(), kp, topk=self.topk,
@@ -179,9 +175,10 @@ class ShardedBlockSparse:
         pad = torch.zeros(mine.shape[0], mine.shape[1], width, mine.shape[3], dtype=mine.dtype,
                           device=mine.device)
         pad[:, :, :s1 - s0] = mine
-        every = _gather_rows(_seq_major(pad), self.group)      # (world * width, B, H, W)
-        rows = torch.cat([every[r * width:r * width + (e - b)] for r, (b, e) in enumerate(ranges)])
-        return _bhld(rows[a:a + nq]).contiguous()
+        every = _gather_seq(pad, self.group)                  # (B, H, world * width, W)
+        rows = torch.cat([every[:, :, r * width:r * width + (e - b)]
+                          for r, (b, e) in enumerate(ranges)], dim=2)
+        return rows[:, :, a:a + nq].contiguous()
 
     def forward(self, q, k, v):
         """Returns (o, ctx): o is this rank's (B, H, Ls, D) output; ctx carries what
@@ -202,6 +199,6 @@ class ShardedBlockSparse:
                                        q_blk0=a)
         if _world(self.group)[0] == 1:
             return dq, dk, dv
-        dk_s = _reduce_scatter_rows(_seq_major(dk.float()), self.group)
-        dv_s = _reduce_scatter_rows(_seq_major(dv.float()), self.group)
-        return dq, _bhld(dk_s).to(dk.dtype).contiguous(), _bhld(dv_s).to(dv.dtype).contiguous()
+        dk_s = _reduce_scatter_seq(dk.float(), self.group)
+        dv_s = _reduce_scatter_seq(dv.float(), self.group)
+        return dq, dk_s.to(dk.dtype), dv_s.to(dv.dtype)
