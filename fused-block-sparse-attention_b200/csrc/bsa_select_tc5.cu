@@ -320,43 +320,50 @@ __global__ void __launch_bounds__(kThreads, 1)
       named_bar_sync(1, 128);  // norms written; every epilogue warp sees the same e_err
       if (e_err) break;
       const int cend = min(kN, jend - k0);  // columns < cend may be valid for this row
-#pragma unroll 1
-      for (int cc = 0; cc < kN; cc += 32) {
+      // 1. candidate masks of the four 32-column chunks, branch-free: valid
+      //    columns, and the approximate score against the current threshold
+      unsigned mk[kN / 32];
+#pragma unroll
+      for (int ch = 0; ch < kN / 32; ++ch) {
+        const int cc = ch * 32;
         __syncwarp();
         float v[32];
         tc05::ld32(tc05::taddr(tmem, warp * 32, b * kN + cc), v);
         tc05::wait_ld();
-        if (cc + 32 >= kN) {
+        if (ch == kN / 32 - 1) {
           tc05::fence_before();
           __syncwarp();
           if (lane == 0) tc05::mbar_arrive(&acc_empty[b]);
         }
-        // candidates of this 32-column chunk against the current threshold (it
-        // only rises while they are processed, so the mask is a superset)
-        // candidate mask, branch-free: valid columns of this chunk, and the
-        // approximate score against the current threshold
         const int lim = min(max(cend - cc, 0), 32);
         unsigned m = lim >= 32 ? 0xffffffffu : ((1u << lim) - 1u);
         if (jskip >= k0 + cc && jskip < k0 + cc + 32) m &= ~(1u << (jskip - k0 - cc));
-        {
-          const float thr = Ls[KT - 1];
-          unsigned pass = 0;
-          const float4 *nb4 = reinterpret_cast<const float4 *>(nbs + cc);
+        const float thr = Ls[KT - 1];
+        unsigned pass = 0;
+        const float4 *nb4 = reinterpret_cast<const float4 *>(nbs + cc);
 #pragma unroll
-          for (int c4 = 0; c4 < 8; ++c4) {
-            const float4 nb = nb4[c4];
-            pass |= (unsigned)(fmaf(ka, nb.x, v[4 * c4 + 0]) >= thr) << (4 * c4 + 0);
-            pass |= (unsigned)(fmaf(ka, nb.y, v[4 * c4 + 1]) >= thr) << (4 * c4 + 1);
-            pass |= (unsigned)(fmaf(ka, nb.z, v[4 * c4 + 2]) >= thr) << (4 * c4 + 2);
-            pass |= (unsigned)(fmaf(ka, nb.w, v[4 * c4 + 3]) >= thr) << (4 * c4 + 3);
-          }
-          m &= pass;
+        for (int c4 = 0; c4 < 8; ++c4) {
+          const float4 nb = nb4[c4];
+          pass |= (unsigned)(fmaf(ka, nb.x, v[4 * c4 + 0]) >= thr) << (4 * c4 + 0);
+          pass |= (unsigned)(fmaf(ka, nb.y, v[4 * c4 + 1]) >= thr) << (4 * c4 + 1);
+          pass |= (unsigned)(fmaf(ka, nb.z, v[4 * c4 + 2]) >= thr) << (4 * c4 + 2);
+          pass |= (unsigned)(fmaf(ka, nb.w, v[4 * c4 + 3]) >= thr) << (4 * c4 + 3);
         }
-        // The candidates of the whole warp are re-scored cooperatively (one per
-        // lane, so the exact dot products never run with idle lanes): each lane
-        // queues its (row, column) pairs at its exclusive prefix, the warp scores
-        // the queue 32 at a time, then every lane inserts its own results.
-        const int nc = __popc(m);
+        mk[ch] = m & pass;
+      }
+      // 2. The candidates of the whole warp are re-scored cooperatively (one per
+      //    lane, so the exact dot products never run with idle lanes): each lane
+      //    queues its (row, column) pairs at its exclusive prefix, the warp scores
+      //    the queue 32 at a time, then every lane inserts its own results.  The
+      //    whole tile forms one group unless its candidates overflow the queue
+      //    (early tiles, whose threshold is still low): then chunk by chunk.
+      uint16_t *wq = qent + warp * kQueue;
+      float *wr = qres + warp * kQueue;
+      auto group = [&](int c0, int c1) {
+        int nc = 0;
+#pragma unroll
+        for (int ch = 0; ch < kN / 32; ++ch)
+          if (ch >= c0 && ch < c1) nc += __popc(mk[ch]);
         int pre = nc;
 #pragma unroll
         for (int o = 1; o < 32; o <<= 1) {
@@ -364,16 +371,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane >= o) pre += y;
         }
         const int total = __shfl_sync(0xffffffffu, pre, 31);
-        if (total == 0) continue;
+        if (total == 0) return;
         pre -= nc;
-        uint16_t *wq = qent + warp * kQueue;
-        float *wr = qres + warp * kQueue;
         {
-          unsigned mm = m;
           int p = pre;
-          while (mm) {
-            wq[p++] = (uint16_t)((lane << 5) | (__ffs(mm) - 1));
-            mm &= mm - 1;
+#pragma unroll
+          for (int ch = 0; ch < kN / 32; ++ch) {
+            if (ch < c0 || ch >= c1) continue;
+            unsigned mm = mk[ch];
+            while (mm) {
+              wq[p++] = (uint16_t)((lane << 7) | (ch * 32 + __ffs(mm) - 1));
+              mm &= mm - 1;
+            }
           }
         }
         __syncwarp();
@@ -381,7 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int idx = base + lane;
           if (idx < total) {
             const int ent = wq[idx];
-            const int r = warp * 32 + (ent >> 5), col = cc + (ent & 31);
+            const int r = warp * 32 + (ent >> 7), col = ent & 127;
             float e = 0.f;
 #pragma unroll 4
             for (int d = 0; d < DIM; d += 4) {
@@ -397,7 +406,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         __syncwarp();
         for (int x = pre; x < pre + nc; ++x) {
-          const int j = k0 + cc + (wq[x] & 31);
+          const int j = k0 + (wq[x] & 127);
           float cs = wr[x];
           if (!(cs > -INFINITY)) continue;  // -inf / NaN never rank
           if (!better(cs, j, Ls[KT - 1], Li[KT - 1])) continue;
@@ -414,6 +423,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             ci = bt ? ti : ci;
           }
         }
+        __syncwarp();  // the queue is reused by the next group
+      };
+      int tile_n = 0;
+#pragma unroll
+      for (int ch = 0; ch < kN / 32; ++ch) tile_n += __popc(mk[ch]);
+      const int tile_total = __reduce_add_sync(0xffffffffu, tile_n);
+      if (tile_total <= kQueue) {
+        group(0, kN / 32);
+      } else {
+#pragma unroll 1
+        for (int ch = 0; ch < kN / 32; ++ch) group(ch, ch + 1);
       }
       named_bar_sync(1, 128);  // nbs is rewritten by the next tile
       __syncwarp();
