@@ -208,6 +208,30 @@ __device__ __forceinline__ float ex2(float x) {
 
 constexpr float kLog2e = 1.4426950408889634f;
 
+// Packed fp32 pairs (sm_100 f32x2 arithmetic: one instruction for two lanes of
+// work, each element rounded exactly as the scalar instruction would).
+#define BSA_F32X2_OP(name, op)                                                            \
+  __device__ __forceinline__ float2 name(float2 a, float2 b) {                             \
+    float2 d;                                                                            \
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t" \
+        op " rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"                                  \
+        : "=f"(d.x), "=f"(d.y)                                                           \
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));                                       \
+    return d;                                                                            \
+  }
+BSA_F32X2_OP(add2, "add.rn.f32x2")
+BSA_F32X2_OP(sub2, "sub.rn.f32x2")
+BSA_F32X2_OP(mul2, "mul.rn.f32x2")
+#undef BSA_F32X2_OP
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mov.b64 rc, {%6, %7};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
 // ---------------------------------------------------------------- slot kinds
 // Classification of one selected slot for one query block.
 enum : int { KIND_SKIP = 0, KIND_FULL = 1, KIND_TRIU = 2, KIND_PAD = 4 };
