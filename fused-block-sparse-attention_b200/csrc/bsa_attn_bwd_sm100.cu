@@ -403,20 +403,27 @@ __global__ void __launch_bounds__(320, 1)
                 if (!key_ok || (triu && kr > qc) || q0 + 16 * h2 + c >= p.Lq) sv[h2][c] = -INFINITY;
               }
             }
+            // pairs of columns through the packed f32x2 pipe (same per-element
+            // rounding as the scalar sequence)
+            const float2 s22 = make_float2(p.scale2, p.scale2), g22 = make_float2(g2, g2);
 #pragma unroll
             for (int c = 0; c < 16; c += 4) {
               const float4 a4 = *reinterpret_cast<const float4 *>(lsep + 16 * h2 + c);
               const float4 d4 = *reinterpret_cast<const float4 *>(lsep + B5_BS + 16 * h2 + c);
               const float *x = sv[h2], *y = dp[h2];
-              const float p0 = ex2(fmaf(x[c], p.scale2, g2 - a4.x));
-              const float p1 = ex2(fmaf(x[c + 1], p.scale2, g2 - a4.y));
-              const float p2 = ex2(fmaf(x[c + 2], p.scale2, g2 - a4.z));
-              const float p3 = ex2(fmaf(x[c + 3], p.scale2, g2 - a4.w));
+              const float2 e01 = fma2(make_float2(x[c], x[c + 1]), s22,
+                                      sub2(g22, make_float2(a4.x, a4.y)));
+              const float2 e23 = fma2(make_float2(x[c + 2], x[c + 3]), s22,
+                                      sub2(g22, make_float2(a4.z, a4.w)));
+              const float2 p01 = make_float2(ex2(e01.x), ex2(e01.y));
+              const float2 p23 = make_float2(ex2(e23.x), ex2(e23.y));
+              const float2 d01 = mul2(p01, sub2(make_float2(y[c], y[c + 1]), make_float2(d4.x, d4.y)));
+              const float2 d23 = mul2(p23, sub2(make_float2(y[c + 2], y[c + 3]), make_float2(d4.z, d4.w)));
               const int o = 8 * h2 + (c >> 1);
-              wp[o] = Mma<T>::pack(p0, p1);
-              wp[o + 1] = Mma<T>::pack(p2, p3);
-              wd[o] = Mma<T>::pack(p0 * (y[c] - d4.x), p1 * (y[c + 1] - d4.y));
-              wd[o + 1] = Mma<T>::pack(p2 * (y[c + 2] - d4.z), p3 * (y[c + 3] - d4.w));
+              wp[o] = Mma<T>::pack(p01.x, p01.y);
+              wp[o + 1] = Mma<T>::pack(p23.x, p23.y);
+              wd[o] = Mma<T>::pack(d01.x, d01.y);
+              wd[o + 1] = Mma<T>::pack(d23.x, d23.y);
             }
           }
         }
