@@ -272,6 +272,16 @@ def run_ours(a):
     for _ in range(a.warmup):
         step(cfg, q, k, v, do)
     torch.cuda.synchronize()
+    if a.kernels_only:
+        # profiling runs (ncu): the timed steps only, no profiler, copies or CPU legs
+        for _ in range(a.steps):
+            step(cfg, q, k, v, do)
+        torch.cuda.synchronize()
+        if rank == 0:
+            print(json.dumps({"kernels_only": True, "steps": a.steps, "warmup": a.warmup}))
+        if dist:
+            dist.destroy_process_group()
+        return
     nlaunch, kernel_names = count_launches(cfg, q, k, v, do)
 
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(a.steps)]
@@ -774,6 +784,8 @@ def main():
                     help="query blocks per step of the --impl reference arm")
     ap.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     ap.add_argument("--no-long", action="store_true", help="skip the long_fwd (16M) sub-object")
+    ap.add_argument("--kernels-only", action="store_true",
+                    help="run warm-up + steps of the hot path only (for ncu captures); no JSON line")
     ap.add_argument("--no-qsharded", action="store_true", help="skip the qsharded_262k sub-object")
     ap.add_argument("--long-n", type=int, default=1 << 24, help="tokens of the long_fwd sub-object")
     ap.add_argument("--steps-long", type=int, default=5, help="timed steps of long_fwd")
