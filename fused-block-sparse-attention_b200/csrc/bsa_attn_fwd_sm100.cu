@@ -301,14 +301,20 @@ __global__ void __launch_bounds__(192, 1)
         float sum8[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) sum8[i] = 0.f;
+        // column pairs through the packed f32x2 pipe (same rounding per element)
+        const float2 s22 = make_float2(p.scale2, p.scale2), off2 = make_float2(off, off);
+        float2 acc2[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc2[i] = make_float2(0.f, 0.f);
 #pragma unroll
         for (int c = 0; c < 64; c += 2) {
-          const float p0 = ex2(fmaf(s[c], p.scale2, off));
-          const float p1 = ex2(fmaf(s[c + 1], p.scale2, off));
-          sum8[c & 7] += p0;
-          sum8[(c & 7) + 1] += p1;
-          w[c >> 1] = Mma<T>::pack(p0, p1);
+          const float2 e = fma2(make_float2(s[c], s[c + 1]), s22, off2);
+          const float2 pp = make_float2(ex2(e.x), ex2(e.y));
+          acc2[(c >> 1) & 3] = add2(acc2[(c >> 1) & 3], pp);
+          w[c >> 1] = Mma<T>::pack(pp.x, pp.y);
         }
+        sum8[0] = acc2[0].x; sum8[1] = acc2[0].y; sum8[2] = acc2[1].x; sum8[3] = acc2[1].y;
+        sum8[4] = acc2[2].x; sum8[5] = acc2[2].y; sum8[6] = acc2[3].x; sum8[7] = acc2[3].y;
         l += ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
       }
       // PV_{j-1} must be complete: it reads the P buffer and accumulates into O
