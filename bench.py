@@ -413,8 +413,7 @@ def run_qsharded(a, dist, world, rank, dev, flush):
     def fn(ev):
         if ev:
             ev[0].record()
-        kf, vf = m.gather_kv(k, v)
-        sel = m.select(q, k)
+        kf, vf, sel = m.select_and_gather(q, k, v)
         if ev:
             ev[1].record()
         o, lse = _bsa.attn_fwd(q, kf, vf, sel, None, bs=bs, causal=True, q_blk0=a0)
@@ -439,7 +438,9 @@ def run_long_fwd(a, dist, world, rank, dev, flush):
     top-16 + own, query blocks sharded over the ranks (one NCCL all-gather of K and
     V, all-gathers of the pooled summaries and of the selection rows), the causal
     top-k streamed through the tensor-core selector so that no nblk x nblk score
-    matrix is ever stored.  Same total work at every N (strong scaling)."""
+    matrix is ever stored; the K/V all-gather (2 (N-1)/N of 34 GB arrives at
+    every rank) runs while the selection is computed.  Same total work at every
+    N (strong scaling)."""
     import sharded
     import _bsa
     B, H, N, D, bs, topk = 1, 8, a.long_n, 64, 128, 16
@@ -459,22 +460,20 @@ def run_long_fwd(a, dist, world, rank, dev, flush):
     def fn(ev):
         if ev:
             ev[0].record()
-        kf, vf = m.gather_kv(k, v)
+        kf, vf, sel = m.select_and_gather(q, k, v)
         if ev:
             ev[1].record()
-        sel = m.select(q, k)
-        if ev:
-            ev[2].record()
         _bsa.attn_fwd(q, kf, vf, sel, None, bs=bs, causal=True, want_lse=False, q_blk0=a0)
         if ev:
-            ev[3].record()
-    ms, ms_kv, ms_sel, ms_fwd = _phase_loop(fn, 3, a.steps_long, 3, flush, dist, dev)
+            ev[2].record()
+    ms, ms_kvsel, ms_fwd = _phase_loop(fn, 2, a.steps_long, 3, flush, dist, dev)
     peak = torch.cuda.max_memory_allocated(dev) - base
     fwd_flops = 4.0 * B * H * N * (topk + 1) * bs * D
     score_bytes = 4.0 * nblk * nblk * H / world
     return {"N": N, "ms_per_step": round(ms, 3), "tokens_per_s": round(B * N / (ms * 1e-3), 1),
-            "phases_ms_max_over_ranks": {"gather_kv": round(ms_kv, 3), "select": round(ms_sel, 3),
+            "phases_ms_max_over_ranks": {"select+gather_kv (overlapped)": round(ms_kvsel, 3),
                                          "attn_fwd": round(ms_fwd, 3)},
+            "gather_bytes_per_rank": int(2 * (world - 1) * q.numel() * 2),
             "attn_fwd_tflops_per_gpu": round(fwd_flops / world / (ms_fwd * 1e-3) / 1e12, 1),
             "peak_extra_alloc_bytes_per_rank": int(peak),
             "score_matrix_bytes_per_rank_if_stored": int(score_bytes),
@@ -672,8 +671,7 @@ def run_config(a):
             if ev:
                 ev[0].record()
             if m:
-                kf, vf = m.gather_kv(k, v)
-                sel = m.select(q, k)
+                kf, vf, sel = m.select_and_gather(q, k, v)
                 if ev:
                     ev[1].record()
                 o, _ = _bsa.attn_fwd(q, kf, vf, sel, bs=bs, causal=True, want_lse=False,

@@ -104,20 +104,24 @@ class CudaOps:
         return dq, dk, dv
 
 
-def _gather_seq(x, group):
+def _gather_seq(x, group, async_op=False):
     """x: (B, H, n, ...) this rank's rows along dim 2 -> (B, H, world * n, ...) in rank
     order, contiguous: one all_gather_into_tensor per (b, h) slice, each slice
-    contiguous on both sides, so no layout copy is needed on either end."""
+    contiguous on both sides, so no layout copy is needed on either end.  With
+    async_op, returns (out, works): the caller waits on the works before use."""
     world, _ = _world(group)
     if world == 1:
-        return x
+        return (x, []) if async_op else x
     x = x.contiguous()
     B, H, n = x.shape[:3]
     out = torch.empty((B, H, world * n) + tuple(x.shape[3:]), dtype=x.dtype, device=x.device)
+    works = []
     for b in range(B):
         for h in range(H):
-            dist.all_gather_into_tensor(out[b, h], x[b, h], group=group)
-    return out
+            w = dist.all_gather_into_tensor(out[b, h], x[b, h], group=group, async_op=async_op)
+            if async_op:
+                works.append(w)
+    return (out, works) if async_op else out
 
 
 def _reduce_scatter_seq(x, group):
@@ -160,13 +164,41 @@ class ShardedBlockSparse:
     def select(self, q, k):
         """This rank's selection rows (B, H, nq, 1 + min(topk, nblk-1)), int32,
         computed over the equal-area ranges of select_ranges and exchanged."""
+        return self._select(q, k, None)
+
+    def select_and_gather(self, q, k, v):
+        """(K, V gathered, this rank's selection rows).  The K/V all-gathers are
+        started after the small pooled-summary gathers and run while this rank
+        computes its selection rows (the collectives of one communicator run in
+        order, so the summaries must go first); the selection-row exchange
+        follows once K/V have arrived."""
+        if _world(self.group)[0] == 1:
+            return k, v, self._select(q, k, None)
+        box = {}
+
+        def start():
+            box["k"], wk = _gather_seq(k, self.group, async_op=True)
+            box["v"], wv = _gather_seq(v, self.group, async_op=True)
+            box["works"] = wk + wv
+
+        sel = self._select(q, k, start)
+        for w in box["works"]:
+            w.wait()
+        return box["k"], box["v"], sel
+
+    def _select(self, q, k, before_exchange):
         world, rank, nblk, a = self._geometry(q)
         nq = q.shape[2] // self.bs
         qp_local = self.ops.pool(q, self.bs)                  # (B, H, nq, D) fp32
         kp = _gather_seq(self.ops.pool(k, self.bs), self.group)
         if world == 1 or not self.causal:
+            qp = None
+        else:
+            qp = _gather_seq(qp_local, self.group)
+        if before_exchange is not None:
+            before_exchange()                                 # start the K/V gathers
+        if qp is None:
             return self.ops.select(qp_local, kp, topk=self.topk, causal=self.causal, q_blk0=a)
-        qp = _gather_seq(qp_local, self.group)
         ranges = select_ranges(nblk, world, self.causal)
         s0, s1 = ranges[rank]
         mine = self.ops.select(qp[:, :, s0:s1].contiguous(), kp, topk=self.topk,
@@ -186,8 +218,7 @@ class ShardedBlockSparse:
         _, _, _, a = self._geometry(q)
         # K/V first: every rank reaches this collective at once, before the
         # position-dependent (causal, unbalanced) selection work
-        kf, vf = self.gather_kv(k, v)
-        sel = self.select(q, k)
+        kf, vf, sel = self.select_and_gather(q, k, v)
         o, lse = self.ops.attn_fwd(q, kf, vf, sel, bs=self.bs, causal=self.causal, q_blk0=a)
         return o, (kf, vf, sel, lse)
 
