@@ -94,8 +94,9 @@ class CudaOps:
         return sel
 
     @staticmethod
-    def attn_fwd(q, k, v, sel, *, bs, causal, q_blk0):
-        return _bsa.attn_fwd(q, k, v, sel, None, bs=bs, causal=causal, q_blk0=q_blk0)
+    def attn_fwd(q, k, v, sel, *, bs, causal, q_blk0, out=None, want_lse=True):
+        return _bsa.attn_fwd(q, k, v, sel, None, bs=bs, causal=causal, q_blk0=q_blk0, out=out,
+                             want_lse=want_lse)
 
     @staticmethod
     def attn_bwd(q, k, v, o, do, sel, lse, *, bs, causal, q_blk0):
@@ -221,6 +222,40 @@ class ShardedBlockSparse:
         kf, vf, sel = self.select_and_gather(q, k, v)
         o, lse = self.ops.attn_fwd(q, kf, vf, sel, bs=self.bs, causal=self.causal, q_blk0=a)
         return o, (kf, vf, sel, lse)
+
+    def forward_pipelined(self, q, k, v, kv_group=None):
+        """Forward only, for long sequences where moving K and V dominates: the K/V
+        all-gathers run per head on `kv_group` (a second communicator over the
+        same ranks, so they proceed while the selection's own collectives run on
+        this module's group), the selection is computed meanwhile, and the
+        attention of head h starts as soon as head h's K and V have arrived, so
+        it overlaps the transfer of the later heads.  Returns this rank's o."""
+        world, rank, nblk, a = self._geometry(q)
+        if world == 1:
+            sel = self.select(q, k)
+            return self.ops.attn_fwd(q, k, v, sel, bs=self.bs, causal=self.causal, q_blk0=a,
+                                     want_lse=False)[0]
+        kvg = kv_group if kv_group is not None else self.group
+        k, v = k.contiguous(), v.contiguous()
+        B, H, n = k.shape[:3]
+        kf = torch.empty((B, H, world * n) + tuple(k.shape[3:]), dtype=k.dtype, device=k.device)
+        vf = torch.empty_like(kf)
+        works = [[] for _ in range(H)]
+        for h in range(H):
+            for b in range(B):
+                works[h].append(dist.all_gather_into_tensor(kf[b, h], k[b, h], group=kvg,
+                                                            async_op=True))
+                works[h].append(dist.all_gather_into_tensor(vf[b, h], v[b, h], group=kvg,
+                                                            async_op=True))
+        sel = self._select(q, k, None)
+        o = torch.empty_like(q, memory_format=torch.contiguous_format)
+        for h in range(H):
+            for w in works[h]:
+                w.wait()
+            self.ops.attn_fwd(q[:, h:h + 1], kf[:, h:h + 1], vf[:, h:h + 1], sel[:, h:h + 1],
+                              bs=self.bs, causal=self.causal, q_blk0=a, out=o[:, h:h + 1],
+                              want_lse=False)
+        return o
 
     def backward(self, q, o, do, ctx):
         """Returns this rank's (dq, dk, dv) shards; dk/dv are summed over ranks."""

@@ -91,7 +91,10 @@ def _nccl_worker(rank, world, port, L, out_q):
         qs, ks, vs, dos = (t[:, :, sl].contiguous() for t in (q, k, v, do))
         o, ctx = m.forward(qs, ks, vs)
         dq, dk, dv = m.backward(qs, o, dos, ctx)
+        kv_group = dist.new_group(list(range(world)))
+        o2 = m.forward_pipelined(qs, ks, vs, kv_group=kv_group)   # per-head pipelined forward
         torch.cuda.synchronize()
+        assert torch.equal(o, o2)
         out_q.put((rank, ctx[2].cpu().numpy(), o.float().cpu().numpy(), dq.float().cpu().numpy(),
                    dk.float().cpu().numpy(), dv.float().cpu().numpy()))
     finally:
