@@ -119,7 +119,11 @@ bsa_status bsa_attn_fwd(const bsa_attn_args *a, bsa_stream_t stream);
  * Replaces triton_kernel.bsattn_backward (reference src/triton_kernel.py:210-234,
  * kernel :77-181).  dk/dv are produced per key block over a CSR transpose of
  * sel (no float atomics; bitwise deterministic).  Needs a device workspace of
- * bsa_attn_bwd_workspace(a) bytes, 256-byte aligned. */
+ * bsa_attn_bwd_workspace(a) bytes, 256-byte aligned.  For block 64 / head dim
+ * 64 in bf16/f16 without dgate the workspace also holds every 64x64 dS tile of
+ * the active entries (B*Hq*nq*kk*8 KB, 4.6 GB at 262k tokens x 8 heads, kk 17;
+ * at most 24 GB, beyond which the recomputing dQ path is used): the dK/dV
+ * kernel writes them and the dQ kernel reads them back. */
 size_t bsa_attn_bwd_workspace(const bsa_attn_args *a);
 bsa_status bsa_attn_bwd(const bsa_attn_args *a, void *workspace, size_t workspace_bytes,
                         bsa_stream_t stream);
