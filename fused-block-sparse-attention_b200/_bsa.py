@@ -57,13 +57,17 @@ class AttnArgs(ctypes.Structure):
         ("gate", ctypes.c_void_p), ("gate_sb", ctypes.c_int64), ("gate_sh", ctypes.c_int64),
         ("gate_sn", ctypes.c_int64),
         ("lse", ctypes.c_void_p), ("dgate", ctypes.c_void_p), ("status", ctypes.c_void_p),
-        ("q_blk0", ctypes.c_int32), ("Lq", ctypes.c_int32)]
+        ("q_blk0", ctypes.c_int32), ("Lq", ctypes.c_int32),
+        ("rope_cos", ctypes.c_void_p), ("rope_sin", ctypes.c_void_p), ("rope_sb", ctypes.c_int64),
+        ("rope_sl", ctypes.c_int64), ("rope_rot", ctypes.c_int32)]
 
 
 class PoolArgs(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int32) for n in ("dtype", "B", "H", "L", "D", "bs", "nblk", "grp")] + [
         ("x", View), ("mean", ctypes.c_void_p), ("vmin", ctypes.c_void_p),
-        ("vmax", ctypes.c_void_p), ("status", ctypes.c_void_p)]
+        ("vmax", ctypes.c_void_p), ("status", ctypes.c_void_p),
+        ("rope_cos", ctypes.c_void_p), ("rope_sin", ctypes.c_void_p), ("rope_sb", ctypes.c_int64),
+        ("rope_sl", ctypes.c_int64), ("rope_rot", ctypes.c_int32)]
 
 
 class SelectArgs(ctypes.Structure):
@@ -302,12 +306,14 @@ def _base_args(q, k, v, bs, mask_mode, causal, scale, sel, gate, q_blk0=None):
 
 
 def attn_fwd(q, k, v, sel, gate=None, *, bs, causal, mask_mode=MASK_SLOT, scale=None,
-             out=None, out_gate=None, want_lse=True, q_blk0=None):
+             out=None, out_gate=None, want_lse=True, q_blk0=None, rope=None):
     """Block-sparse attention forward (bsa_attn_fwd).  Returns (o, lse or None).
     `out` may be a strided (B,Hq,L,D) view (e.g. a transpose of (B,L,Hq,D)).
-    q_blk0: q is the query shard starting at that block (k, v: the whole sequence)."""
+    q_blk0: q is the query shard starting at that block (k, v: the whole sequence).
+    rope=(cos, sin): rotate q inside the kernel (k must be rotated already)."""
     q, k, v = _prep(q), _prep(k), _prep(v)
     a, keep = _base_args(q, k, v, bs, mask_mode, causal, scale, sel, gate, q_blk0)
+    keep_rope = _set_rope(a, q, rope) if rope is not None else None
     a.q, a.k, a.v = _view4(q), _view4(k), _view4(v)
     o = torch.empty_like(q, memory_format=torch.contiguous_format) if out is None else out
     a.o = _view4(o)
@@ -349,8 +355,26 @@ def attn_bwd(q, k, v, o, do, sel, lse, gate=None, *, bs, causal, mask_mode=MASK_
     return dq, dk, dv, dgate
 
 
-def pool(x, bs, *, grp=1, mean=True, vmin=False, vmax=False):
-    """Block pooling (bsa_pool) of a (B,H,L,D) tensor -> fp32 (B,H/grp,nblk,D) tensors."""
+def _rope_tables(x, rope):
+    """(cos, sin) of (L, rot) or (B, L, rot) -> contiguous (B|1, L, rot) in x's dtype."""
+    cos, sin = rope
+    if cos.dim() == 2:
+        cos, sin = cos.unsqueeze(0), sin.unsqueeze(0)
+    return cos.to(x.dtype).contiguous(), sin.to(x.dtype).contiguous()
+
+
+def _set_rope(a, x, rope):
+    cos, sin = _rope_tables(x, rope)
+    a.rope_cos, a.rope_sin = cos.data_ptr(), sin.data_ptr()
+    a.rope_sb = cos.stride(0) if cos.shape[0] > 1 else 0
+    a.rope_sl = cos.stride(1)
+    a.rope_rot = cos.shape[-1]
+    return cos, sin
+
+
+def pool(x, bs, *, grp=1, mean=True, vmin=False, vmax=False, rope=None):
+    """Block pooling (bsa_pool) of a (B,H,L,D) tensor -> fp32 (B,H/grp,nblk,D) tensors.
+    rope=(cos, sin): pool the partially rotated rows (bsa_rope's arithmetic) instead."""
     _need_cuda(x)
     if not _tma_ok(x):
         x = x.contiguous()
@@ -360,6 +384,7 @@ def pool(x, bs, *, grp=1, mean=True, vmin=False, vmax=False):
     a.dtype = _dtype(x)
     a.B, a.H, a.L, a.D, a.bs, a.nblk, a.grp = B, H, L, D, bs, nblk, grp
     a.x = _view4(x)
+    keep = _set_rope(a, x, rope) if rope is not None else None
     outs = []
     for flag, name in ((mean, "mean"), (vmin, "vmin"), (vmax, "vmax")):
         if flag:

@@ -34,6 +34,10 @@ struct AttnParams {
   // kernel and read back by the dQ kernel that consumes them (null: dQ
   // recomputes S and dP itself): bf16/f16 [B][Hq][nq][kk][64 keys][64 rows]
   void *ds;
+  // partial rotary embedding of q applied inside the forward (null: none)
+  const void *rope_cos, *rope_sin;
+  int64_t rope_sb, rope_sl;
+  int rope_rot;
   int32_t *status;
 };
 

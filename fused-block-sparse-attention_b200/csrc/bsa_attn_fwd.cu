@@ -523,6 +523,13 @@ bsa_status run_attn_fwd(const bsa_attn_args *a, cudaStream_t st) {
     return fail(BSA_ERR_UNSUPPORTED, "attn_fwd: no fp32 kernel for (bs, D) = (" +
                                          std::to_string(a->bs) + ", " + std::to_string(a->D) + ")");
   }
+  if (a->rope_cos) {
+    // the in-kernel rotation of q lives in the block-128 tcgen05 kernel
+    if (!fwd_b128_applicable(a) || a->D != 256)
+      return fail(BSA_ERR_UNSUPPORTED,
+                  "attn_fwd: rope inside the kernel needs block 128, D 256, 16-bit types");
+    return launch_fwd_b128(a, p, st);
+  }
   if (fwd_sm100_applicable(a)) return launch_fwd_sm100(a, p, st);
   if (fwd_b128_applicable(a)) return launch_fwd_b128(a, p, st);
   if (a->dtype == BSA_BF16) return dispatch_fwd_tc<__nv_bfloat16>(a, p, st);

@@ -74,7 +74,7 @@ __global__ void __launch_bounds__(G8_THREADS, G8<D>::MINB)
   uint8_t *sR = sQ + NCH * G8_TILE;         // K/V ring: NSL chunk slots
   uint8_t *sP = sR + NSL * G8_TILE;         // P: keys 0-63 at sP, 64-127 at sP + TILE
   __shared__ __align__(8) uint64_t bar_q, r_full[NSL], r_empty[NSL], s_full, s_empty, p_full,
-      o_done;
+      o_done, q_ready;
   __shared__ uint32_t tmem_base_sh;
   constexpr int MAXN = G8<D>::MAXN;
   __shared__ int s_item[MAXN];   // (kb << 3) | kind of the j-th live slot
@@ -131,6 +131,7 @@ __global__ void __launch_bounds__(G8_THREADS, G8<D>::MINB)
     mbar_init(&s_empty, 8);  // one arrive per softmax warp
     mbar_init(&p_full, 8);
     mbar_init(&o_done, 1);
+    mbar_init(&q_ready, 8);  // one arrive per softmax warp once q is rotated (rope)
     fence_mbar_init();
   }
   if (warp == G8_WMMA) {
@@ -172,7 +173,8 @@ __global__ void __launch_bounds__(G8_THREADS, G8<D>::MINB)
   } else if (warp == G8_WMMA) {
     // ================= MMA issuer
     if (lane == 0) {
-      if (!mbar_wait(&bar_q, 0)) report(p.status, BSA_DEVERR_TIMEOUT);
+      if (!mbar_wait((D == 256 && p.rope_cos) ? &q_ready : &bar_q, 0))
+        report(p.status, BSA_DEVERR_TIMEOUT);
       const uint64_t dq = tc05::sdesc(smem_u32(sQ), 16, 1024);
       int n = 0;
       auto issue_s = [&](int js) {
@@ -221,6 +223,37 @@ __global__ void __launch_bounds__(G8_THREADS, G8<D>::MINB)
     const float *gaterow = (p.gate && p.sel)
                                ? p.gate + b * p.gate_sb + hk * p.gate_sh + (long long)qi * p.gate_sn
                                : nullptr;
+    if constexpr (D == 256) if (p.rope_cos) {
+      // partial rotary embedding of q in shared memory, before the first S MMA:
+      // the rotary dims (< rope_rot <= 64) all lie in Q's first 64-column chunk;
+      // item = (row, group of 8 pairs), 16-byte loads of the swizzled tile
+      if (!mbar_wait(&bar_q, 0)) report(p.status, BSA_DEVERR_TIMEOUT);
+      const int half = p.rope_rot / 2, ng = half / 8;
+      for (int it = warp * 32 + lane; it < G8_BS * ng; it += 256) {
+        const int row = it / ng, i0 = 8 * (it % ng), i1 = i0 + half;
+        const long long pos = (long long)qblk * p.bs + row;
+        if (pos >= p.L) continue;
+        uint4 *a0 = reinterpret_cast<uint4 *>(sQ + swz(0, G8_BS, row, i0));
+        uint4 *a1 = reinterpret_cast<uint4 *>(sQ + swz(0, G8_BS, row, i1));
+        const T *cs = reinterpret_cast<const T *>(p.rope_cos) + b * p.rope_sb + pos * p.rope_sl;
+        const T *sn = reinterpret_cast<const T *>(p.rope_sin) + b * p.rope_sb + pos * p.rope_sl;
+        const uint4 ux0 = *a0, ux1 = *a1;
+        const uint4 uc0 = *reinterpret_cast<const uint4 *>(cs + i0), uc1 = *reinterpret_cast<const uint4 *>(cs + i1);
+        const uint4 us0 = *reinterpret_cast<const uint4 *>(sn + i0), us1 = *reinterpret_cast<const uint4 *>(sn + i1);
+        const T *x0 = reinterpret_cast<const T *>(&ux0), *x1 = reinterpret_cast<const T *>(&ux1);
+        const T *c0 = reinterpret_cast<const T *>(&uc0), *c1 = reinterpret_cast<const T *>(&uc1);
+        const T *s0 = reinterpret_cast<const T *>(&us0), *s1 = reinterpret_cast<const T *>(&us1);
+        uint4 uy0, uy1;
+        T *y0 = reinterpret_cast<T *>(&uy0), *y1 = reinterpret_cast<T *>(&uy1);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) rope_pair<T>(x0[e], x1[e], c0[e], s0[e], c1[e], s1[e], y0[e], y1[e]);
+        *a0 = uy0;
+        *a1 = uy1;
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) tc05::mbar_arrive(&q_ready);
+    }
     float m_used = -INFINITY, l = 0.f;
     for (int j = 0; j < nsteps; ++j) {
       if (!mbar_wait(&s_full, j & 1)) report(p.status, BSA_DEVERR_TIMEOUT);

@@ -113,6 +113,17 @@ bsa_status fill_attn_params(const bsa_attn_args *a, AttnParams *p, bool bwd) {
   P.og_sh = a->out_gate.sh;
   P.og_sl = a->out_gate.sl;
   P.lse = a->lse;
+  if (a->rope_cos) {
+    if (bwd) return fail(BSA_ERR_ARG, "attn_bwd: rope is forward-only (pass the rotated q)");
+    if (!a->rope_sin || a->rope_rot <= 0 || a->rope_rot % 16 || a->rope_rot > 64 ||
+        a->rope_rot > a->D)
+      return fail(BSA_ERR_ARG, "attn_fwd: rope needs cos and sin and 16 <= rot <= 64, rot % 16 == 0");
+    P.rope_cos = a->rope_cos;
+    P.rope_sin = a->rope_sin;
+    P.rope_sb = a->rope_sb;
+    P.rope_sl = a->rope_sl;
+    P.rope_rot = a->rope_rot;
+  }
   P.q = a->q.ptr;
   P.q_sb = a->q.sb;
   P.q_sh = a->q.sh;

@@ -208,6 +208,20 @@ __device__ __forceinline__ float ex2(float x) {
 
 constexpr float kLog2e = 1.4426950408889634f;
 
+// One rotary pair with transformers' op-by-op rounding to T (apply_rotary_pos_emb
+// in the tensor dtype): y0 = x0*c0 + (-x1)*s0, y1 = x1*c1 + x0*s1, each product
+// and each sum rounded to T.  Shared by bsa_rope, the rope-aware pooling and the
+// in-kernel rotation of q so that all three produce identical values.
+template <typename T>
+__device__ __forceinline__ void rope_pair(T x0t, T x1t, T c0t, T s0t, T c1t, T s1t, T &y0, T &y1) {
+  const float x0 = Mma<T>::to_f(x0t), x1 = Mma<T>::to_f(x1t);
+  auto rd = [](float v) { return Mma<T>::to_f(Mma<T>::from_f(v)); };
+  const float t0 = rd(__fmul_rn(x0, Mma<T>::to_f(c0t))), u0 = rd(__fmul_rn(-x1, Mma<T>::to_f(s0t)));
+  const float t1 = rd(__fmul_rn(x1, Mma<T>::to_f(c1t))), u1 = rd(__fmul_rn(x0, Mma<T>::to_f(s1t)));
+  y0 = Mma<T>::from_f(__fadd_rn(t0, u0));
+  y1 = Mma<T>::from_f(__fadd_rn(t1, u1));
+}
+
 // Packed fp32 pairs (sm_100 f32x2 arithmetic: one instruction for two lanes of
 // work, each element rounded exactly as the scalar instruction would).
 #define BSA_F32X2_OP(name, op)                                                            \

@@ -45,24 +45,51 @@ __global__ void pool_kernel(const bsa_pool_args a, int Hout) {
       mx[e] = -INFINITY;
     }
     const T *x = reinterpret_cast<const T *>(a.x.ptr) + b * a.x.sb + dg * V;
+    // rope-aware pooling: this column group's rotated values need the partner
+    // group half a rotation away (16-bit types; rope_rot % 16 == 0)
+    const int half = a.rope_rot / 2;
+    const bool rot = sizeof(T) == 2 && a.rope_cos && dg * V < a.rope_rot;
+    const bool lowhalf = dg * V < half;
+    const long long pofs = lowhalf ? half : -half;  // partner column offset
+    // reads the 8 (or 4) values of head hh, row gr, rotated when needed
+    auto load = [&](long long hh, long long gr, float *out) {
+      const uint4 u = *reinterpret_cast<const uint4 *>(x + hh * a.x.sh + gr * a.x.sl);
+      const T *ue = reinterpret_cast<const T *>(&u);
+      if constexpr (sizeof(T) == 2) {
+        if (rot) {
+          const uint4 w = *reinterpret_cast<const uint4 *>(x + hh * a.x.sh + gr * a.x.sl + pofs);
+          const T *we = reinterpret_cast<const T *>(&w);
+          const T *cs = reinterpret_cast<const T *>(a.rope_cos) + b * a.rope_sb + gr * a.rope_sl;
+          const T *sn = reinterpret_cast<const T *>(a.rope_sin) + b * a.rope_sb + gr * a.rope_sl;
+          const int c0 = lowhalf ? dg * V : dg * V - half;  // the pair's low index
+#pragma unroll
+          for (int e = 0; e < V; ++e) {
+            const T lo = lowhalf ? ue[e] : we[e], hi = lowhalf ? we[e] : ue[e];
+            T y0, y1;
+            rope_pair<T>(lo, hi, cs[c0 + e], sn[c0 + e], cs[c0 + half + e], sn[c0 + half + e], y0,
+                         y1);
+            out[e] = tof(lowhalf ? y0 : y1);
+          }
+          return;
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < V; ++e) out[e] = tof(ue[e]);
+    };
     for (int row = 0; row < a.bs; ++row) {
       const long long gr = (long long)blk * a.bs + row;
       float val[V];
       if (gr < a.L) {
         if (a.grp == 1) {
-          const uint4 u = *reinterpret_cast<const uint4 *>(x + ho * a.x.sh + gr * a.x.sl);
-          const T *ue = reinterpret_cast<const T *>(&u);
-#pragma unroll
-          for (int e = 0; e < V; ++e) val[e] = tof(ue[e]);
+          load(ho, gr, val);
         } else {
 #pragma unroll
           for (int e = 0; e < V; ++e) val[e] = 0.f;
           for (int gi = 0; gi < a.grp; ++gi) {
-            const uint4 u = *reinterpret_cast<const uint4 *>(
-                x + (long long)(ho * a.grp + gi) * a.x.sh + gr * a.x.sl);
-            const T *ue = reinterpret_cast<const T *>(&u);
+            float ve[V];
+            load((long long)(ho * a.grp + gi), gr, ve);
 #pragma unroll
-            for (int e = 0; e < V; ++e) val[e] = __fadd_rn(val[e], tof(ue[e]));
+            for (int e = 0; e < V; ++e) val[e] = __fadd_rn(val[e], ve[e]);
           }
 #pragma unroll
           for (int e = 0; e < V; ++e) val[e] = __fdiv_rn(val[e], (float)a.grp);
@@ -95,6 +122,9 @@ bsa_status run_pool(const bsa_pool_args *a, cudaStream_t st) {
     return fail(BSA_ERR_SHAPE, "pool: bad shape (need H % grp == 0, nblk == ceil(L/bs))");
   if (a->grp > 1 && (a->vmin || a->vmax))
     return fail(BSA_ERR_ARG, "pool: min/max need grp == 1");
+  if (a->rope_cos && (!a->rope_sin || a->dtype == BSA_F32 || a->rope_rot <= 0 ||
+                      a->rope_rot % 16 || a->rope_rot > a->D))
+    return fail(BSA_ERR_ARG, "pool: rope needs cos/sin, a 16-bit dtype and rot % 16 == 0, rot <= D");
   const int V = a->dtype == BSA_F32 ? 4 : 8;
   if (a->D % V) return fail(BSA_ERR_SHAPE, "pool: D must be a multiple of 16 bytes");
   const size_t es = elem_size(a->dtype);
@@ -420,11 +450,71 @@ __global__ void rope_kernel(const bsa_rope_args a) {
   }
 }
 
+// Vectorised form (16-bit types, rot % 16 == 0, 16-byte rows): one thread per
+// (row, group of 8 pairs), plus pass-through groups of 8 when y is not x.
+template <typename T>
+__global__ void rope_vec_kernel(const bsa_rope_args a) {
+  const int half = a.rot / 2;
+  const int ng = half / 8, npass = (a.x.ptr != a.y.ptr) ? (a.D - a.rot) / 8 : 0;
+  const int per_row = ng + npass;
+  const long long n = (long long)a.B * a.H * a.L * per_row;
+  for (long long t = blockIdx.x * (long long)blockDim.x + threadIdx.x; t < n;
+       t += (long long)gridDim.x * blockDim.x) {
+    const int g = (int)(t % per_row);
+    long long r = t / per_row;
+    const int l = (int)(r % a.L);
+    r /= a.L;
+    const int h = (int)(r % a.H);
+    const int b = (int)(r / a.H);
+    const T *x = reinterpret_cast<const T *>(a.x.ptr) + b * a.x.sb + h * a.x.sh + (long long)l * a.x.sl;
+    T *y = reinterpret_cast<T *>(a.y.ptr) + b * a.y.sb + h * a.y.sh + (long long)l * a.y.sl;
+    if (g >= ng) {
+      const int d = a.rot + 8 * (g - ng);
+      *reinterpret_cast<uint4 *>(y + d) = *reinterpret_cast<const uint4 *>(x + d);
+      continue;
+    }
+    const int i0 = 8 * g, i1 = i0 + half;
+    const T *c = reinterpret_cast<const T *>(a.cos) + b * a.cs_sb + (long long)l * a.cs_sl;
+    const T *s = reinterpret_cast<const T *>(a.sin) + b * a.cs_sb + (long long)l * a.cs_sl;
+    const uint4 ux0 = *reinterpret_cast<const uint4 *>(x + i0), ux1 = *reinterpret_cast<const uint4 *>(x + i1);
+    const uint4 uc0 = *reinterpret_cast<const uint4 *>(c + i0), uc1 = *reinterpret_cast<const uint4 *>(c + i1);
+    const uint4 us0 = *reinterpret_cast<const uint4 *>(s + i0), us1 = *reinterpret_cast<const uint4 *>(s + i1);
+    const T *x0 = reinterpret_cast<const T *>(&ux0), *x1 = reinterpret_cast<const T *>(&ux1);
+    const T *c0 = reinterpret_cast<const T *>(&uc0), *c1 = reinterpret_cast<const T *>(&uc1);
+    const T *s0 = reinterpret_cast<const T *>(&us0), *s1 = reinterpret_cast<const T *>(&us1);
+    uint4 uy0, uy1;
+    T *y0 = reinterpret_cast<T *>(&uy0), *y1 = reinterpret_cast<T *>(&uy1);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) rope_pair<T>(x0[e], x1[e], c0[e], s0[e], c1[e], s1[e], y0[e], y1[e]);
+    *reinterpret_cast<uint4 *>(y + i0) = uy0;
+    *reinterpret_cast<uint4 *>(y + i1) = uy1;
+  }
+}
+
 bsa_status run_rope(const bsa_rope_args *a, cudaStream_t st) {
   if (!a->x.ptr || !a->y.ptr || !a->cos || !a->sin) return fail(BSA_ERR_ARG, "rope: NULL pointer");
   if (a->rot <= 0 || a->rot % 2 || a->rot > a->D || a->B <= 0 || a->H <= 0 || a->L <= 0)
     return fail(BSA_ERR_SHAPE, "rope: need 0 < rot <= D, rot even");
   const int half = a->rot / 2;
+  {
+    const size_t es = elem_size(a->dtype);
+    auto al = [&](const void *p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+    const bool vec = a->dtype != BSA_F32 && a->rot % 16 == 0 && a->D % 8 == 0 && al(a->x.ptr) &&
+                     al(a->y.ptr) && al(a->cos) && al(a->sin) && (a->x.sb * es) % 16 == 0 &&
+                     (a->x.sh * es) % 16 == 0 && (a->x.sl * es) % 16 == 0 &&
+                     (a->y.sb * es) % 16 == 0 && (a->y.sh * es) % 16 == 0 &&
+                     (a->y.sl * es) % 16 == 0 && (a->cs_sb * es) % 16 == 0 && (a->cs_sl * es) % 16 == 0;
+    if (vec) {
+      const int per_row = half / 8 + ((a->x.ptr != a->y.ptr) ? (a->D - a->rot) / 8 : 0);
+      const long long n = (long long)a->B * a->H * a->L * per_row;
+      const long long blocks = std::max<long long>(1, std::min<long long>((n + 255) / 256, 1LL << 20));
+      if (a->dtype == BSA_BF16)
+        rope_vec_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, st>>>(*a);
+      else
+        rope_vec_kernel<__half><<<(unsigned)blocks, 256, 0, st>>>(*a);
+      return check_launch("rope");
+    }
+  }
   const int per_row = half + ((a->x.ptr != a->y.ptr) ? a->D - a->rot : 0);
   const long long n = (long long)a->B * a->H * a->L * per_row;
   const int threads = 256;

@@ -184,18 +184,30 @@ def qwen_attention(q, k, v, cos, sin, gate, *, selector, topk, bs, scale=None):
     q: (B, Hq, L, D) pre-RoPE; k: (B, Hkv, L, D) pre-RoPE; v: (B, Hkv, L, D);
     cos/sin: (L, rot) or (B, L, rot); gate: (B, L, Hq*D) output gate.
     Returns (B, L, Hq*D) = attention(rope(q), rope(k), v) * sigmoid(gate), written
-    directly in that layout by the attention epilogue."""
+    directly in that layout by the attention epilogue.
+
+    With SelectMax (or all blocks) and head dim 256 the rotation of q is folded
+    into the kernels: the selection pools rope(q) inside its pooling kernel and
+    the attention rotates its q tile in shared memory after loading it, so the
+    rotated q (the largest tensor here) is never written; k, shared by the query
+    heads of its group, is rotated once by bsa_rope."""
     B, Hq, L, D = q.shape
-    qr = _bsa.rope(q, cos, sin)
     kr = _bsa.rope(k, cos, sin)
+    nblk = (L + bs - 1) // bs
+    fold = D == 256 and bs == 128 and q.dtype != torch.float32 and \
+        (isinstance(selector, (SelectMax, SelectAll)) or (selector is None and topk >= nblk))
+    qr = q if fold else _bsa.rope(q, cos, sin)
     out = torch.empty(B, L, Hq, D, dtype=q.dtype, device=q.device)
     og = gate.reshape(B, L, Hq, D).transpose(1, 2)
     nblk = (L + bs - 1) // bs
     scale = D ** -0.5 if scale is None else scale
     if (selector is None and topk >= nblk) or isinstance(selector, SelectAll):
         sel = None
+    elif fold:
+        sel = select_quest(q, kr, bs=bs, topk=selector.topk, sink=selector.sink, rope=(cos, sin))
     else:
         sel = selector.select(qr, kr).to(torch.int32)
     _bsa.attn_fwd(qr, kr, v, sel, None, bs=bs, causal=True, mask_mode=_bsa.MASK_TOKEN, scale=scale,
-                  out=out.transpose(1, 2), out_gate=og, want_lse=False)
+                  out=out.transpose(1, 2), out_gate=og, want_lse=False,
+                  rope=(cos, sin) if fold else None)
     return out.view(B, L, Hq * D)

@@ -32,12 +32,14 @@ def select_meanpool(q, k, *, bs, topk, causal=True, want_gate=False, want_score=
     return sel, gate, score
 
 
-def select_quest(q, k, *, bs, topk, sink=True):
+def select_quest(q, k, *, bs, topk, sink=True, rope=None):
     """q (B, Hq, L, D), k (B, Hkv, L, D) -> int32 (B, Hkv, nblk, min(topk,nblk)+1+sink),
     sorted ascending: top-k by sum_d max(q_d*kmax_d, q_d*kmin_d) with q mean-pooled over
-    the query group and the block, causal, missing picks -> own, plus own and sink."""
+    the query group and the block, causal, missing picks -> own, plus own and sink.
+    rope=(cos, sin): q is pooled after its partial rotary embedding (computed inside
+    the pooling kernel, the values of bsa_rope), so the rotated q is never stored."""
     grp = q.shape[1] // k.shape[1]
-    (qp,) = _bsa.pool(q, bs, grp=grp)
+    (qp,) = _bsa.pool(q, bs, grp=grp, rope=rope)
     kmin, kmax = _bsa.pool(k, bs, mean=False, vmin=True, vmax=True)
     sel, _, _ = _bsa.select(qp, kmax, kmin, kind=_bsa.SCORE_QUEST, layout=_bsa.SEL_FINISH,
                             topk=topk, sink=sink)

@@ -106,6 +106,17 @@ typedef struct {
    * multiple of bs unless the range ends at L.  No reference counterpart: used by
    * the query-block sharding across GPUs. */
   int32_t q_blk0, Lq;
+  /* Forward only, optional (rope_cos NULL = none): the partial rotary embedding
+   * of q is applied inside the attention kernel, after q is loaded and before
+   * the first product, with the arithmetic of bsa_rope (transformers'
+   * apply_rotary_pos_emb, each product and sum rounded to the dtype).  cos/sin:
+   * (B, L, rope_rot) in q's dtype with element strides rope_sb (0 = shared over
+   * the batch) and rope_sl, indexed by the token position.  Supported by the
+   * block-128 tcgen05 kernel at D 256, rope_rot a multiple of 16, at most 64 (the
+   * Qwen configuration: 64 of 256 dims).  k must already be rotated. */
+  const void *rope_cos, *rope_sin;
+  int64_t rope_sb, rope_sl;
+  int32_t rope_rot;
 } bsa_attn_args;
 
 /* Forward: o = softmax(q k^T * scale + gate + mask) v over the selected blocks.
@@ -142,6 +153,13 @@ typedef struct {
   bsa_view x;
   float *mean, *vmin, *vmax;
   int32_t *status;
+  /* Optional (rope_cos NULL = none): pool the rows of x after the partial rotary
+   * embedding of bsa_rope (same rounding), without writing the rotated tensor:
+   * cos/sin (B, L, rope_rot) in x's dtype, strides rope_sb (0 = shared), rope_sl;
+   * rope_rot a multiple of 16. */
+  const void *rope_cos, *rope_sin;
+  int64_t rope_sb, rope_sl;
+  int32_t rope_rot;
 } bsa_pool_args;
 bsa_status bsa_pool(const bsa_pool_args *a, bsa_stream_t stream);
 

@@ -381,3 +381,47 @@ def test_centroid_module_matches_oracle_attention(cuda, monkeypatch):
                           mask_mode=seen["mode"])
         err = (seen["out"].detach().float().cpu() - ref).abs().max().item()
         assert err < 1e-4, err
+
+
+@pytest.mark.parametrize("grp,D,rot", [(8, 256, 64), (1, 256, 64), (2, 64, 32)])
+def test_rope_aware_pooling_equals_pooling_rotated(cuda, grp, D, rot):
+    """bsa_pool with rope=(cos, sin) pools exactly the values bsa_rope writes."""
+    import _bsa
+    gen = torch.Generator().manual_seed(grp + D)
+    B, Hkv, L, bs = 1, 2, 1000, 128
+    x = torch.randn(B, Hkv * grp, L, D, generator=gen).to(torch.bfloat16).to(cuda)
+    cos, sin = O.rope_cos_sin(L, rot, 1e7, torch.bfloat16)
+    cos, sin = cos.to(cuda), sin.to(cuda)
+    xr = _bsa.rope(x, cos, sin)
+    a = _bsa.pool(x, bs, grp=grp, rope=(cos, sin))
+    r = _bsa.pool(xr, bs, grp=grp)
+    assert torch.equal(a[0], r[0])
+    if grp == 1:
+        a2 = _bsa.pool(x, bs, mean=False, vmin=True, vmax=True, rope=(cos, sin))
+        r2 = _bsa.pool(xr, bs, mean=False, vmin=True, vmax=True)
+        assert torch.equal(a2[0], r2[0]) and torch.equal(a2[1], r2[1])
+
+
+def test_rope_inside_attention_equals_rotated_input(cuda):
+    """bsa_attn_fwd with the rotation of q folded in (block 128, D 256) gives the
+    same output, bit for bit, as the forward on bsa_rope(q); the Qwen drop-in
+    (which folds it) matches the unfolded composition."""
+    import _bsa
+    import qwen_blocksparse as qb
+    gen = torch.Generator().manual_seed(5)
+    B, Hq, Hkv, L, D, bs, rot = 1, 8, 2, 2048 + 77, 256, 128, 64
+    q = torch.randn(B, Hq, L, D, generator=gen).to(torch.bfloat16).to(cuda)
+    k, v = (torch.randn(B, Hkv, L, D, generator=gen).to(torch.bfloat16).to(cuda) for _ in range(2))
+    cos, sin = (t.to(cuda) for t in O.rope_cos_sin(L, rot, 1e7, torch.bfloat16))
+    kr = _bsa.rope(k, cos, sin)
+    qr = _bsa.rope(q, cos, sin)
+    sel = qb.SelectMax(4, bs).select(qr, kr).to(torch.int32)
+    kw = dict(bs=bs, causal=True, mask_mode=_bsa.MASK_TOKEN, want_lse=False)
+    o1, _ = _bsa.attn_fwd(qr, kr, v, sel, **kw)
+    o2, _ = _bsa.attn_fwd(q, kr, v, sel, rope=(cos, sin), **kw)
+    assert torch.equal(o1, o2)
+    o3, _ = _bsa.attn_fwd(q, kr, v, None, rope=(cos, sin), **kw)    # all blocks
+    o4, _ = _bsa.attn_fwd(qr, kr, v, None, **kw)
+    assert torch.equal(o3, o4)
+    import selection
+    assert torch.equal(selection.select_quest(q, kr, bs=bs, topk=4, rope=(cos, sin)), sel)
