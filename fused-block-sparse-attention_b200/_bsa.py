@@ -115,6 +115,12 @@ class CsrArgs(ctypes.Structure):
         ("status", ctypes.c_void_p), ("q_blk0", ctypes.c_int32), ("nq", ctypes.c_int32)]
 
 
+class CentroidArgs(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in ("B", "nblk", "C", "cpq", "cap", "dim", "rk")] + [
+        ("key_cent", ctypes.c_void_p), ("top_c", ctypes.c_void_p), ("q_blk", ctypes.c_void_p),
+        ("k_blk", ctypes.c_void_p), ("sel", ctypes.c_void_p)]
+
+
 class RopeArgs(ctypes.Structure):
     _fields_ = [(n, ctypes.c_int32) for n in ("dtype", "B", "H", "L", "D", "rot")] + [
         ("x", View), ("y", View), ("cos", ctypes.c_void_p), ("sin", ctypes.c_void_p),
@@ -142,6 +148,8 @@ SYMBOLS = {
                                    ctypes.c_void_p]),
     "bsa_sel_csr_noalloc": (ctypes.c_int, [ctypes.POINTER(CsrArgs), ctypes.c_void_p]),
     "bsa_rope": (ctypes.c_int, [ctypes.POINTER(RopeArgs), ctypes.c_void_p]),
+    "bsa_centroid_width": (ctypes.c_int32, [ctypes.POINTER(CentroidArgs)]),
+    "bsa_centroid_route": (ctypes.c_int, [ctypes.POINTER(CentroidArgs), ctypes.c_void_p]),
     "bsa_decode_workspace": (ctypes.c_size_t, [ctypes.POINTER(DecodeArgs)]),
     "bsa_decode": (ctypes.c_int, [ctypes.POINTER(DecodeArgs), ctypes.c_void_p, ctypes.c_size_t,
                                   ctypes.c_void_p]),
@@ -589,6 +597,32 @@ def sel_csr(sel, *, bs, L, causal, mask_mode=MASK_SLOT):
     ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=sel.device)
     _check(Lb.bsa_sel_csr(ctypes.byref(c), ctypes.c_void_p(ws.data_ptr()), nbytes, _stream()))
     return row_ptr, col
+
+
+def centroid_route(key_cent, top_c, *, C, cap, q_blk=None, k_blk=None, rk=None):
+    """CentroidSSA bucket routing (bsa_centroid_route).  key_cent (B, nblk) and top_c
+    (B, nblk, cpq) integer centroid ids; optional refine with fp32 q_blk / k_blk
+    (B, nblk, dim) keeping rk candidates.  Returns int32 (B, nblk, 1 + m): the own
+    block, then the candidates (-1 = empty)."""
+    _need_cuda(key_cent, top_c)
+    kc = key_cent.to(torch.int32).contiguous()
+    tc = top_c.to(torch.int32).contiguous()
+    B, nblk = kc.shape
+    a = CentroidArgs()
+    a.B, a.nblk, a.C, a.cpq, a.cap = B, nblk, C, tc.shape[-1], cap
+    a.key_cent, a.top_c = kc.data_ptr(), tc.data_ptr()
+    keep = []
+    if q_blk is not None and rk is not None:
+        qb = q_blk.float().contiguous()
+        kb = k_blk.float().contiguous()
+        keep += [qb, kb]
+        a.q_blk, a.k_blk, a.dim, a.rk = qb.data_ptr(), kb.data_ptr(), qb.shape[-1], rk
+    L = lib()
+    W = L.bsa_centroid_width(ctypes.byref(a))
+    sel = torch.empty(B, nblk, W, dtype=torch.int32, device=kc.device)
+    a.sel = sel.data_ptr()
+    _check(L.bsa_centroid_route(ctypes.byref(a), _stream()))
+    return sel
 
 
 def rope(x, cos, sin, *, out=None):

@@ -19,6 +19,8 @@ int32_t lsh_width(const bsa_lsh_args *a);
 size_t lsh_workspace(const bsa_lsh_args *a);
 bsa_status run_lsh(const bsa_lsh_args *a, void *ws, size_t ws_bytes, cudaStream_t st);
 bsa_status run_rope(const bsa_rope_args *a, cudaStream_t st);
+int32_t centroid_width(const bsa_centroid_args *a);
+bsa_status run_centroid_route(const bsa_centroid_args *a, cudaStream_t st);
 int32_t scores_width(int nblk, int topk, int sink);
 bsa_status run_scores_topk(const bsa_scores_args *a, cudaStream_t st);
 bsa_status run_qmax(const bsa_qmax_args *a, cudaStream_t st);
@@ -253,6 +255,13 @@ bsa_status bsa_select_qmax(const bsa_qmax_args *a, bsa_stream_t stream) {
 bsa_status bsa_rope(const bsa_rope_args *a, bsa_stream_t stream) {
   if (!a) return fail(BSA_ERR_ARG, "rope: args is NULL");
   return run_rope(a, reinterpret_cast<cudaStream_t>(stream));
+}
+
+int32_t bsa_centroid_width(const bsa_centroid_args *a) { return a ? centroid_width(a) : 0; }
+
+bsa_status bsa_centroid_route(const bsa_centroid_args *a, bsa_stream_t stream) {
+  if (!a) return fail(BSA_ERR_ARG, "centroid_route: args is NULL");
+  return run_centroid_route(a, reinterpret_cast<cudaStream_t>(stream));
 }
 
 bsa_status bsa_status_decode(int32_t w) {

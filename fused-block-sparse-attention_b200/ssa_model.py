@@ -218,38 +218,24 @@ def centroid_select(sq, sk, cent, *, cpq, cap, refine=None):
     block dropped from them; optional refine = (q_blk, k_blk, rk): keep the rk
     candidates with the largest q_blk_i . k_blk_j.  sq, sk: (B, nblk, s);
     cent: (C, s).  Returns (sel (B, nblk, 1 + m) int64 with the own block first and
-    -1 for empty slots, key_cent (B, nblk), qc (B, nblk, C)).  O(nblk * C) tensors
-    only; no nblk x nblk score matrix.  Ties follow torch's argmax / topk."""
-    B, nblk, _ = sq.shape
+    -1 for empty slots, key_cent (B, nblk), qc (B, nblk, C)).  The centroid scores,
+    argmax and top-cpq are O(nblk * C) tensor ops; the buckets, the gather and the
+    refine step run in one device kernel (bsa_centroid_route); no nblk x nblk
+    tensor exists."""
     C = cent.shape[0]
+    nblk = sq.shape[1]
     cpq, cap = min(cpq, C), min(cap, nblk)
-    dev = sq.device
     kc = sk @ cent.t()
     qc = sq @ cent.t()
     key_cent = kc.argmax(-1)                                            # (B, nblk)
     top_c = qc.topk(cpq, dim=-1).indices                                # (B, nblk, cpq)
-    # bucket lists: a stable sort by centroid keeps block order inside a bucket;
-    # a block's rank is its sorted position minus its bucket's first position
-    order = torch.sort(key_cent, dim=1, stable=True).indices            # (B, nblk)
-    sorted_c = key_cent.gather(1, order)
-    counts = F.one_hot(key_cent, C).sum(1)                              # (B, C)
-    first = torch.cumsum(counts, 1) - counts                            # (B, C)
-    rank = torch.arange(nblk, device=dev).view(1, nblk) - first.gather(1, sorted_c)
-    lists = torch.full((B, C, cap), -1, dtype=torch.long, device=dev)
-    ok = rank < cap
-    bidx = torch.arange(B, device=dev).view(B, 1).expand(B, nblk)
-    lists[bidx[ok], sorted_c[ok], rank[ok]] = order[ok]
-    selb = lists[torch.arange(B, device=dev).view(B, 1, 1), top_c].reshape(B, nblk, cpq * cap)
-    own = torch.arange(nblk, device=dev).view(1, nblk, 1).expand(B, nblk, 1)
-    selb = selb.masked_fill(selb == own, -1)
+    kw = {}
     if refine is not None:
         q_blk, k_blk, rk = refine
         if rk < cpq * cap:
-            valid = selb >= 0
-            kcand = k_blk[torch.arange(B, device=dev).view(B, 1, 1), selb.clamp(min=0)]
-            score = (q_blk.unsqueeze(2) * kcand).sum(-1).masked_fill(~valid, float("-inf"))
-            selb = selb.gather(-1, score.topk(rk, dim=-1).indices)
-    return torch.cat([own, selb], dim=-1), key_cent, qc
+            kw = dict(q_blk=q_blk, k_blk=k_blk, rk=rk)
+    sel = _bsa.centroid_route(key_cent, top_c, C=C, cap=cap, **kw)
+    return sel.long(), key_cent, qc
 
 
 class CentroidSSA(nn.Module):

@@ -324,6 +324,24 @@ bsa_status bsa_sel_csr(const bsa_csr_args *a, void *workspace, size_t workspace_
  * share the array, so calls that overlap on the GPU race.  Allocates nothing. */
 bsa_status bsa_sel_csr_noalloc(const bsa_csr_args *a, bsa_stream_t stream);
 
+/* CentroidSSA's bucket routing (reference src/ssa_model.py:263-299): bucket c
+ * holds the first cap key blocks j (by index) with key_cent[b,j] == c; query
+ * block i reads the buckets of top_c[b,i,0..cpq) (cpq-major, cap-minor), its own
+ * block replaced by -1; with q_blk (refine, rk < cpq*cap) only the rk candidates
+ * of largest q_blk[b,i].k_blk[b,j] (fp32 fma chains over dim) are kept, best
+ * first, -1 for missing picks.  sel: int32 (B, nblk, bsa_centroid_width(a)) with
+ * the own block in column 0.  key_cent / top_c come from the module's
+ * differentiable centroid scores (argmax / top-cpq), which stay in torch. */
+typedef struct {
+  int32_t B, nblk, C, cpq, cap, dim, rk;
+  const int32_t *key_cent; /* (B, nblk) */
+  const int32_t *top_c;    /* (B, nblk, cpq) */
+  const float *q_blk, *k_blk; /* (B, nblk, dim), optional (refine) */
+  int32_t *sel;
+} bsa_centroid_args;
+int32_t bsa_centroid_width(const bsa_centroid_args *a);
+bsa_status bsa_centroid_route(const bsa_centroid_args *a, bsa_stream_t stream);
+
 /* Partial rotary embedding with the arithmetic of transformers'
  * apply_rotary_pos_emb (qwen3_5_moe, v5.5.0): on the first `rot` dims,
  * y = x*cos + rotate_half(x)*sin with each product and the sum rounded to the

@@ -37,7 +37,7 @@ def test_struct_layouts_match_the_header(tmp_path):
                "bsa_select_args": _bsa.SelectArgs, "bsa_lsh_args": _bsa.LshArgs,
                "bsa_csr_args": _bsa.CsrArgs, "bsa_rope_args": _bsa.RopeArgs,
                "bsa_decode_args": _bsa.DecodeArgs, "bsa_scores_args": _bsa.ScoresArgs,
-               "bsa_qmax_args": _bsa.QmaxArgs}
+               "bsa_qmax_args": _bsa.QmaxArgs, "bsa_centroid_args": _bsa.CentroidArgs}
     lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "bsa.h"', "int main(void) {"]
     for cname, cls in structs.items():
         lines.append('printf("%s %%zu\\n", sizeof(%s));' % (cname, cname))

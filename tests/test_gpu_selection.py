@@ -425,3 +425,41 @@ def test_rope_inside_attention_equals_rotated_input(cuda):
     assert torch.equal(o3, o4)
     import selection
     assert torch.equal(selection.select_quest(q, kr, bs=bs, topk=4, rope=(cos, sin)), sel)
+
+
+@pytest.mark.parametrize("B,nblk,C,cpq,cap,refine", [(2, 300, 8, 2, 6, None), (1, 1000, 16, 3, 8, 5),
+                                                     (2, 77, 4, 4, 30, 9), (1, 2048, 32, 2, 64, None)])
+def test_centroid_routing_kernel_vs_oracle(cuda, B, nblk, C, cpq, cap, refine):
+    """The device routing (bsa_centroid_route, with the module's argmax / top-cpq)
+    equals the oracle's tensor-op restatement, with and without the refine step;
+    and on the reference's own goldens."""
+    import ssa_model
+    gen = torch.Generator().manual_seed(nblk + C)
+    s = 16
+    sq, sk = torch.randn(B, nblk, s, generator=gen), torch.randn(B, nblk, s, generator=gen)
+    cent = torch.randn(C, s, generator=gen)
+    rf = None
+    if refine:
+        qb, kb = torch.randn(B, nblk, 24, generator=gen), torch.randn(B, nblk, 24, generator=gen)
+        rf = (qb, kb, refine)
+    ref, rkc, _ = O.centroid_select(sq, sk, cent, cpq=cpq, cap=cap, refine=rf)
+    rfd = tuple(t.to(cuda) for t in rf[:2]) + (refine,) if rf else None
+    got, kc, _ = ssa_model.centroid_select(sq.to(cuda), sk.to(cuda), cent.to(cuda), cpq=cpq, cap=cap,
+                                           refine=rfd)
+    assert torch.equal(kc.cpu(), rkc)
+    assert torch.equal(got.cpu(), ref)
+
+
+@pytest.mark.parametrize("name", ["centroid_plain.npz", "centroid_refine.npz"])
+def test_centroid_routing_kernel_golden(cuda, name):
+    import ssa_model
+    g = golden(name)
+    t = lambda x: torch.from_numpy(np.ascontiguousarray(x)).to(cuda)
+    rk = int(g["refine"])
+    refine = (t(g["q_blk"]), t(g["k_blk"]), rk) if rk > 0 else None
+    sel, _, _ = ssa_model.centroid_select(t(g["sq"]), t(g["sk"]), t(g["cent"]), cpq=int(g["cpq"]),
+                                          cap=int(g["cap"]), refine=refine)
+    sel = sel.cpu().numpy()
+    valid = g["valid"].astype(bool)
+    assert np.array_equal(sel[valid], g["sel"][valid])
+    assert (sel[~valid] == -1).all()

@@ -228,15 +228,15 @@ def test_other_selectors_match_reference():
 
 
 def test_centroid_routing_matches_reference():
-    """ssa_model.centroid_select (torch, no nblk^2 tensor) reproduces CentroidSSA's
-    selection (src/ssa_model.py:254-299), with and without the refine step."""
-    import ssa_model
+    """The oracle's centroid routing (tensor ops, no nblk^2 tensor) reproduces
+    CentroidSSA's selection (src/ssa_model.py:254-299), with and without the refine
+    step."""
     for name in ("centroid_plain.npz", "centroid_refine.npz"):
         g = golden(name)
         rk = int(g["refine"])
         refine = (_t(g["q_blk"]), _t(g["k_blk"]), rk) if rk > 0 else None
-        sel, _, _ = ssa_model.centroid_select(_t(g["sq"]), _t(g["sk"]), _t(g["cent"]),
-                                              cpq=int(g["cpq"]), cap=int(g["cap"]), refine=refine)
+        sel, _, _ = O.centroid_select(_t(g["sq"]), _t(g["sk"]), _t(g["cent"]),
+                                      cpq=int(g["cpq"]), cap=int(g["cap"]), refine=refine)
         sel = sel.numpy()
         valid = g["valid"].astype(bool)
         assert sel.shape == g["sel"].shape, name
