@@ -306,20 +306,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint8_t *Bs = sm + L.b + s * TB;
       // column norms of this key tile (thread t: key row t of the stage)
       {
-        float nb = 0.f;
-#pragma unroll 4
+        // four independent chains (only an upper bound is needed: the 1.0001
+        // factor covers any summation order's rounding)
+        float n0 = 0.f, n1 = 0.f, n2 = 0.f, n3 = 0.f;
+#pragma unroll
         for (int d = 0; d < DIM; d += 4) {
           const float4 x = *reinterpret_cast<const float4 *>(Bs + off(row, d));
-          nb = fmaf(x.x, x.x, nb);
-          nb = fmaf(x.y, x.y, nb);
-          nb = fmaf(x.z, x.z, nb);
-          nb = fmaf(x.w, x.w, nb);
+          n0 = fmaf(x.x, x.x, n0);
+          n1 = fmaf(x.y, x.y, n1);
+          n2 = fmaf(x.z, x.z, n2);
+          n3 = fmaf(x.w, x.w, n3);
         }
-        nbs[row] = sqrtf(nb) * 1.0001f;
+        // the tile's largest key norm: one bound for every column of the tile
+        float nbm = sqrtf((n0 + n1) + (n2 + n3)) * 1.0001f;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) nbm = fmaxf(nbm, __shfl_xor_sync(0xffffffffu, nbm, o));
+        if (lane == 0) nbs[warp] = nbm;
       }
       named_bar_sync(1, 128);  // norms written; every epilogue warp sees the same e_err
       if (e_err) break;
       const int cend = min(kN, jend - k0);  // columns < cend may be valid for this row
+      const float nbmax = fmaxf(fmaxf(nbs[0], nbs[1]), fmaxf(nbs[2], nbs[3]));
+      const float cut = __fsub_rd(Ls[KT - 1], __fmul_ru(ka, nbmax));
       // 1. candidate masks of the four 32-column chunks, branch-free: valid
       //    columns, and the approximate score against the current threshold
       unsigned mk[kN / 32];
@@ -338,17 +346,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int lim = min(max(cend - cc, 0), 32);
         unsigned m = lim >= 32 ? 0xffffffffu : ((1u << lim) - 1u);
         if (jskip >= k0 + cc && jskip < k0 + cc + 32) m &= ~(1u << (jskip - k0 - cc));
-        const float thr = Ls[KT - 1];
+        // S~ >= cut with cut = thr - ka * max|b|, rounded down (directed
+        // rounding keeps the test a superset of S~ + eps >= thr)
         unsigned pass = 0;
-        const float4 *nb4 = reinterpret_cast<const float4 *>(nbs + cc);
 #pragma unroll
-        for (int c4 = 0; c4 < 8; ++c4) {
-          const float4 nb = nb4[c4];
-          pass |= (unsigned)(fmaf(ka, nb.x, v[4 * c4 + 0]) >= thr) << (4 * c4 + 0);
-          pass |= (unsigned)(fmaf(ka, nb.y, v[4 * c4 + 1]) >= thr) << (4 * c4 + 1);
-          pass |= (unsigned)(fmaf(ka, nb.z, v[4 * c4 + 2]) >= thr) << (4 * c4 + 2);
-          pass |= (unsigned)(fmaf(ka, nb.w, v[4 * c4 + 3]) >= thr) << (4 * c4 + 3);
-        }
+        for (int c = 0; c < 32; ++c) pass |= (unsigned)(v[c] >= cut) << c;
         mk[ch] = m & pass;
       }
       // 2. The candidates of the whole warp are re-scored cooperatively (one per
@@ -571,7 +573,7 @@ bsa_status run_select_tc5(const bsa_select_args *a, int T, int W, cudaStream_t s
   // query tiles to fill the SMs (one resident CTA per SM); measured on B200:
   // clusters of 4 fill best, clusters of 8 schedule worse than 4
   int C = 1;
-  while (C < 4 && (long long)nqt * a->G * C * 2 <= 2LL * nsm && C * 2 <= std::max(1, nkt / 2)) C *= 2;
+  while (C < 4 && (long long)nqt * a->G * C * 2 <= nsm && C * 2 <= std::max(1, nkt / 2)) C *= 2;
   if (const char *e = getenv("BSA_SELECT_SPLIT")) C = std::max(1, std::min(8, atoi(e)));
   const int smem = layout(a->dim).total + 1024;
   void (*kern)(const CUtensorMap, const CUtensorMap, const bsa_select_args, int, int, int) = nullptr;
