@@ -5,25 +5,29 @@
 // the key-block CSR plan, each a key block of one KV head with up to 32 listed
 // (query block, slot) entries.  The key block's K and V stay in shared memory
 // as the stationary A operands; the listed query blocks stream through a
-// 4-stage ring (Q, dO by TMA, lse and Dvec rows by bulk copy).
+// 5-stage ring (Q, dO by TMA, lse and Dvec rows by bulk copy).
 //
 // Per step j (one entry and query head of each tile):
 //   S^T  = K  Q_j^T    dP^T = V dO_j^T         (tcgen05, fp32 in TMEM, 2 buffers)
 //   P^T  = 2^(S^T*scale*log2e + gate - lse_j)  dS^T = P^T (dP^T - Dvec_j)
-//   dV  += P^T dO_j    dK  += dS^T Q_j          (tcgen05, accumulators in TMEM)
-// The elementwise step has no cross-column dependency, so every row (key) is
-// split over two warps of the same TMEM quadrant (32 columns each): 8 warps.
+//   dV  += P^T dO_j    dK  += dS^T Q_j          (tcgen05, A operand in TMEM)
+// P^T and dS^T (16-bit pairs) are written back over the step's own S^T and dP^T
+// columns, so they are double-buffered with them and need no shared memory.
+// The two tiles run as independent pipelines: each has its own S/dP buffers,
+// hand-off barriers and dK/dV accumulators; they share only the ring stage.
 //
 // Warp roles (320 threads, one CTA per SM):
-//   warps 0-7  elementwise: TMEM -> registers, P^T / dS^T (bf16) -> shared
-//              memory in the 128B-swizzled K-major layout, final dK / dV.
+//   warps 0-3  elementwise for tile A, warps 4-7 for tile B: each warp owns the
+//              tile's 16 TMEM lanes of its quadrant (16x32bx2 loads and
+//              stores), writes P^T / dS^T to TMEM, dS^T rows to global memory
+//              for the dQ pass, and the final dK / dV.
 //   warp 8     TMA producer: the warp reads a unit's CSR entries and gate values
-//              at once, then one thread issues the ring loads.
+//              at once, then one thread publishes the unit to the other warps
+//              and issues the ring loads.
 //   warp 9     TMEM allocation (512 columns) and the MMA-issuing thread, which
-//              polls two queues: dV/dK of step j as soon as P/dS are written,
-//              S/dP of the next step as soon as its ring stage has landed.
+//              polls per tile an S/dP queue and a dV/dK queue.
 // TMEM columns: S^T [0,64) [64,128), dP^T [128,192) [192,256), dV [256,320),
-// dK [320,384); tile B at lane offset 16.
+// dK [320,384), second accumulator pair at +128; tile B at lane offset 16.
 #include <algorithm>
 #include <type_traits>
 
@@ -37,11 +41,10 @@ namespace {
 constexpr int B5_BS = 64, B5_D = 64;
 constexpr int B5_TILE = B5_BS * B5_D * 2;            // 8 KB
 constexpr int B5_ROWB = B5_BS * 4;                   // one lse / Dvec row chunk
-// NKV K/V buffers, NST ring stages, NPD P^T/dS^T buffers
-constexpr int b5_smem(int NST, int NPD, int NKV) {
+// NKV K/V buffers, NST ring stages
+constexpr int b5_smem(int NST, int NKV) {
   return 1024 + NKV * 4 * B5_TILE    // K, V of both tiles
          + NST * 4 * B5_TILE         // ring: (stage, tile) Q, dO
-         + NPD * 4 * B5_TILE         // P^T, dS^T of both tiles
          + NST * 2 * 2 * B5_ROWB;    // ring: (stage, tile) lse, Dvec
 }
 constexpr uint32_t B5_TMEM_COLS = 512;
@@ -83,7 +86,7 @@ __device__ __forceinline__ void b5_unit(const BwdPlan &pl, const AttnParams &p, 
 
 // GATE: a gate tensor is present (without one the exponent's offset is -lse, which
 // folds into the FMA)
-template <typename T, int B5_NST, int NPD, int NKV, bool GATE>
+template <typename T, int B5_NST, int NKV, bool GATE>
 __global__ void __launch_bounds__(320, 1)
     attn_dkdv_sm100_kernel(const __grid_constant__ CUtensorMap tq,
                            const __grid_constant__ CUtensorMap tdo,
@@ -99,18 +102,26 @@ __global__ void __launch_bounds__(320, 1)
                                               ~uintptr_t(1023));
   uint8_t *sKV = smem;                       // (buffer, tile): K, V
   uint8_t *sR = sKV + NKV * 4 * B5_TILE;     // (stage, tile): Q, dO
-  uint8_t *sPD = sR + B5_NST * 4 * B5_TILE;  // (buffer, tile): P^T, dS^T
-  float *sRow = reinterpret_cast<float *>(sPD + NPD * 4 * B5_TILE);  // (stage, tile): lse[64], Dvec[64]
-  // p_full[b] / g_done[b]: P/dS of a step with parity b written / consumed by
-  // its dV/dK MMAs.  One barrier per buffer: with two buffers the elementwise
-  // warps may run one step ahead of the MMA issuer, and a single barrier would
-  // then be two phases ahead of its waiter (ambiguous parity).
+  float *sRow = reinterpret_cast<float *>(sR + B5_NST * 4 * B5_TILE);  // (stage, tile): lse[64], Dvec[64]
+  // per tile and TMEM buffer b (the step's parity): s_full (S^T, dP^T computed),
+  // p_full (P^T, dS^T written over them), s_empty (the step's dV/dK MMAs, the
+  // last readers of the buffer, are done)
   __shared__ __align__(8) uint64_t kv_full[NKV], kv_empty[NKV], r_full[B5_NST], r_empty[B5_NST],
-      s_full[2], s_empty[2], p_full[NPD], g_done[NPD], acc_empty[2];
+      s_full[2][2], s_empty[2][2], p_full[2][2], acc_empty[2][2];
   __shared__ uint32_t tmem_base_sh;
   // per ring stage and tile: (local query block, slot, query head) and the gate
   // value of the step, written by the producer before it arrives on r_full
   __shared__ int s_meta[B5_NST][2][3];
+  // per non-empty work unit (ring of 8, indexed by the unit's ordinal): the two
+  // tiles' step counts and max(n0, n1), -1 after the last unit; written by the
+  // producer before it arms the unit's K/V barrier, read by the MMA issuer
+  __shared__ int s_unit[8][3];
+  // every work unit (ring of 8, indexed by the unit's position in this CTA's
+  // sequence) for the elementwise warps, per tile: steps, key block, batch,
+  // KV head, valid, chunks of the bin, partial index base; and (u mod Y)
+  __shared__ int s_eu[8][2][7];
+  __shared__ int s_euy[8];
+  __shared__ __align__(8) uint64_t eu_full[8], eu_empty[8];
   __shared__ float s_g2[B5_NST][2];
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -118,22 +129,28 @@ __global__ void __launch_bounds__(320, 1)
   const int nunits = (int)((total + 1) / 2) * pl.Y;
 
   if (tid == 0) {
+    // per tile t: s_full/p_full/s_empty (S^T, dP^T buffers and the P^T, dS^T
+    // written over them), acc_empty (dK/dV accumulators); the ring stage and the K/V buffer are
+    // released by both tiles' MMAs (two commits each)
     for (int s = 0; s < NKV; ++s) {
       mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&kv_empty[s], 2);
     }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&s_full[s], 1);
-      mbar_init(&s_empty[s], 256);
-      mbar_init(&acc_empty[s], 256);
-    }
-    for (int s = 0; s < NPD; ++s) {
-      mbar_init(&g_done[s], 1);
-      mbar_init(&p_full[s], 256);
+    for (int t = 0; t < 2; ++t) {
+      for (int s = 0; s < 2; ++s) {
+        mbar_init(&s_full[t][s], 1);
+        mbar_init(&s_empty[t][s], 1);
+        mbar_init(&p_full[t][s], 128);
+        mbar_init(&acc_empty[t][s], 128);
+      }
     }
     for (int s = 0; s < B5_NST; ++s) {
       mbar_init(&r_full[s], 1);
-      mbar_init(&r_empty[s], 1);
+      mbar_init(&r_empty[s], 2);
+    }
+    for (int s = 0; s < 8; ++s) {
+      mbar_init(&eu_full[s], 1);
+      mbar_init(&eu_empty[s], 8);  // lane 0 of each elementwise warp
     }
     fence_mbar_init();
   }
@@ -152,17 +169,36 @@ __global__ void __launch_bounds__(320, 1)
     // at once; lane 0 then issues the loads step by step from shared memory.
     __shared__ int s_pq[2][32], s_ps[2][32];
     __shared__ float s_pg[2][32];
-    int gs = 0, ne = 0;
+    int gs = 0, ne = 0, iu = 0;
     uint32_t idle = 0;
-    for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
+    for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++iu) {
       B5Unit w;
       b5_unit(pl, p, total, u, w);
       const int ns = max(w.n[0], w.n[1]);
-      if (ns == 0) continue;
       if (w.b[0] < 0 || w.b[0] >= p.B || w.b[1] < 0 || w.b[1] >= p.B) {
         report(p.status, BSA_DEVERR_INDEX);  // self-check: keep every address in range
         w.b[0] = w.b[1] = 0;
       }
+      if (lane == 0) {
+        // publish the unit to the elementwise warps (every unit, empty ones too:
+        // their valid tiles still write zero dK / dV)
+        const int eb = iu & 7;
+        if (iu >= 8 && !mbar_wait(&eu_empty[eb], ((iu >> 3) - 1) & 1))
+          report(p.status, BSA_DEVERR_TIMEOUT);
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          s_eu[eb][t][0] = w.n[t];
+          s_eu[eb][t][1] = w.kb[t];
+          s_eu[eb][t][2] = w.b[t];
+          s_eu[eb][t][3] = w.hk[t];
+          s_eu[eb][t][4] = w.valid[t];
+          s_eu[eb][t][5] = w.nch[t];
+          s_eu[eb][t][6] = w.poff[t] + w.cidx[t];
+        }
+        s_euy[eb] = u % pl.Y;
+        tc05::mbar_arrive(&eu_full[eb]);
+      }
+      if (ns == 0) continue;
       __syncwarp();  // lane 0 is done with the previous unit's entries
 #pragma unroll
       for (int t = 0; t < 2; ++t) {
@@ -191,6 +227,9 @@ __global__ void __launch_bounds__(320, 1)
       const int kvb = ne % NKV;
       if (ne >= NKV && !mbar_wait(&kv_empty[kvb], ((ne / NKV) - 1) & 1))
         report(p.status, BSA_DEVERR_TIMEOUT);
+      s_unit[ne & 7][0] = w.n[0];
+      s_unit[ne & 7][1] = w.n[1];
+      s_unit[ne & 7][2] = ns;
       mbar_expect_tx(&kv_full[kvb], ((w.n[0] > 0) + (w.n[1] > 0)) * 2 * B5_TILE);
       #pragma unroll
       for (int t = 0; t < 2; ++t) {
@@ -241,98 +280,119 @@ __global__ void __launch_bounds__(320, 1)
           }
         }
     }
+    if (lane == 0) {
+      // end of the unit sequence for the MMA issuer
+      const int kvb = ne % NKV;
+      if (ne >= NKV && !mbar_wait(&kv_empty[kvb], ((ne / NKV) - 1) & 1))
+        report(p.status, BSA_DEVERR_TIMEOUT);
+      s_unit[ne & 7][0] = s_unit[ne & 7][1] = 0;
+      s_unit[ne & 7][2] = -1;
+      tc05::mbar_arrive(&kv_full[kvb]);
+    }
   } else if (warp == 9) {
-    // ================= MMA issuer: S/dP queue and dV/dK queue, polled
+    // ================= MMA issuer: per tile an S/dP queue and a dV/dK queue, polled
     if (lane == 0) {
       // descriptors built once; per MMA only a 64-bit add
       const uint64_t dkv0 = tc05::sdesc(smem_u32(sKV), 16, 1024);          // K, V (A, K-major)
       const uint64_t drk0 = tc05::sdesc(smem_u32(sR), 16, 1024);           // Q, dO as K-major B
       const uint64_t drm0 = tc05::sdesc(smem_u32(sR), B5_BS * 128, 1024);  // Q, dO as MN-major B
-      const uint64_t dpd0 = tc05::sdesc(smem_u32(sPD), 16, 1024);          // P^T, dS^T (A)
-      // S queue state
-      int us = blockIdx.x, js = 0, gss = 0, nes = -1;
-      B5Unit ws;
-      bool have_s = false;
-      // G queue state
-      int ug = blockIdx.x, jg = 0, gsg = 0, neg = -1;
-      B5Unit wg;
-      bool have_g = false;
+      // queue state per tile: S (js, gss, nes) and G (jg, gsg, neg); the units
+      // (ordinals ne = 0, 1, ...) come from the producer's s_unit ring: an S
+      // queue opens unit nes once its K/V barrier has completed
+      int js[2], gss[2], nes[2], jg[2], gsg[2], neg[2];
+      int sn[2], gn[2], sns[2], gns[2];  // tile length and unit length of the current units
+      bool s_open[2], have_s[2], have_g[2];
       uint32_t idle = 0;
-      auto next_unit = [&](int &u, B5Unit &w, int &ne) -> bool {
-        for (; u < nunits; u += gridDim.x) {
-          b5_unit(pl, p, total, u, w);
-          if (max(w.n[0], w.n[1]) > 0) {
-            ++ne;
-            return true;
-          }
-        }
-        return false;
-      };
-      have_s = next_unit(us, ws, nes);
-      have_g = next_unit(ug, wg, neg);
-      while (have_g) {
+#pragma unroll
+      for (int t = 0; t < 2; ++t) {
+        js[t] = jg[t] = gss[t] = gsg[t] = 0;
+        nes[t] = neg[t] = 0;
+        s_open[t] = false;
+        have_s[t] = have_g[t] = true;
+        sn[t] = gn[t] = sns[t] = gns[t] = 0;
+      }
+      while (have_g[0] || have_g[1]) {
         bool progress = false;
-        // ---- dV += P^T dO, dK += dS^T Q for step (ug, jg)
-        if (gsg < gss && mbar_test(&p_full[gsg % NPD], (gsg / NPD) & 1) &&
-            (jg > 0 || neg < 2 || mbar_test(&acc_empty[neg & 1], ((neg >> 1) - 1) & 1))) {
-          const int st = gsg % B5_NST, ab = neg & 1;
-          tc05::fence_after();
-          #pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            if (jg >= wg.n[t]) continue;
-            const uint32_t roff = (st * 2 + t) * 2 * B5_TILE;        // Q; dO at + TILE
-            const uint32_t poff = ((gsg % NPD) * 2 + t) * 2 * B5_TILE;  // P^T; dS^T at + TILE
-            const uint64_t ap = tc05::dadd(dpd0, poff), ads = tc05::dadd(dpd0, poff + B5_TILE);
-            const uint64_t bdo = tc05::dadd(drm0, roff + B5_TILE), bq = tc05::dadd(drm0, roff);
-            const uint32_t dv = tc05::taddr(tmem, 16 * t, B5_DVCOL + 128 * ab);
-            const uint32_t dk = tc05::taddr(tmem, 16 * t, B5_DKCOL + 128 * ab);
 #pragma unroll
-            for (int ks = 0; ks < B5_BS / 16; ++ks) {
-              const uint32_t acc = (jg > 0 || ks > 0) ? 1u : 0u;
-              tc05::mma_f16(dv, tc05::dadd(ap, ks * 32), tc05::dadd(bdo, ks * 2048), IDESC_KM, acc);
-              tc05::mma_f16(dk, tc05::dadd(ads, ks * 32), tc05::dadd(bq, ks * 2048), IDESC_KM, acc);
+        for (int t = 0; t < 2; ++t) {
+          // ---- open the next unit of tile t's S queue once its K/V have landed
+          if (have_s[t] && !s_open[t] && mbar_test(&kv_full[nes[t] % NKV], (nes[t] / NKV) & 1)) {
+            sns[t] = s_unit[nes[t] & 7][2];
+            sn[t] = s_unit[nes[t] & 7][t];
+            if (sns[t] < 0) {
+              have_s[t] = false;
+            } else {
+              s_open[t] = true;
             }
+            progress = true;
           }
-          tc05::commit(&r_empty[st]);
-          tc05::commit(&g_done[gsg % NPD]);
-          ++gsg;
-          if (++jg == max(wg.n[0], wg.n[1])) {
-            jg = 0;
-            ug += gridDim.x;
-            have_g = next_unit(ug, wg, neg);
-          }
-          progress = true;
-        }
-        // ---- S^T = K Q^T, dP^T = V dO^T for step (us, js)
-        if (have_s && mbar_test(&r_full[gss % B5_NST], (gss / B5_NST) & 1) &&
-            (gss < 2 || mbar_test(&s_empty[gss & 1], ((gss >> 1) - 1) & 1)) &&
-            (js > 0 || mbar_test(&kv_full[nes % NKV], (nes / NKV) & 1))) {
-          const int st = gss % B5_NST, bb = gss & 1;
-          tc05::fence_after();
-          #pragma unroll
-          for (int t = 0; t < 2; ++t) {
-            if (js >= ws.n[t]) continue;
-            const uint32_t roff = (st * 2 + t) * 2 * B5_TILE;          // Q; dO at + TILE
-            const uint32_t koff = ((nes % NKV) * 2 + t) * 2 * B5_TILE;  // K; V at + TILE
-            const uint64_t ak = tc05::dadd(dkv0, koff), av = tc05::dadd(dkv0, koff + B5_TILE);
-            const uint64_t bq = tc05::dadd(drk0, roff), bdo = tc05::dadd(drk0, roff + B5_TILE);
-            const uint32_t ds = tc05::taddr(tmem, 16 * t, B5_SCOL + 64 * bb);
-            const uint32_t ddp = tc05::taddr(tmem, 16 * t, B5_DPCOL + 64 * bb);
+          // ---- dV += P^T dO, dK += dS^T Q of tile t, step gsg[t] (its unit neg[t]
+          // was opened by the S queue, which runs ahead)
+          if (have_g[t] && gsg[t] < gss[t] &&
+              mbar_test(&p_full[t][gsg[t] & 1], (gsg[t] >> 1) & 1) &&
+              (jg[t] > 0 || neg[t] < 2 ||
+               mbar_test(&acc_empty[t][neg[t] & 1], ((neg[t] >> 1) - 1) & 1))) {
+            if (jg[t] == 0) {
+              gns[t] = s_unit[neg[t] & 7][2];
+              gn[t] = s_unit[neg[t] & 7][t];
+            }
+            const int st = gsg[t] % B5_NST, ab = neg[t] & 1, bb = gsg[t] & 1;
+            tc05::fence_after();
+            if (jg[t] < gn[t]) {
+              const uint32_t roff = (st * 2 + t) * 2 * B5_TILE;  // Q; dO at + TILE
+              const uint64_t bdo = tc05::dadd(drm0, roff + B5_TILE), bq = tc05::dadd(drm0, roff);
+              // P^T and dS^T (16-bit pairs) over the step's S^T and dP^T columns
+              const uint32_t ap = tc05::taddr(tmem, 16 * t, B5_SCOL + 64 * bb);
+              const uint32_t ads = tc05::taddr(tmem, 16 * t, B5_DPCOL + 64 * bb);
+              const uint32_t dv = tc05::taddr(tmem, 16 * t, B5_DVCOL + 128 * ab);
+              const uint32_t dk = tc05::taddr(tmem, 16 * t, B5_DKCOL + 128 * ab);
 #pragma unroll
-            for (int ks = 0; ks < B5_D / 16; ++ks) {
-              tc05::mma_f16(ds, tc05::dadd(ak, ks * 32), tc05::dadd(bq, ks * 32), IDESC_KK, ks > 0);
-              tc05::mma_f16(ddp, tc05::dadd(av, ks * 32), tc05::dadd(bdo, ks * 32), IDESC_KK, ks > 0);
+              for (int ks = 0; ks < B5_BS / 16; ++ks) {
+                const uint32_t acc = (jg[t] > 0 || ks > 0) ? 1u : 0u;
+                tc05::mma_f16_ts(dv, ap + ks * 8, tc05::dadd(bdo, ks * 2048), IDESC_KM, acc);
+                tc05::mma_f16_ts(dk, ads + ks * 8, tc05::dadd(bq, ks * 2048), IDESC_KM, acc);
+              }
             }
+            tc05::commit(&r_empty[st]);  // count 2: the stage is free once both tiles are done
+            tc05::commit(&s_empty[t][bb]);
+            ++gsg[t];
+            if (++jg[t] == gns[t]) {
+              jg[t] = 0;
+              ++neg[t];
+              have_g[t] = have_s[t] || neg[t] < nes[t];
+            }
+            progress = true;
+          } else if (have_g[t] && !have_s[t] && gsg[t] == gss[t]) {
+            have_g[t] = false;  // every opened step is done and no unit follows
           }
-          tc05::commit(&s_full[bb]);
-          ++gss;
-          if (++js == max(ws.n[0], ws.n[1])) {
-            tc05::commit(&kv_empty[nes % NKV]);  // last reader of this unit's K/V
-            js = 0;
-            us += gridDim.x;
-            have_s = next_unit(us, ws, nes);
+          // ---- S^T = K Q^T, dP^T = V dO^T of tile t, step gss[t]
+          if (s_open[t] && mbar_test(&r_full[gss[t] % B5_NST], (gss[t] / B5_NST) & 1) &&
+              (gss[t] < 2 || mbar_test(&s_empty[t][gss[t] & 1], ((gss[t] >> 1) - 1) & 1))) {
+            const int st = gss[t] % B5_NST, bb = gss[t] & 1;
+            tc05::fence_after();
+            if (js[t] < sn[t]) {
+              const uint32_t roff = (st * 2 + t) * 2 * B5_TILE;             // Q; dO at + TILE
+              const uint32_t koff = ((nes[t] % NKV) * 2 + t) * 2 * B5_TILE;  // K; V at + TILE
+              const uint64_t ak = tc05::dadd(dkv0, koff), av = tc05::dadd(dkv0, koff + B5_TILE);
+              const uint64_t bq = tc05::dadd(drk0, roff), bdo = tc05::dadd(drk0, roff + B5_TILE);
+              const uint32_t ds = tc05::taddr(tmem, 16 * t, B5_SCOL + 64 * bb);
+              const uint32_t ddp = tc05::taddr(tmem, 16 * t, B5_DPCOL + 64 * bb);
+#pragma unroll
+              for (int ks = 0; ks < B5_D / 16; ++ks) {
+                tc05::mma_f16(ds, tc05::dadd(ak, ks * 32), tc05::dadd(bq, ks * 32), IDESC_KK, ks > 0);
+                tc05::mma_f16(ddp, tc05::dadd(av, ks * 32), tc05::dadd(bdo, ks * 32), IDESC_KK, ks > 0);
+              }
+            }
+            tc05::commit(&s_full[t][bb]);
+            ++gss[t];
+            if (++js[t] == sns[t]) {
+              tc05::commit(&kv_empty[nes[t] % NKV]);  // count 2: last readers of the K/V buffer
+              js[t] = 0;
+              ++nes[t];
+              s_open[t] = false;
+            }
+            progress = true;
           }
-          progress = true;
         }
         if (progress) {
           idle = 0;
@@ -346,71 +406,71 @@ __global__ void __launch_bounds__(320, 1)
       }
     }
   } else {
-    // ================= elementwise warps 0-7
-    const int quad = warp & 3, hf = warp >> 2;
-    const int t = lane >> 4;
+    // ================= elementwise warps 0-7: warps 0-3 tile A, warps 4-7 tile B,
+    // so that the two tiles' steps run as independent pipelines.  Each warp
+    // reads its tile's 16 TMEM lanes of its quadrant (16x32bx2 loads): thread
+    // (lane) = key row quad*16 + (lane & 15), 16 query columns at
+    // 32*g + 16*(lane >> 4) for g = 0, 1.
+    const int quad = warp & 3, t = warp >> 2, hh = lane >> 4;
     const int kr = quad * 16 + (lane & 15);  // key row within the block
-    const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
-    int gs = 0, ne = 0;
+    const uint32_t lane_base = (uint32_t)(quad * 32 + 16 * t) << 16;
+    int gs = 0, ne = 0, iu = 0;
     uint64_t evict_first;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(evict_first));
-    for (int u = blockIdx.x; u < nunits; u += gridDim.x) {
-      B5Unit w;
-      b5_unit(pl, p, total, u, w);
-      const int ns = max(w.n[0], w.n[1]);
-      // this thread's tile by selects (a runtime index would put the unit in local memory)
-      const int nmine = t ? w.n[1] : w.n[0], kb = t ? w.kb[1] : w.kb[0];
-      const int b = t ? w.b[1] : w.b[0], hk = t ? w.hk[1] : w.hk[0];
-      const bool wvalid = t ? w.valid[1] : w.valid[0];
-      const int wnch = t ? w.nch[1] : w.nch[0];
-      const int wpc = t ? w.poff[1] + w.cidx[1] : w.poff[0] + w.cidx[0];
+    for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++iu) {
+      // the unit as the producer published it
+      const int eb = iu & 7;
+      if (!mbar_wait(&eu_full[eb], (iu >> 3) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
+      const int ns = max(s_eu[eb][0][0], s_eu[eb][1][0]);
+      const int nmine = s_eu[eb][t][0], kb = s_eu[eb][t][1];
+      const int b = s_eu[eb][t][2], hk = s_eu[eb][t][3];
+      const bool wvalid = s_eu[eb][t][4] != 0;
+      const int wnch = s_eu[eb][t][5];
+      const int wpc = s_eu[eb][t][6];
+      const int uy = s_euy[eb];
+      __syncwarp();
+      if (lane == 0) tc05::mbar_arrive(&eu_empty[eb]);
       const bool key_ok = (long long)kb * p.bs + kr < p.L;
       for (int j = 0; j < ns; ++j, ++gs) {
         const int bb = gs & 1, st = gs % B5_NST;
-        if (!mbar_wait(&s_full[bb], (gs >> 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
+        if (!mbar_wait(&s_full[t][bb], (gs >> 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
         // acquire the stage's TMA / bulk data and the producer's metadata
         if (!mbar_wait(&r_full[st], (gs / B5_NST) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
         tc05::fence_after();
-        // two 16-column halves, loaded one after the other (keeps the live
-        // registers under the 168 a 10-warp CTA allows)
         uint32_t wp[16], wd[16];
         const bool active = j < nmine;
         const int qblk = s_meta[st][t][0], slot = s_meta[st][t][1];
         // qblk is the local query block; kb is global
         const bool triu = p.causal && ((p.mask_mode == BSA_MASK_SLOT) ? slot == 0 : kb == p.q0 + qblk);
         const float g2 = GATE ? s_g2[st][t] : 0.f;
-        const float *lsep = sRow + (st * 2 + t) * 2 * B5_BS + 32 * hf;
-        const long long q0 = (long long)qblk * p.bs + 32 * hf;
-        const bool edge = triu || !key_ok || q0 + 32 > p.Lq;
+        const float *lsep = sRow + (st * 2 + t) * 2 * B5_BS;
         float sv[2][16], dp[2][16];
-        tc05::ld16(tmem + lane_base + B5_SCOL + 64 * bb + 32 * hf, sv[0]);
-        tc05::ld16(tmem + lane_base + B5_DPCOL + 64 * bb + 32 * hf, dp[0]);
+        tc05::ld16x2(tmem + lane_base + B5_SCOL + 64 * bb, sv[0]);
+        tc05::ld16x2(tmem + lane_base + B5_DPCOL + 64 * bb, dp[0]);
         tc05::wait_ld();
 #pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {
-          if (h2 == 1) {
-            tc05::ld16(tmem + lane_base + B5_SCOL + 64 * bb + 32 * hf + 16, sv[1]);
-            tc05::ld16(tmem + lane_base + B5_DPCOL + 64 * bb + 32 * hf + 16, dp[1]);
+        for (int g = 0; g < 2; ++g) {
+          const int cg = 32 * g + 16 * hh;  // first query column of this group
+          if (g == 1) {
+            tc05::ld16x2(tmem + lane_base + B5_SCOL + 64 * bb + 32, sv[1]);
+            tc05::ld16x2(tmem + lane_base + B5_DPCOL + 64 * bb + 32, dp[1]);
             tc05::wait_ld();
-            tc05::fence_before();
-            tc05::mbar_arrive(&s_empty[bb]);
           }
           if (active) {
-            if (edge) {  // diagonal / padded steps: explicit masks
+            const long long q0 = (long long)qblk * p.bs + cg;
+            if (triu || !key_ok || q0 + 16 > p.Lq) {  // diagonal / padded steps: explicit masks
 #pragma unroll
-              for (int c = 0; c < 16; ++c) {
-                const int qc = 32 * hf + 16 * h2 + c;
-                if (!key_ok || (triu && kr > qc) || q0 + 16 * h2 + c >= p.Lq) sv[h2][c] = -INFINITY;
-              }
+              for (int c = 0; c < 16; ++c)
+                if (!key_ok || (triu && kr > cg + c) || q0 + c >= p.Lq) sv[g][c] = -INFINITY;
             }
             // pairs of columns through the packed f32x2 pipe (same per-element
             // rounding as the scalar sequence)
             const float2 s22 = make_float2(p.scale2, p.scale2), g22 = make_float2(g2, g2);
 #pragma unroll
             for (int c = 0; c < 16; c += 4) {
-              const float4 a4 = *reinterpret_cast<const float4 *>(lsep + 16 * h2 + c);
-              const float4 d4 = *reinterpret_cast<const float4 *>(lsep + B5_BS + 16 * h2 + c);
-              const float *x = sv[h2], *y = dp[h2];
+              const float4 a4 = *reinterpret_cast<const float4 *>(lsep + cg + c);
+              const float4 d4 = *reinterpret_cast<const float4 *>(lsep + B5_BS + cg + c);
+              const float *x = sv[g], *y = dp[g];
               const float2 e01 = fma2(make_float2(x[c], x[c + 1]), s22,
                                       sub2(g22, make_float2(a4.x, a4.y)));
               const float2 e23 = fma2(make_float2(x[c + 2], x[c + 3]), s22,
@@ -419,7 +479,7 @@ __global__ void __launch_bounds__(320, 1)
               const float2 p23 = make_float2(ex2(e23.x), ex2(e23.y));
               const float2 d01 = mul2(p01, sub2(make_float2(y[c], y[c + 1]), make_float2(d4.x, d4.y)));
               const float2 d23 = mul2(p23, sub2(make_float2(y[c + 2], y[c + 3]), make_float2(d4.z, d4.w)));
-              const int o = 8 * h2 + (c >> 1);
+              const int o = 8 * g + (c >> 1);
               wp[o] = Mma<T>::pack(p01.x, p01.y);
               wp[o + 1] = Mma<T>::pack(p23.x, p23.y);
               wd[o] = Mma<T>::pack(d01.x, d01.y);
@@ -427,53 +487,49 @@ __global__ void __launch_bounds__(320, 1)
             }
           }
         }
-        if (gs >= NPD) {  // dV/dK of step gs-NPD read P / dS buffer gs % NPD
-          if (!mbar_wait(&g_done[gs % NPD], ((gs / NPD) - 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
-          tc05::fence_after();
-        }
         if (active) {
-          const uint32_t pa = smem_u32(sPD + ((gs % NPD) * 2 + t) * 2 * B5_TILE);
+          // P^T / dS^T over the S^T / dP^T columns just read (this warp's loads of
+          // all 64 columns have completed): query column c -> column c / 2
 #pragma unroll
-          for (int c8 = 0; c8 < 4; ++c8) {
-            const int col = 32 * hf + 8 * c8;
-            asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(swz(pa, B5_BS, kr, col)),
-                         "r"(wp[4 * c8]), "r"(wp[4 * c8 + 1]), "r"(wp[4 * c8 + 2]), "r"(wp[4 * c8 + 3])
-                         : "memory");
-            asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(swz(pa + B5_TILE, B5_BS, kr, col)),
-                         "r"(wd[4 * c8]), "r"(wd[4 * c8 + 1]), "r"(wd[4 * c8 + 2]), "r"(wd[4 * c8 + 3])
-                         : "memory");
+          for (int g = 0; g < 2; ++g) {
+            tc05::st16x2_8(tmem + lane_base + B5_SCOL + 64 * bb + 16 * g, wp + 8 * g);
+            tc05::st16x2_8(tmem + lane_base + B5_DPCOL + 64 * bb + 16 * g, wd + 8 * g);
           }
+          tc05::wait_st();
         }
-        fence_proxy_async_smem();
         tc05::fence_before();
-        tc05::mbar_arrive(&p_full[gs % NPD]);
+        tc05::mbar_arrive(&p_full[t][bb]);
         if (p.ds && active) {
-          // dS^T row of this key for the dQ pass (32 query columns, 64 bytes),
-          // after the MMA hand-off; evict-first so that the stream of dS tiles
-          // does not push the gathered Q / dO rows out of L2
+          // dS^T row of this key for the dQ pass (2 x 16 query columns), after the
+          // MMA hand-off; evict-first so that the stream of dS tiles does not
+          // push the gathered Q / dO rows out of L2
           const int hq = s_meta[st][t][2];
           T *dst = reinterpret_cast<T *>(p.ds) +
-                   (((((long long)b * p.Hq + hq) * p.nq + qblk) * p.kk + slot) * B5_BS + kr) * B5_BS +
-                   32 * hf;
+                   (((((long long)b * p.Hq + hq) * p.nq + qblk) * p.kk + slot) * B5_BS + kr) * B5_BS;
 #pragma unroll
-          for (int c8 = 0; c8 < 4; ++c8)
-            asm volatile("st.global.L2::cache_hint.v4.b32 [%0], {%1,%2,%3,%4}, %5;" ::"l"(dst + 8 * c8),
-                         "r"(wd[4 * c8]), "r"(wd[4 * c8 + 1]), "r"(wd[4 * c8 + 2]),
-                         "r"(wd[4 * c8 + 3]), "l"(evict_first)
-                         : "memory");
+          for (int g = 0; g < 2; ++g)
+#pragma unroll
+            for (int c8 = 0; c8 < 2; ++c8) {
+              const int o = 8 * g + 4 * c8;
+              asm volatile("st.global.L2::cache_hint.v4.b32 [%0], {%1,%2,%3,%4}, %5;" ::"l"(
+                               dst + 32 * g + 16 * hh + 8 * c8),
+                           "r"(wd[o]), "r"(wd[o + 1]), "r"(wd[o + 2]), "r"(wd[o + 3]),
+                           "l"(evict_first)
+                           : "memory");
+            }
         }
       }
-      // ---- dK (scaled) and dV of this unit: this thread's row, columns [32*hf, +32),
-      // one accumulator at a time (32 registers)
+      // ---- dK (scaled) and dV of this unit: this thread's row, its two 16-column
+      // groups, one accumulator at a time
       const int ab = ne & 1;
       if (ns > 0) {
         const int gl = gs - 1;  // last step of this unit
-        if (!mbar_wait(&g_done[gl % NPD], (gl / NPD) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
+        if (!mbar_wait(&s_empty[t][gl & 1], (gl >> 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
         tc05::fence_after();
       }
       long long pidx = -1;
       if (wvalid && wnch > 1) {
-        pidx = (long long)wpc * pl.Y + (u % pl.Y);
+        pidx = (long long)wpc * pl.Y + uy;
         if (pidx < 0 || pidx >= pl.npart * pl.Y) {  // self-check: partial tile in range
           report(p.status, BSA_DEVERR_INDEX);
           pidx = -2;
@@ -481,42 +537,47 @@ __global__ void __launch_bounds__(320, 1)
       }
 #pragma unroll 1
       for (int m = 0; m < 2; ++m) {  // 0: dK, 1: dV
-        float acc[32];
+        float acc[2][16];
         if (ns > 0) {
-          tc05::ld32(tmem + lane_base + (m ? B5_DVCOL : B5_DKCOL) + 128 * ab + 32 * hf, acc);
+          tc05::ld16x2(tmem + lane_base + (m ? B5_DVCOL : B5_DKCOL) + 128 * ab, acc[0]);
+          tc05::ld16x2(tmem + lane_base + (m ? B5_DVCOL : B5_DKCOL) + 128 * ab + 32, acc[1]);
           tc05::wait_ld();
           if (m == 1) {
             tc05::fence_before();
-            tc05::mbar_arrive(&acc_empty[ab]);
+            tc05::mbar_arrive(&acc_empty[t][ab]);
           }
         }
         if (!wvalid) continue;
         if (nmine == 0) {
 #pragma unroll
-          for (int c = 0; c < 32; ++c) acc[c] = 0.f;
+          for (int c = 0; c < 16; ++c) acc[0][c] = acc[1][c] = 0.f;
         }
         if (wnch == 1) {
-          const long long g = (long long)kb * p.bs + kr;
-          if (g < p.L) {
+          const long long gk = (long long)kb * p.bs + kr;
+          if (gk < p.L) {
             const float sc = m ? 1.f : p.scale;
-            T *dst = m ? reinterpret_cast<T *>(p.dv) + b * p.dv_sb + hk * p.dv_sh + g * p.dv_sl
-                       : reinterpret_cast<T *>(p.dk) + b * p.dk_sb + hk * p.dk_sh + g * p.dk_sl;
+            T *dst = m ? reinterpret_cast<T *>(p.dv) + b * p.dv_sb + hk * p.dv_sh + gk * p.dv_sl
+                       : reinterpret_cast<T *>(p.dk) + b * p.dk_sb + hk * p.dk_sh + gk * p.dk_sl;
 #pragma unroll
-            for (int c = 0; c < 32; c += 8) {
-              uint4 a4;
-              a4.x = Mma<T>::pack(acc[c] * sc, acc[c + 1] * sc);
-              a4.y = Mma<T>::pack(acc[c + 2] * sc, acc[c + 3] * sc);
-              a4.z = Mma<T>::pack(acc[c + 4] * sc, acc[c + 5] * sc);
-              a4.w = Mma<T>::pack(acc[c + 6] * sc, acc[c + 7] * sc);
-              *reinterpret_cast<uint4 *>(dst + 32 * hf + c) = a4;
-            }
+            for (int g = 0; g < 2; ++g)
+#pragma unroll
+              for (int c = 0; c < 16; c += 8) {
+                uint4 a4;
+                a4.x = Mma<T>::pack(acc[g][c] * sc, acc[g][c + 1] * sc);
+                a4.y = Mma<T>::pack(acc[g][c + 2] * sc, acc[g][c + 3] * sc);
+                a4.z = Mma<T>::pack(acc[g][c + 4] * sc, acc[g][c + 5] * sc);
+                a4.w = Mma<T>::pack(acc[g][c + 6] * sc, acc[g][c + 7] * sc);
+                *reinterpret_cast<uint4 *>(dst + 32 * g + 16 * hh + c) = a4;
+              }
           }
         } else if (pidx >= 0) {
           float *part = pl.part + pidx * (2LL * B5_BS * B5_D) + m * (B5_BS * B5_D);
 #pragma unroll
-          for (int c = 0; c < 32; c += 4)
-            *reinterpret_cast<float4 *>(part + kr * B5_D + 32 * hf + c) =
-                make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
+          for (int g = 0; g < 2; ++g)
+#pragma unroll
+            for (int c = 0; c < 16; c += 4)
+              *reinterpret_cast<float4 *>(part + kr * B5_D + 32 * g + 16 * hh + c) =
+                  make_float4(acc[g][c], acc[g][c + 1], acc[g][c + 2], acc[g][c + 3]);
         }
       }
       if (ns > 0) ++ne;
@@ -545,21 +606,21 @@ bsa_status launch_dkdv_sm100(int dtype, const CUtensorMap &mq, const CUtensorMap
   cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
   const long long units_max = ((dkv_grid + 1) / 2) * pl.Y;
   const unsigned grid = (unsigned)std::max<long long>(1, std::min<long long>(nsm, units_max));
-  // ring stages / P-dS buffers: 4/1 by default (the deeper ring hides more of
-  // the Q/dO load latency than a second P/dS buffer saves); BSA_DKDV_CFG=32 for 3/2
-  const char *cfg = getenv("BSA_DKDV_CFG");
-  const int variant = cfg ? atoi(cfg) : 41;
-#define BSA_B5_LAUNCH(T_, N_, P_, KV_)                                                      \
+  // ring stages: 5 by default, BSA_DKDV_STAGES=4 for 4
+  const char *cfg = getenv("BSA_DKDV_STAGES");
+  const int variant = cfg ? atoi(cfg) : 5;
+#define BSA_B5_LAUNCH(T_, N_, KV_)                                                          \
   {                                                                                         \
-    auto kern = p.gate ? attn_dkdv_sm100_kernel<T_, N_, P_, KV_, true>                      \
-                       : attn_dkdv_sm100_kernel<T_, N_, P_, KV_, false>;                    \
-    constexpr int sm = b5_smem(N_, P_, KV_);                                                \
+    auto kern = p.gate ? attn_dkdv_sm100_kernel<T_, N_, KV_, true>                          \
+                       : attn_dkdv_sm100_kernel<T_, N_, KV_, false>;                        \
+    constexpr int sm = b5_smem(N_, KV_);                                                    \
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);            \
     kern<<<grid, 320, sm, st>>>(mq, mdo, mk, mv, pq, pdo, pk, pv, p, pl);                   \
   }
 #define BSA_B5_PICK(T_)                                      \
-  if (variant == 32) BSA_B5_LAUNCH(T_, 3, 2, 1)              \
-  else BSA_B5_LAUNCH(T_, 4, 1, 1)
+  if (variant == 4) BSA_B5_LAUNCH(T_, 4, 1)                  \
+  else if (variant == 42) BSA_B5_LAUNCH(T_, 4, 2)            \
+  else BSA_B5_LAUNCH(T_, 5, 1)
   if (dtype == BSA_BF16) {
     BSA_B5_PICK(__nv_bfloat16)
   } else {

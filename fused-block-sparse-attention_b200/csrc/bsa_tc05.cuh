@@ -53,6 +53,19 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem], kind::f16: A (M x K, K-major) in the data-path
+// layout of D with two 16-bit elements per 32-bit column; a K-step of 16 spans 8
+// columns.
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Shared-memory matrix descriptor, 128-byte swizzle, sm_100 version field.
 //  K-major tiles (rows of 128 B holding 64 16-bit K elements): lbo unused,
 //  sbo = 1024 (8-row group stride).  MN-major tiles (rows = K, 128 B = 64 MN
@@ -113,6 +126,20 @@ __device__ __forceinline__ void ld16(uint32_t ta, float *v) {
       : "memory");
 }
 
+// ---- TMEM -> registers: 16 lanes (starting at the address's lane), 32 columns:
+// thread t gets lane base + (t & 15), columns col + 16*(t >> 4) .. +15
+__device__ __forceinline__ void ld16x2(uint32_t ta, float *v) {
+  uint32_t *r = reinterpret_cast<uint32_t *>(v);
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x32bx2.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16], 16;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(ta)
+      : "memory");
+}
+
 __device__ __forceinline__ void st32(uint32_t ta, const float *v) {
   const uint32_t *r = reinterpret_cast<const uint32_t *>(v);
   asm volatile(
@@ -124,6 +151,15 @@ __device__ __forceinline__ void st32(uint32_t ta, const float *v) {
       "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
       "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
       "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+// ---- registers -> TMEM: 16 lanes (starting at the address's lane), 16 columns:
+// thread t writes lane base + (t & 15), columns col + 8*(t >> 4) .. +7
+__device__ __forceinline__ void st16x2_8(uint32_t ta, const uint32_t *r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.16x32bx2.x8.b32 [%0], 8, {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(ta),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
       : "memory");
 }
 
