@@ -9,18 +9,22 @@
 // Warp roles (192 threads; 6 warps x <=168 registers keeps two CTAs resident
 // per SM, since each SM sub-partition holds 16K registers):
 //   warps 0-3  softmax: TMEM -> registers (32x32b loads), scale, gate, masks,
-//              lazy-rescaled online softmax, P (bf16) -> shared memory in the
-//              128B-swizzled K-major layout the MMA reads, final O / l.
+//              lazy-rescaled online softmax, P (16-bit pairs) written back over
+//              the row's own S columns, final O / l.
 //   warp 4     TMA producer (one thread): Q tiles once, then K blocks into a
 //              ring that is freed as soon as S_j completes and V blocks into a
 //              ring freed when PV_j completes; it polls both rings without
 //              blocking so neither stream waits behind the other.
 //   warp 5     TMEM allocation (256 columns); lane 0 issues the MMAs, polling
 //              two queues without blocking: PV_j = P_j V_j into the TMEM O
-//              accumulator as soon as P_j is ready (first priority), and
-//              S_j = Q K_j^T into a double-buffered TMEM S as soon as K_j has
-//              landed.  Completions are signalled by tcgen05.commit.
-// TMEM columns: S buffers [0,64) and [64,128), O [128,192).
+//              accumulator as soon as P_j is ready (first priority; P_j is the
+//              A operand, read from TMEM), and S_j = Q K_j^T into a
+//              double-buffered TMEM S as soon as K_j has landed and PV_{j-2}
+//              (the last reader of that buffer) is done.  Completions are
+//              signalled by tcgen05.commit.
+// TMEM columns: S / P buffers [0,64) and [64,128), O [128,192).  Since P lives in
+// the S buffers, the softmax of step j+1 never waits for PV_j; only a rescale
+// of O does.
 //
 // The running max is only raised (and O, l rescaled) when a row's new maximum
 // exceeds the one in use by more than 2^8, so the rescale of O in TMEM is rare;
@@ -39,14 +43,15 @@ namespace {
 constexpr int F5_BS = 64, F5_D = 64;
 constexpr int F5_TILE = F5_BS * F5_D * 2;  // 8 KB
 constexpr int F5_MAXN = 64;                // live slots per tile kept in shared memory
-template <int NST>
-constexpr int f5_smem() { return 1024 + 2 * F5_TILE + NST * 4 * F5_TILE + 2 * F5_TILE; }
+// Q of both tiles, NK K stages and NV V stages (each stage both tiles)
+template <int NK, int NV>
+constexpr int f5_smem() { return 1024 + 2 * F5_TILE + (NK + NV) * 2 * F5_TILE; }
 constexpr uint32_t F5_TMEM_COLS = 256;
 constexpr int F5_SCOL0 = 0, F5_OCOL = 128;
 constexpr float F5_RESCALE = 8.f;  // log2 units
 }  // namespace
 
-template <typename T, int F5_NST>
+template <typename T, int NK, int NV>
 __global__ void __launch_bounds__(192, 1)
     attn_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tq,
                           const __grid_constant__ CUtensorMap tk,
@@ -60,10 +65,11 @@ __global__ void __launch_bounds__(192, 1)
                                               ~uintptr_t(1023));
   uint8_t *sQ = smem;                          // tile t at sQ + t*TILE
   uint8_t *sK = smem + 2 * F5_TILE;              // K ring: (stage, tile)
-  uint8_t *sV = sK + F5_NST * 2 * F5_TILE;       // V ring: (stage, tile)
-  uint8_t *sP = sV + F5_NST * 2 * F5_TILE;       // P: tile t at sP + t*TILE
-  __shared__ __align__(8) uint64_t bar_q, k_full[F5_NST], k_empty[F5_NST], v_full[F5_NST],
-      v_empty[F5_NST], s_full[2], s_empty[2], p_full, o_done;
+  uint8_t *sV = sK + NK * 2 * F5_TILE;           // V ring: (stage, tile)
+  // per TMEM buffer b (the step's parity): s_full (S computed), p_full (P written
+  // over S), s_empty (PV, the last reader of P, done)
+  __shared__ __align__(8) uint64_t bar_q, k_full[NK], k_empty[NK], v_full[NV], v_empty[NV],
+      s_full[2], s_empty[2], p_full[2], o_done;
   __shared__ uint32_t tmem_base_sh;
   __shared__ int s_item[2][F5_MAXN];  // (kb << 3) | kind of the j-th live slot
   __shared__ int s_islot[2][F5_MAXN];
@@ -108,17 +114,19 @@ __global__ void __launch_bounds__(192, 1)
   }
   if (tid == 0) {
     mbar_init(&bar_q, 1);
-    for (int s = 0; s < F5_NST; ++s) {
+    for (int s = 0; s < NK; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
+    }
+    for (int s = 0; s < NV; ++s) {
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(&s_full[s], 1);
-      mbar_init(&s_empty[s], 128);
+      mbar_init(&s_empty[s], 1);
+      mbar_init(&p_full[s], 128);
     }
-    mbar_init(&p_full, 128);
     mbar_init(&o_done, 1);
     fence_mbar_init();
   }
@@ -144,7 +152,7 @@ __global__ void __launch_bounds__(192, 1)
       int jk = 0, jv = 0;
       uint32_t idle = 0;
       auto issue = [&](bool isv, int j) {
-        const int st = j % F5_NST;
+        const int st = isv ? j % NV : j % NK;
         uint64_t *full = isv ? &v_full[st] : &k_full[st];
         uint8_t *ring = isv ? sV : sK;
         const int act = (j < nA ? 1 : 0) + (j < nB ? 1 : 0);
@@ -158,13 +166,11 @@ __global__ void __launch_bounds__(192, 1)
       };
       while (jk < nsteps || jv < nsteps) {
         bool progress = false;
-        if (jk < nsteps &&
-            (jk < F5_NST || mbar_test(&k_empty[jk % F5_NST], ((jk / F5_NST) - 1) & 1))) {
+        if (jk < nsteps && (jk < NK || mbar_test(&k_empty[jk % NK], ((jk / NK) - 1) & 1))) {
           issue(false, jk++);
           progress = true;
         }
-        if (jv < nsteps &&
-            (jv < F5_NST || mbar_test(&v_empty[jv % F5_NST], ((jv / F5_NST) - 1) & 1))) {
+        if (jv < nsteps && (jv < NV || mbar_test(&v_empty[jv % NV], ((jv / NV) - 1) & 1))) {
           issue(true, jv++);
           progress = true;
         }
@@ -186,35 +192,36 @@ __global__ void __launch_bounds__(192, 1)
       // descriptors built once; per MMA only a 64-bit add (the issuing thread's
       // scalar work is on the critical path of every step)
       const uint64_t dq0 = tc05::sdesc(smem_u32(sQ), 16, 1024);
-      const uint64_t dp0 = tc05::sdesc(smem_u32(sP), 16, 1024);
       const uint64_t dk0 = tc05::sdesc(smem_u32(sK), 16, 1024);
       const uint64_t dv0 = tc05::sdesc(smem_u32(sV), F5_BS * 128, 1024);
       int js = 0, jp = 0;
       uint32_t idle = 0;
       while (js < nsteps || jp < nsteps) {
         bool progress = false;
-        if (jp < js && mbar_test(&p_full, jp & 1) &&
-            mbar_test(&v_full[jp % F5_NST], (jp / F5_NST) & 1)) {
-          const int st = jp % F5_NST;
+        if (jp < js && mbar_test(&p_full[jp & 1], (jp >> 1) & 1) &&
+            mbar_test(&v_full[jp % NV], (jp / NV) & 1)) {
+          const int st = jp % NV, bb = jp & 1;
           tc05::fence_after();
           for (int t = 0; t < 2; ++t) {
             if (jp >= (t ? nB : nA)) continue;
-            const uint64_t da = tc05::dadd(dp0, t * F5_TILE);
+            // P (16-bit pairs) over the step's S columns is the A operand
+            const uint32_t ta = tc05::taddr(tmem, 16 * t, F5_SCOL0 + 64 * bb);
             const uint64_t db = tc05::dadd(dv0, (st * 2 + t) * F5_TILE);
             const uint32_t d = tc05::taddr(tmem, 16 * t, F5_OCOL);
 #pragma unroll
             for (int ks = 0; ks < F5_BS / 16; ++ks)
-              tc05::mma_f16(d, tc05::dadd(da, ks * 32), tc05::dadd(db, ks * 2048), IDESC_PV,
-                            (jp > 0 || ks > 0) ? 1u : 0u);
+              tc05::mma_f16_ts(d, ta + ks * 8, tc05::dadd(db, ks * 2048), IDESC_PV,
+                               (jp > 0 || ks > 0) ? 1u : 0u);
           }
           tc05::commit(&v_empty[st]);
+          tc05::commit(&s_empty[bb]);
           tc05::commit(&o_done);
           ++jp;
           progress = true;
         }
-        if (js < nsteps && mbar_test(&k_full[js % F5_NST], (js / F5_NST) & 1) &&
+        if (js < nsteps && mbar_test(&k_full[js % NK], (js / NK) & 1) &&
             (js < 2 || mbar_test(&s_empty[js & 1], ((js >> 1) - 1) & 1))) {
-          const int st = js % F5_NST, bb = js & 1;
+          const int st = js % NK, bb = js & 1;
           tc05::fence_after();
           for (int t = 0; t < 2; ++t) {
             if (js >= (t ? nB : nA)) continue;
@@ -261,8 +268,6 @@ __global__ void __launch_bounds__(192, 1)
       tc05::ld32(tmem + lane_base + F5_SCOL0 + 64 * bb, s);
       tc05::ld32(tmem + lane_base + F5_SCOL0 + 64 * bb + 32, s + 32);
       tc05::wait_ld();
-      tc05::fence_before();
-      tc05::mbar_arrive(&s_empty[bb]);
       const bool active = j < nmine;
       float mx = -INFINITY, g2 = 0.f;
       if (active) {
@@ -317,12 +322,11 @@ __global__ void __launch_bounds__(192, 1)
         sum8[4] = acc2[2].x; sum8[5] = acc2[2].y; sum8[6] = acc2[3].x; sum8[7] = acc2[3].y;
         l += ((sum8[0] + sum8[1]) + (sum8[2] + sum8[3])) + ((sum8[4] + sum8[5]) + (sum8[6] + sum8[7]));
       }
-      // PV_{j-1} must be complete: it reads the P buffer and accumulates into O
-      if (j >= 1) {
+      // a rescale of O needs PV_{j-1} complete (S_j was issued after PV_{j-2}
+      // completed, so the barrier is at most one phase behind: no ambiguity)
+      if (__any_sync(0xffffffffu, need) && j >= 1) {
         if (!mbar_wait(&o_done, (j - 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
         tc05::fence_after();
-      }
-      if (__any_sync(0xffffffffu, need) && j >= 1) {
         float o[32];
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
@@ -335,20 +339,17 @@ __global__ void __launch_bounds__(192, 1)
         }
         tc05::wait_st();
       }
-      if (active) {
-        const uint32_t prow = smem_u32(sP + t * F5_TILE);
-#pragma unroll
-        for (int c8 = 0; c8 < 8; ++c8)
-          asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(swz(prow, F5_BS, r, c8 * 8)),
-                       "r"(w[4 * c8]), "r"(w[4 * c8 + 1]), "r"(w[4 * c8 + 2]), "r"(w[4 * c8 + 3])
-                       : "memory");
-      }
-      fence_proxy_async_smem();
+      // P over this row's S columns (all 64 were read above)
+      tc05::st32(tmem + lane_base + F5_SCOL0 + 64 * bb, reinterpret_cast<const float *>(w));
+      tc05::wait_st();
       tc05::fence_before();
-      tc05::mbar_arrive(&p_full);
+      tc05::mbar_arrive(&p_full[bb]);
     }
     // ---- epilogue: O / l
     if (nsteps > 0) {
+      // the last S was issued once PV_{n-3} had completed, so o_done may still be
+      // two phases behind: wait for PV_{n-2} first, then PV_{n-1}
+      if (nsteps > 1 && !mbar_wait(&o_done, (nsteps - 2) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
       if (!mbar_wait(&o_done, (nsteps - 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
       tc05::fence_after();
     }
@@ -404,20 +405,26 @@ bsa_status launch_fwd_sm100(const bsa_attn_args *a, const AttnParams &p, cudaStr
     return s;
   auto pk = [](const TensorMap4 &m) { return m.perm[0] | (m.perm[1] << 2) | (m.perm[2] << 4); };
   const long long grid = (long long)a->B * a->Hq * ((p.nq + 1) / 2);
+  // K / V ring stages: 2 / 2 by default; BSA_FWD_STAGES="KV" (two digits) overrides
   const char *env = getenv("BSA_FWD_STAGES");
-  const bool three = env && env[0] == '3';
-#define BSA_F5_LAUNCH(T_, N_)                                                                   \
+  const int cfg = env ? atoi(env) : 22;
+#define BSA_F5_LAUNCH(T_, K_, V_)                                                                \
   {                                                                                             \
-    auto kern = attn_fwd_sm100_kernel<T_, N_>;                                                  \
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, f5_smem<N_>());      \
-    kern<<<(unsigned)grid, 192, f5_smem<N_>(), st>>>(mq.map, mk.map, mv.map, pk(mq), pk(mk),    \
-                                                      pk(mv), p);                               \
+    auto kern = attn_fwd_sm100_kernel<T_, K_, V_>;                                              \
+    constexpr int sm = f5_smem<K_, V_>();                                                       \
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);                \
+    kern<<<(unsigned)grid, 192, sm, st>>>(mq.map, mk.map, mv.map, pk(mq), pk(mk), pk(mv), p);   \
   }
+#define BSA_F5_PICK(T_)                                   \
+  if (cfg == 32) BSA_F5_LAUNCH(T_, 3, 2)                  \
+  else if (cfg == 23) BSA_F5_LAUNCH(T_, 2, 3)             \
+  else BSA_F5_LAUNCH(T_, 2, 2)
   if (a->dtype == BSA_BF16) {
-    if (three) BSA_F5_LAUNCH(__nv_bfloat16, 3) else BSA_F5_LAUNCH(__nv_bfloat16, 2)
+    BSA_F5_PICK(__nv_bfloat16)
   } else {
-    if (three) BSA_F5_LAUNCH(__half, 3) else BSA_F5_LAUNCH(__half, 2)
+    BSA_F5_PICK(__half)
   }
+#undef BSA_F5_PICK
 #undef BSA_F5_LAUNCH
   return check_launch("attn_fwd_sm100");
 }
