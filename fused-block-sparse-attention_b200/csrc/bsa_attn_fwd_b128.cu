@@ -6,10 +6,12 @@
 // (16 KB each), so D = 256 needs no more buffer than D = 64 per ring slot.
 // Per live slot j (a selected key block):
 //   S_j  = Q K_j^T      per 64-column chunk 4 x tcgen05.mma 128x128x16 (fp32, TMEM)
-//   P_j  = 2^(S_j * scale * log2e + gate - m)   (bf16, shared memory)
-//   O   += P_j V_j      per 64-column chunk 8 x tcgen05.mma 128x64x16 into TMEM
-// TMEM: S columns [0, 128), O columns [128, 128 + D) (D = 64: 256 allocated,
-// two CTAs per SM; D = 256: 512, one).  Row m of every tile lives in lane m.
+//   P_j  = 2^(S_j * scale * log2e + gate - m)   (bf16 pairs, TMEM)
+//   O   += P_j V_j      per 64-column chunk 8 x tcgen05.mma 128x64x16 into TMEM,
+//                       P_j as the A operand from TMEM
+// TMEM: S columns [0, 128), P [128, 192), O [192, 192 + D) (D = 64: 256
+// allocated, two CTAs per SM; D = 256: 512, one).  Row m of every tile lives in
+// lane m.
 // An optional sigmoid output gate (Qwen) is applied in the epilogue.
 //
 // Warp roles (320 threads; <= 96 registers per thread keeps two CTAs per SM):
@@ -19,8 +21,8 @@
 //              the maximum in use is raised only when the block exceeds it by
 //              more than 2^8 (lazy rescaling; O is then rescaled in TMEM); the
 //              exponentials go to registers while PV_{j-1} may still run, and P
-//              is written 128B-swizzled K-major in two 64-key regions once
-//              PV_{j-1} has released the buffer; final O / l.
+//              is written to its TMEM columns once PV_{j-1} has released them;
+//              final O / l.
 //   warp 8     TMA producer (one thread): Q once, then the K and V chunks into
 //              ONE ring of 64-column slots, in the order the MMAs consume them
 //              (K of step 0; then K of step j + 1 and V of step j for each j),
@@ -41,14 +43,14 @@ namespace {
 constexpr int G8_BS = 128;
 constexpr int G8_TILE = G8_BS * 64 * 2;  // 16 KB: a 128-row block of 64 columns
 constexpr int G8_WPROD = 8, G8_WMMA = 9, G8_THREADS = 320;
-constexpr int G8_SCOL = 0, G8_OCOL = 128;
+constexpr int G8_SCOL = 0, G8_PCOL = 128, G8_OCOL = 192;
 constexpr float G8_RESCALE = 8.f;  // log2 units
 template <int D>
 struct G8 {
   static constexpr int NCH = D / 64;                 // 64-column chunks per row
-  // ring slots shared by K and V chunks (D = 64: 3 x 16 KB keeps two CTAs per SM)
-  static constexpr int NSL = D == 64 ? 3 : 6;
-  static constexpr int SMEM = 1024 + NCH * G8_TILE + NSL * G8_TILE + 2 * G8_TILE;
+  // ring slots shared by K and V chunks (D = 64: 5 x 16 KB keeps two CTAs per SM)
+  static constexpr int NSL = D == 64 ? 5 : 8;
+  static constexpr int SMEM = 1024 + NCH * G8_TILE + NSL * G8_TILE;
   static constexpr uint32_t TMEM_COLS = D == 64 ? 256 : 512;
   static constexpr int MINB = D == 64 ? 2 : 1;       // CTAs per SM
   // live slots kept in shared memory (D = 256 also runs the identity selection,
@@ -72,7 +74,6 @@ __global__ void __launch_bounds__(G8_THREADS, G8<D>::MINB)
                                               ~uintptr_t(1023));
   uint8_t *sQ = smem;                       // Q chunk c at sQ + c * TILE
   uint8_t *sR = sQ + NCH * G8_TILE;         // K/V ring: NSL chunk slots
-  uint8_t *sP = sR + NSL * G8_TILE;         // P: keys 0-63 at sP, 64-127 at sP + TILE
   __shared__ __align__(8) uint64_t bar_q, r_full[NSL], r_empty[NSL], s_full, s_empty, p_full,
       o_done, q_ready;
   __shared__ uint32_t tmem_base_sh;
@@ -197,17 +198,16 @@ __global__ void __launch_bounds__(G8_THREADS, G8<D>::MINB)
       for (int jp = 0; jp < nsteps; ++jp) {
         if (jp + 1 < nsteps) issue_s(jp + 1);
         if (!mbar_wait(&p_full, jp & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
-        const uint64_t dp = tc05::sdesc(smem_u32(sP), 16, 1024);
         for (int c = 0; c < NCH; ++c, ++n) {
           const int sl = n % NSL;
           if (!mbar_wait(&r_full[sl], (n / NSL) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
           tc05::fence_after();
           const uint64_t dv = tc05::sdesc(smem_u32(sR + sl * G8_TILE), G8_TILE, 1024);
 #pragma unroll
-          for (int ks = 0; ks < G8_BS / 16; ++ks)  // keys 16*ks: P region ks/4, +32 B per 16 keys
-            tc05::mma_f16(tc05::taddr(tmem, 0, G8_OCOL + 64 * c),
-                          dp + (ks >> 2) * (G8_TILE >> 4) + 2 * (ks & 3), dv + 128 * ks, IDESC_PV,
-                          (jp > 0 || ks > 0) ? 1u : 0u);
+          for (int ks = 0; ks < G8_BS / 16; ++ks)  // keys 16*ks: P columns 8*ks (16-bit pairs)
+            tc05::mma_f16_ts(tc05::taddr(tmem, 0, G8_OCOL + 64 * c),
+                             tc05::taddr(tmem, 0, G8_PCOL + 8 * ks), dv + 128 * ks, IDESC_PV,
+                             (jp > 0 || ks > 0) ? 1u : 0u);
           tc05::commit(&r_empty[sl]);
         }
         tc05::commit(&o_done);
@@ -219,7 +219,6 @@ __global__ void __launch_bounds__(G8_THREADS, G8<D>::MINB)
     const int r = quad * 32 + lane;  // query row within the block
     const int cb = 64 * hf;          // first key column of this warp
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
-    const uint32_t pbase = smem_u32(sP + hf * G8_TILE);
     const float *gaterow = (p.gate && p.sel)
                                ? p.gate + b * p.gate_sb + hk * p.gate_sh + (long long)qi * p.gate_sn
                                : nullptr;
@@ -329,12 +328,9 @@ __global__ void __launch_bounds__(G8_THREADS, G8<D>::MINB)
         }
         tc05::wait_st();
       }
-#pragma unroll
-      for (int c8 = 0; c8 < 8; ++c8)
-        asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(swz(pbase, 128, r, c8 * 8)),
-                     "r"(w[4 * c8]), "r"(w[4 * c8 + 1]), "r"(w[4 * c8 + 2]), "r"(w[4 * c8 + 3])
-                     : "memory");
-      fence_proxy_async_smem();
+      // P of keys cb..cb+63 -> TMEM columns PCOL + cb/2 .. +31 of this row
+      tc05::st32(tmem + lane_base + G8_PCOL + 32 * hf, reinterpret_cast<const float *>(w));
+      tc05::wait_st();
       tc05::fence_before();
       __syncwarp();
       if (lane == 0) tc05::mbar_arrive(&p_full);
