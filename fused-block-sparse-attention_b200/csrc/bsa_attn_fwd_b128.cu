@@ -275,15 +275,7 @@ __global__ void __launch_bounds__(G8_THREADS, G8<D>::MINB)
       }
       // block row maximum (both halves of the row, through shared memory), then
       // the exponentials into registers while PV_{j-1} may still be running
-      float m8[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) m8[i] = fmaxf(s[i], s[i + 8]);
-#pragma unroll
-      for (int c = 16; c < 64; c += 8)
-#pragma unroll
-        for (int i = 0; i < 8; ++i) m8[i] = fmaxf(m8[i], s[c + i]);
-      const float mh = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                             fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+      const float mh = max64(s);
       s_xch[j & 1][quad][hf][lane] = mh;
       named_bar_sync(1 + quad, 64);
       const float mr = fmaxf(mh, s_xch[j & 1][quad][hf ^ 1][lane]);

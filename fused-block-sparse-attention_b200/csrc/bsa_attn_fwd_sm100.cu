@@ -280,16 +280,8 @@ __global__ void __launch_bounds__(192, 1)
             if (((kind & KIND_TRIU) && c > r) || ((kind & KIND_PAD) && kb * p.bs + c >= p.L))
               s[c] = -INFINITY;
         }
-        // row max of the raw scores (scale2 > 0), 8-way tree
-        float m8[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) m8[i] = fmaxf(s[i], s[i + 8]);
-#pragma unroll
-        for (int c = 16; c < 64; c += 8)
-#pragma unroll
-          for (int i = 0; i < 8; ++i) m8[i] = fmaxf(m8[i], s[c + i]);
-        const float mr = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                               fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7])));
+        // row max of the raw scores (scale2 > 0)
+        const float mr = max64(s);
         mx = mr == -INFINITY ? -INFINITY : fmaf(mr, p.scale2, g2);
       }
       const bool need = active && mx > -INFINITY && (m_used == -INFINITY || mx > m_used + F5_RESCALE);

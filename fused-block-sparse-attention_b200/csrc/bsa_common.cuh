@@ -246,6 +246,27 @@ __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
   return d;
 }
 
+// Three-input maximum (one sm_100 instruction; same result as two fmaxf).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Maximum of 64 registers: 8 independent chains of three-input maxima.
+__device__ __forceinline__ float max64(const float *s) {
+  float m8[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m8[i] = fmax3(s[i], s[i + 8], s[i + 16]);
+#pragma unroll
+  for (int c = 24; c < 56; c += 16)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m8[i] = fmax3(m8[i], s[c + i], s[c + 8 + i]);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) m8[i] = fmaxf(m8[i], s[56 + i]);
+  return fmax3(fmax3(m8[0], m8[1], m8[2]), fmax3(m8[3], m8[4], m8[5]), fmaxf(m8[6], m8[7]));
+}
+
 // ---------------------------------------------------------------- slot kinds
 // Classification of one selected slot for one query block.
 enum : int { KIND_SKIP = 0, KIND_FULL = 1, KIND_TRIU = 2, KIND_PAD = 4 };
