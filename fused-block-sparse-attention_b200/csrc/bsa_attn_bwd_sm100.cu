@@ -48,7 +48,10 @@ constexpr int b5_smem(int NST, int NKV) {
          + NST * 2 * 2 * B5_ROWB;    // ring: (stage, tile) lse, Dvec
 }
 constexpr uint32_t B5_TMEM_COLS = 512;
-constexpr int B5_SCOL = 0, B5_DPCOL = 128, B5_DVCOL = 256, B5_DKCOL = 320;  // +128: 2nd acc buffer
+// TMEM: NSB buffers of S^T (P^T) and of dP^T (dS^T), NAB dV/dK accumulator pairs
+constexpr int B5_NSB = 3, B5_NAB = 1;
+static_assert(128 * B5_NSB + 128 * B5_NAB == (int)B5_TMEM_COLS, "TMEM columns");
+constexpr int B5_SCOL = 0, B5_DPCOL = 64 * B5_NSB, B5_DVCOL = 128 * B5_NSB, B5_DKCOL = B5_DVCOL + 64;
 }  // namespace
 
 // Work unit u -> (two chunks of the plan, KV head within the bin group).
@@ -87,7 +90,7 @@ __device__ __forceinline__ void b5_unit(const BwdPlan &pl, const AttnParams &p, 
 // GATE: a gate tensor is present (without one the exponent's offset is -lse, which
 // folds into the FMA)
 template <typename T, int B5_NST, int NKV, bool GATE>
-__global__ void __launch_bounds__(320, 1)
+__global__ void __launch_bounds__(352, 1)
     attn_dkdv_sm100_kernel(const __grid_constant__ CUtensorMap tq,
                            const __grid_constant__ CUtensorMap tdo,
                            const __grid_constant__ CUtensorMap tk,
@@ -107,7 +110,7 @@ __global__ void __launch_bounds__(320, 1)
   // p_full (P^T, dS^T written over them), s_empty (the step's dV/dK MMAs, the
   // last readers of the buffer, are done)
   __shared__ __align__(8) uint64_t kv_full[NKV], kv_empty[NKV], r_full[B5_NST], r_empty[B5_NST],
-      s_full[2][2], s_empty[2][2], p_full[2][2], acc_empty[2][2];
+      s_full[2][B5_NSB], s_empty[2][B5_NSB], p_full[2][B5_NSB], acc_empty[2][B5_NAB];
   __shared__ uint32_t tmem_base_sh;
   // per ring stage and tile: (local query block, slot, query head) and the gate
   // value of the step, written by the producer before it arrives on r_full
@@ -137,12 +140,12 @@ __global__ void __launch_bounds__(320, 1)
       mbar_init(&kv_empty[s], 2);
     }
     for (int t = 0; t < 2; ++t) {
-      for (int s = 0; s < 2; ++s) {
+      for (int s = 0; s < B5_NSB; ++s) {
         mbar_init(&s_full[t][s], 1);
         mbar_init(&s_empty[t][s], 1);
         mbar_init(&p_full[t][s], 128);
-        mbar_init(&acc_empty[t][s], 128);
       }
+      for (int s = 0; s < B5_NAB; ++s) mbar_init(&acc_empty[t][s], 128);
     }
     for (int s = 0; s < B5_NST; ++s) {
       mbar_init(&r_full[s], 1);
@@ -289,110 +292,101 @@ __global__ void __launch_bounds__(320, 1)
       s_unit[ne & 7][2] = -1;
       tc05::mbar_arrive(&kv_full[kvb]);
     }
-  } else if (warp == 9) {
-    // ================= MMA issuer: per tile an S/dP queue and a dV/dK queue, polled
+  } else if (warp >= 9) {
+    // ================= MMA issuers: warp 9 for tile A, warp 10 for tile B, each
+    // polling the tile's S/dP queue and its dV/dK queue (tcgen05.commit tracks
+    // the issuing thread's own MMAs; the shared ring stage and K/V buffer are
+    // released by one commit of each)
     if (lane == 0) {
+      const int t = warp - 9;
       // descriptors built once; per MMA only a 64-bit add
       const uint64_t dkv0 = tc05::sdesc(smem_u32(sKV), 16, 1024);          // K, V (A, K-major)
       const uint64_t drk0 = tc05::sdesc(smem_u32(sR), 16, 1024);           // Q, dO as K-major B
       const uint64_t drm0 = tc05::sdesc(smem_u32(sR), B5_BS * 128, 1024);  // Q, dO as MN-major B
-      // queue state per tile: S (js, gss, nes) and G (jg, gsg, neg); the units
-      // (ordinals ne = 0, 1, ...) come from the producer's s_unit ring: an S
-      // queue opens unit nes once its K/V barrier has completed
-      int js[2], gss[2], nes[2], jg[2], gsg[2], neg[2];
-      int sn[2], gn[2], sns[2], gns[2];  // tile length and unit length of the current units
-      bool s_open[2], have_s[2], have_g[2];
+      // S queue (js, gss, nes) and G queue (jg, gsg, neg); the units (ordinals
+      // ne = 0, 1, ...) come from the producer's s_unit ring: the S queue opens
+      // unit nes once its K/V barrier has completed
+      int js = 0, gss = 0, nes = 0, jg = 0, gsg = 0, neg = 0;
+      int sn = 0, gn = 0, sns = 0, gns = 0;  // tile length and unit length of the current units
+      bool s_open = false, have_s = true, have_g = true;
       uint32_t idle = 0;
-#pragma unroll
-      for (int t = 0; t < 2; ++t) {
-        js[t] = jg[t] = gss[t] = gsg[t] = 0;
-        nes[t] = neg[t] = 0;
-        s_open[t] = false;
-        have_s[t] = have_g[t] = true;
-        sn[t] = gn[t] = sns[t] = gns[t] = 0;
-      }
-      while (have_g[0] || have_g[1]) {
+      while (have_g) {
         bool progress = false;
-#pragma unroll
-        for (int t = 0; t < 2; ++t) {
-          // ---- open the next unit of tile t's S queue once its K/V have landed
-          if (have_s[t] && !s_open[t] && mbar_test(&kv_full[nes[t] % NKV], (nes[t] / NKV) & 1)) {
-            sns[t] = s_unit[nes[t] & 7][2];
-            sn[t] = s_unit[nes[t] & 7][t];
-            if (sns[t] < 0) {
-              have_s[t] = false;
-            } else {
-              s_open[t] = true;
-            }
-            progress = true;
+        // ---- open the next unit of the S queue once its K/V have landed
+        if (have_s && !s_open && mbar_test(&kv_full[nes % NKV], (nes / NKV) & 1)) {
+          sns = s_unit[nes & 7][2];
+          sn = s_unit[nes & 7][t];
+          if (sns < 0) {
+            have_s = false;
+          } else {
+            s_open = true;
           }
-          // ---- dV += P^T dO, dK += dS^T Q of tile t, step gsg[t] (its unit neg[t]
-          // was opened by the S queue, which runs ahead)
-          if (have_g[t] && gsg[t] < gss[t] &&
-              mbar_test(&p_full[t][gsg[t] & 1], (gsg[t] >> 1) & 1) &&
-              (jg[t] > 0 || neg[t] < 2 ||
-               mbar_test(&acc_empty[t][neg[t] & 1], ((neg[t] >> 1) - 1) & 1))) {
-            if (jg[t] == 0) {
-              gns[t] = s_unit[neg[t] & 7][2];
-              gn[t] = s_unit[neg[t] & 7][t];
-            }
-            const int st = gsg[t] % B5_NST, ab = neg[t] & 1, bb = gsg[t] & 1;
-            tc05::fence_after();
-            if (jg[t] < gn[t]) {
-              const uint32_t roff = (st * 2 + t) * 2 * B5_TILE;  // Q; dO at + TILE
-              const uint64_t bdo = tc05::dadd(drm0, roff + B5_TILE), bq = tc05::dadd(drm0, roff);
-              // P^T and dS^T (16-bit pairs) over the step's S^T and dP^T columns
-              const uint32_t ap = tc05::taddr(tmem, 16 * t, B5_SCOL + 64 * bb);
-              const uint32_t ads = tc05::taddr(tmem, 16 * t, B5_DPCOL + 64 * bb);
-              const uint32_t dv = tc05::taddr(tmem, 16 * t, B5_DVCOL + 128 * ab);
-              const uint32_t dk = tc05::taddr(tmem, 16 * t, B5_DKCOL + 128 * ab);
-#pragma unroll
-              for (int ks = 0; ks < B5_BS / 16; ++ks) {
-                const uint32_t acc = (jg[t] > 0 || ks > 0) ? 1u : 0u;
-                tc05::mma_f16_ts(dv, ap + ks * 8, tc05::dadd(bdo, ks * 2048), IDESC_KM, acc);
-                tc05::mma_f16_ts(dk, ads + ks * 8, tc05::dadd(bq, ks * 2048), IDESC_KM, acc);
-              }
-            }
-            tc05::commit(&r_empty[st]);  // count 2: the stage is free once both tiles are done
-            tc05::commit(&s_empty[t][bb]);
-            ++gsg[t];
-            if (++jg[t] == gns[t]) {
-              jg[t] = 0;
-              ++neg[t];
-              have_g[t] = have_s[t] || neg[t] < nes[t];
-            }
-            progress = true;
-          } else if (have_g[t] && !have_s[t] && gsg[t] == gss[t]) {
-            have_g[t] = false;  // every opened step is done and no unit follows
+          progress = true;
+        }
+        // ---- dV += P^T dO, dK += dS^T Q, step gsg (its unit neg was opened by
+        // the S queue, which runs ahead)
+        if (gsg < gss && mbar_test(&p_full[t][gsg % B5_NSB], (gsg / B5_NSB) & 1) &&
+            (jg > 0 || neg < B5_NAB ||
+             mbar_test(&acc_empty[t][neg % B5_NAB], ((neg / B5_NAB) - 1) & 1))) {
+          if (jg == 0) {
+            gns = s_unit[neg & 7][2];
+            gn = s_unit[neg & 7][t];
           }
-          // ---- S^T = K Q^T, dP^T = V dO^T of tile t, step gss[t]
-          if (s_open[t] && mbar_test(&r_full[gss[t] % B5_NST], (gss[t] / B5_NST) & 1) &&
-              (gss[t] < 2 || mbar_test(&s_empty[t][gss[t] & 1], ((gss[t] >> 1) - 1) & 1))) {
-            const int st = gss[t] % B5_NST, bb = gss[t] & 1;
-            tc05::fence_after();
-            if (js[t] < sn[t]) {
-              const uint32_t roff = (st * 2 + t) * 2 * B5_TILE;             // Q; dO at + TILE
-              const uint32_t koff = ((nes[t] % NKV) * 2 + t) * 2 * B5_TILE;  // K; V at + TILE
-              const uint64_t ak = tc05::dadd(dkv0, koff), av = tc05::dadd(dkv0, koff + B5_TILE);
-              const uint64_t bq = tc05::dadd(drk0, roff), bdo = tc05::dadd(drk0, roff + B5_TILE);
-              const uint32_t ds = tc05::taddr(tmem, 16 * t, B5_SCOL + 64 * bb);
-              const uint32_t ddp = tc05::taddr(tmem, 16 * t, B5_DPCOL + 64 * bb);
+          const int st = gsg % B5_NST, ab = neg % B5_NAB, bb = gsg % B5_NSB;
+          tc05::fence_after();
+          if (jg < gn) {
+            const uint32_t roff = (st * 2 + t) * 2 * B5_TILE;  // Q; dO at + TILE
+            const uint64_t bdo = tc05::dadd(drm0, roff + B5_TILE), bq = tc05::dadd(drm0, roff);
+            // P^T and dS^T (16-bit pairs) over the step's S^T and dP^T columns
+            const uint32_t ap = tc05::taddr(tmem, 16 * t, B5_SCOL + 64 * bb);
+            const uint32_t ads = tc05::taddr(tmem, 16 * t, B5_DPCOL + 64 * bb);
+            const uint32_t dv = tc05::taddr(tmem, 16 * t, B5_DVCOL + 128 * ab);
+            const uint32_t dk = tc05::taddr(tmem, 16 * t, B5_DKCOL + 128 * ab);
 #pragma unroll
-              for (int ks = 0; ks < B5_D / 16; ++ks) {
-                tc05::mma_f16(ds, tc05::dadd(ak, ks * 32), tc05::dadd(bq, ks * 32), IDESC_KK, ks > 0);
-                tc05::mma_f16(ddp, tc05::dadd(av, ks * 32), tc05::dadd(bdo, ks * 32), IDESC_KK, ks > 0);
-              }
+            for (int ks = 0; ks < B5_BS / 16; ++ks) {
+              const uint32_t acc = (jg > 0 || ks > 0) ? 1u : 0u;
+              tc05::mma_f16_ts(dv, ap + ks * 8, tc05::dadd(bdo, ks * 2048), IDESC_KM, acc);
+              tc05::mma_f16_ts(dk, ads + ks * 8, tc05::dadd(bq, ks * 2048), IDESC_KM, acc);
             }
-            tc05::commit(&s_full[t][bb]);
-            ++gss[t];
-            if (++js[t] == sns[t]) {
-              tc05::commit(&kv_empty[nes[t] % NKV]);  // count 2: last readers of the K/V buffer
-              js[t] = 0;
-              ++nes[t];
-              s_open[t] = false;
-            }
-            progress = true;
           }
+          tc05::commit(&r_empty[st]);  // count 2: the stage is free once both tiles are done
+          tc05::commit(&s_empty[t][bb]);
+          ++gsg;
+          if (++jg == gns) {
+            jg = 0;
+            ++neg;
+          }
+          progress = true;
+        } else if (!have_s && gsg == gss) {
+          have_g = false;  // every opened step is done and no unit follows
+        }
+        // ---- S^T = K Q^T, dP^T = V dO^T, step gss
+        if (s_open && mbar_test(&r_full[gss % B5_NST], (gss / B5_NST) & 1) &&
+            (gss < B5_NSB || mbar_test(&s_empty[t][gss % B5_NSB], ((gss / B5_NSB) - 1) & 1))) {
+          const int st = gss % B5_NST, bb = gss % B5_NSB;
+          tc05::fence_after();
+          if (js < sn) {
+            const uint32_t roff = (st * 2 + t) * 2 * B5_TILE;           // Q; dO at + TILE
+            const uint32_t koff = ((nes % NKV) * 2 + t) * 2 * B5_TILE;  // K; V at + TILE
+            const uint64_t ak = tc05::dadd(dkv0, koff), av = tc05::dadd(dkv0, koff + B5_TILE);
+            const uint64_t bq = tc05::dadd(drk0, roff), bdo = tc05::dadd(drk0, roff + B5_TILE);
+            const uint32_t ds = tc05::taddr(tmem, 16 * t, B5_SCOL + 64 * bb);
+            const uint32_t ddp = tc05::taddr(tmem, 16 * t, B5_DPCOL + 64 * bb);
+#pragma unroll
+            for (int ks = 0; ks < B5_D / 16; ++ks) {
+              tc05::mma_f16(ds, tc05::dadd(ak, ks * 32), tc05::dadd(bq, ks * 32), IDESC_KK, ks > 0);
+              tc05::mma_f16(ddp, tc05::dadd(av, ks * 32), tc05::dadd(bdo, ks * 32), IDESC_KK, ks > 0);
+            }
+          }
+          tc05::commit(&s_full[t][bb]);
+          ++gss;
+          if (++js == sns) {
+            tc05::commit(&kv_empty[nes % NKV]);  // count 2: last readers of the K/V buffer
+            js = 0;
+            ++nes;
+            s_open = false;
+          }
+          progress = true;
         }
         if (progress) {
           idle = 0;
@@ -432,8 +426,8 @@ __global__ void __launch_bounds__(320, 1)
       if (lane == 0) tc05::mbar_arrive(&eu_empty[eb]);
       const bool key_ok = (long long)kb * p.bs + kr < p.L;
       for (int j = 0; j < ns; ++j, ++gs) {
-        const int bb = gs & 1, st = gs % B5_NST;
-        if (!mbar_wait(&s_full[t][bb], (gs >> 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
+        const int bb = gs % B5_NSB, st = gs % B5_NST;
+        if (!mbar_wait(&s_full[t][bb], (gs / B5_NSB) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
         // acquire the stage's TMA / bulk data and the producer's metadata
         if (!mbar_wait(&r_full[st], (gs / B5_NST) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
         tc05::fence_after();
@@ -521,10 +515,10 @@ __global__ void __launch_bounds__(320, 1)
       }
       // ---- dK (scaled) and dV of this unit: this thread's row, its two 16-column
       // groups, one accumulator at a time
-      const int ab = ne & 1;
+      const int ab = ne % B5_NAB;
       if (ns > 0) {
         const int gl = gs - 1;  // last step of this unit
-        if (!mbar_wait(&s_empty[t][gl & 1], (gl >> 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
+        if (!mbar_wait(&s_empty[t][gl % B5_NSB], (gl / B5_NSB) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
         tc05::fence_after();
       }
       long long pidx = -1;
@@ -615,7 +609,7 @@ bsa_status launch_dkdv_sm100(int dtype, const CUtensorMap &mq, const CUtensorMap
                        : attn_dkdv_sm100_kernel<T_, N_, KV_, false>;                        \
     constexpr int sm = b5_smem(N_, KV_);                                                    \
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, sm);            \
-    kern<<<grid, 320, sm, st>>>(mq, mdo, mk, mv, pq, pdo, pk, pv, p, pl);                   \
+    kern<<<grid, 352, sm, st>>>(mq, mdo, mk, mv, pq, pdo, pk, pv, p, pl);                   \
   }
 #define BSA_B5_PICK(T_)                                      \
   if (variant == 4) BSA_B5_LAUNCH(T_, 4, 1)                  \
