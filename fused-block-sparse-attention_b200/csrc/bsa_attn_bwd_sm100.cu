@@ -8,15 +8,16 @@
 // 5-stage ring (Q, dO by TMA, lse and Dvec rows by bulk copy).
 //
 // Per step j (one entry and query head of each tile):
-//   S^T  = K  Q_j^T    dP^T = V dO_j^T         (tcgen05, fp32 in TMEM, 2 buffers)
+//   S^T  = K  Q_j^T    dP^T = V dO_j^T         (tcgen05, fp32 in TMEM, 3 buffers)
 //   P^T  = 2^(S^T*scale*log2e + gate - lse_j)  dS^T = P^T (dP^T - Dvec_j)
 //   dV  += P^T dO_j    dK  += dS^T Q_j          (tcgen05, A operand in TMEM)
 // P^T and dS^T (16-bit pairs) are written back over the step's own S^T and dP^T
 // columns, so they are double-buffered with them and need no shared memory.
 // The two tiles run as independent pipelines: each has its own S/dP buffers,
-// hand-off barriers and dK/dV accumulators; they share only the ring stage.
+// hand-off barriers, dK/dV accumulators and MMA-issuing thread; they share
+// only the ring stage and the K/V buffer.
 //
-// Warp roles (320 threads, one CTA per SM):
+// Warp roles (352 threads, one CTA per SM):
 //   warps 0-3  elementwise for tile A, warps 4-7 for tile B: each warp owns the
 //              tile's 16 TMEM lanes of its quadrant (16x32bx2 loads and
 //              stores), writes P^T / dS^T to TMEM, dS^T rows to global memory
@@ -24,10 +25,12 @@
 //   warp 8     TMA producer: the warp reads a unit's CSR entries and gate values
 //              at once, then one thread publishes the unit to the other warps
 //              and issues the ring loads.
-//   warp 9     TMEM allocation (512 columns) and the MMA-issuing thread, which
-//              polls per tile an S/dP queue and a dV/dK queue.
-// TMEM columns: S^T [0,64) [64,128), dP^T [128,192) [192,256), dV [256,320),
-// dK [320,384), second accumulator pair at +128; tile B at lane offset 16.
+//   warp 9     TMEM allocation (512 columns) and tile A's MMA-issuing thread,
+//   warp 10    tile B's MMA-issuing thread; each polls its tile's S/dP queue
+//              and dV/dK queue.  (One thread for both tiles was the bottleneck:
+//              issuing 32 MMAs and polling took ~3.7k cycles per step.)
+// TMEM columns: S^T [0,192) and dP^T [192,384) in three 64-column buffers, dV
+// [384,448), dK [448,512); tile B at lane offset 16.
 #include <algorithm>
 #include <type_traits>
 

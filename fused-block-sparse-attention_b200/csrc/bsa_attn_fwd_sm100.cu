@@ -69,7 +69,7 @@ __global__ void __launch_bounds__(192, 1)
   // per TMEM buffer b (the step's parity): s_full (S computed), p_full (P written
   // over S), s_empty (PV, the last reader of P, done)
   __shared__ __align__(8) uint64_t bar_q, k_full[NK], k_empty[NK], v_full[NV], v_empty[NV],
-      s_full[2], s_empty[2], p_full[2], o_done;
+      s_full[2], s_empty[2], p_full[2], o_done, o_final;
   __shared__ uint32_t tmem_base_sh;
   __shared__ int s_item[2][F5_MAXN];  // (kb << 3) | kind of the j-th live slot
   __shared__ int s_islot[2][F5_MAXN];
@@ -128,6 +128,7 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&p_full[s], 128);
     }
     mbar_init(&o_done, 1);
+    mbar_init(&o_final, 1);  // one phase: the last PV has completed
     fence_mbar_init();
   }
   if (warp == 5) {
@@ -216,6 +217,7 @@ __global__ void __launch_bounds__(192, 1)
           tc05::commit(&v_empty[st]);
           tc05::commit(&s_empty[bb]);
           tc05::commit(&o_done);
+          if (jp == nsteps - 1) tc05::commit(&o_final);
           ++jp;
           progress = true;
         }
@@ -339,10 +341,9 @@ __global__ void __launch_bounds__(192, 1)
     }
     // ---- epilogue: O / l
     if (nsteps > 0) {
-      // the last S was issued once PV_{n-3} had completed, so o_done may still be
-      // two phases behind: wait for PV_{n-2} first, then PV_{n-1}
-      if (nsteps > 1 && !mbar_wait(&o_done, (nsteps - 2) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
-      if (!mbar_wait(&o_done, (nsteps - 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
+      // the last PV: a barrier with a single phase, since o_done may be anywhere
+      // between PV_{n-3} and PV_{n-1} here (two parity waits on it could miss)
+      if (!mbar_wait(&o_final, 0)) report(p.status, BSA_DEVERR_TIMEOUT);
       tc05::fence_after();
     }
     float o[64];
