@@ -76,6 +76,32 @@ __global__ void pool_kernel(const bsa_pool_args a, int Hout) {
 #pragma unroll
       for (int e = 0; e < V; ++e) out[e] = tof(ue[e]);
     };
+    if (!rot && a.grp == 1) {
+      // plain rows: eight loads in flight per thread, then the same per-row
+      // accumulation order as below (rows past L count as zeros)
+      const T *xr = x + ho * a.x.sh;
+      for (int row0 = 0; row0 < a.bs; row0 += 8) {
+        uint4 u[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const long long gr = (long long)blk * a.bs + row0 + i;
+          u[i] = (row0 + i < a.bs && gr < a.L) ? *reinterpret_cast<const uint4 *>(xr + gr * a.x.sl)
+                                               : make_uint4(0u, 0u, 0u, 0u);
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          if (row0 + i >= a.bs) break;
+          const T *ue = reinterpret_cast<const T *>(&u[i]);
+#pragma unroll
+          for (int e = 0; e < V; ++e) {
+            const float val = tof(ue[e]);
+            sum[e] = __fadd_rn(sum[e], val);
+            mn[e] = fminf(mn[e], val);
+            mx[e] = fmaxf(mx[e], val);
+          }
+        }
+      }
+    } else
     for (int row = 0; row < a.bs; ++row) {
       const long long gr = (long long)blk * a.bs + row;
       float val[V];
