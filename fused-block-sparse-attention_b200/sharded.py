@@ -21,7 +21,9 @@ produces them).
                with kk blocks per query block the attention itself is balanced.
   backward  dQ stays local; dK/dV are this rank's contributions over the whole
             sequence, summed across ranks and returned to their owners by one
-            reduce_scatter.  The per-rank partials come out of the backward in
+            reduce_scatter (dK and dV copied rank-major into one fp32 buffer,
+            the copy doing the conversion, then a single NCCL call instead of
+            one per (batch, head) slice).  The per-rank partials come out of the backward in
             the input dtype (bf16): each is rounded once (relative 2^-9) before
             the fp32 sum, so the summed dK/dV carry at most that rounding of
             each rank's share, the same order as the single-GPU result's own
@@ -125,6 +127,41 @@ def _gather_seq(x, group, async_op=False):
     return (out, works) if async_op else out
 
 
+def _gather_small(x, group):
+    """Same result as _gather_seq for small tensors (pooled summaries, selection
+    rows): one all_gather_into_tensor into a rank-major buffer, then one copy
+    into (B, H, world * n, ...) instead of one collective per (batch, head)."""
+    world, _ = _world(group)
+    if world == 1:
+        return x
+    x = x.contiguous()
+    B, H, n = x.shape[:3]
+    rest = tuple(x.shape[3:])
+    buf = torch.empty((world * B, H, n) + rest, dtype=x.dtype, device=x.device)
+    dist.all_gather_into_tensor(buf, x, group=group)
+    perm = (1, 2, 0, 3) + tuple(range(4, 4 + len(rest)))
+    return buf.view((world, B, H, n) + rest).permute(perm).reshape((B, H, world * n) + rest)
+
+
+def _reduce_scatter_pair(x, y, group):
+    """x, y: (B, H, world * n, ...) per-rank partial sums of the same shape -> this
+    rank's (B, H, n, ...) slices of their fp32 sums over ranks.  Both are copied
+    (and converted) into one rank-major fp32 buffer (world, 2, B, H, n, ...), so a
+    single reduce_scatter_tensor returns (2, B, H, n, ...)."""
+    world, _ = _world(group)
+    if world == 1:
+        return x.float(), y.float()
+    B, H, L = x.shape[:3]
+    n, rest = L // world, tuple(x.shape[3:])
+    buf = torch.empty((world, 2, B, H, n) + rest, dtype=torch.float32, device=x.device)
+    perm = (2, 0, 1, 3) + tuple(range(4, 4 + len(rest)))
+    for i, t in enumerate((x, y)):
+        buf[:, i].copy_(t.reshape((B, H, world, n) + rest).permute(perm))
+    out = torch.empty((2, B, H, n) + rest, dtype=torch.float32, device=x.device)
+    dist.reduce_scatter_tensor(out, buf.view((world * 2, B, H, n) + rest), group=group)
+    return out[0], out[1]
+
+
 def _reduce_scatter_seq(x, group):
     """x: (B, H, world * n, ...) per-rank partial sums -> this rank's (B, H, n, ...)
     slice of the sum over ranks (one reduce_scatter_tensor per (b, h) slice)."""
@@ -191,11 +228,11 @@ class ShardedBlockSparse:
         world, rank, nblk, a = self._geometry(q)
         nq = q.shape[2] // self.bs
         qp_local = self.ops.pool(q, self.bs)                  # (B, H, nq, D) fp32
-        kp = _gather_seq(self.ops.pool(k, self.bs), self.group)
+        kp = _gather_small(self.ops.pool(k, self.bs), self.group)
         if world == 1 or not self.causal:
             qp = None
         else:
-            qp = _gather_seq(qp_local, self.group)
+            qp = _gather_small(qp_local, self.group)
         if before_exchange is not None:
             before_exchange()                                 # start the K/V gathers
         if qp is None:
@@ -208,7 +245,7 @@ class ShardedBlockSparse:
         pad = torch.zeros(mine.shape[0], mine.shape[1], width, mine.shape[3], dtype=mine.dtype,
                           device=mine.device)
         pad[:, :, :s1 - s0] = mine
-        every = _gather_seq(pad, self.group)                  # (B, H, world * width, W)
+        every = _gather_small(pad, self.group)                # (B, H, world * width, W)
         rows = torch.cat([every[:, :, r * width:r * width + (e - b)]
                           for r, (b, e) in enumerate(ranges)], dim=2)
         return rows[:, :, a:a + nq].contiguous()
@@ -265,6 +302,5 @@ class ShardedBlockSparse:
                                        q_blk0=a)
         if _world(self.group)[0] == 1:
             return dq, dk, dv
-        dk_s = _reduce_scatter_seq(dk.float(), self.group)
-        dv_s = _reduce_scatter_seq(dv.float(), self.group)
+        dk_s, dv_s = _reduce_scatter_pair(dk, dv, self.group)
         return dq, dk_s.to(dk.dtype), dv_s.to(dv.dtype)
