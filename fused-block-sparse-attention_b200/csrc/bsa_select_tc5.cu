@@ -327,7 +327,37 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (e_err) break;
       const int cend = min(kN, jend - k0);  // columns < cend may be valid for this row
       const float nbmax = fmaxf(fmaxf(nbs[0], nbs[1]), fmaxf(nbs[2], nbs[3]));
-      const float cut = __fsub_rd(Ls[KT - 1], __fmul_ru(ka, nbmax));
+      float cut = __fsub_rd(Ls[KT - 1], __fmul_ru(ka, nbmax));
+      if (__any_sync(0xffffffffu, Li[KT - 1] == INT_MAX)) {
+        // a list of this warp is not full yet (its cut is -inf): bound the tile's
+        // own KT-th best instead.  The minimum over KT disjoint column groups of
+        // the group maxima of S~ is <= the KT-th largest S~ of the tile (t), and
+        // a key among the tile's best KT exact scores has s >= t - E, so
+        // S~ >= t - 2E (E = ka * max|b| >= eps of every key): exact to skip the rest.
+        constexpr int GS = kN / KT;  // columns per group
+        float tmin = INFINITY;
+#pragma unroll
+        for (int ch = 0; ch < kN / 32; ++ch) {
+          const int cc = ch * 32;
+          __syncwarp();
+          float v[32];
+          tc05::ld32(tc05::taddr(tmem, warp * 32, b * kN + cc), v);
+          tc05::wait_ld();
+          const int lim = min(max(cend - cc, 0), 32);
+#pragma unroll
+          for (int g0 = 0; g0 < 32; g0 += GS) {
+            float gm = -INFINITY;
+#pragma unroll
+            for (int c = g0; c < g0 + GS; ++c) {
+              const bool ok = c < lim && k0 + cc + c != jskip;
+              gm = fmaxf(gm, ok ? v[c] : -INFINITY);
+            }
+            tmin = fminf(tmin, gm);
+          }
+        }
+        const float e2 = 2.f * __fmul_ru(ka, nbmax);
+        cut = fmaxf(cut, __fsub_rd(tmin, e2));
+      }
       // 1. candidate masks of the four 32-column chunks, branch-free: valid
       //    columns, and the approximate score against the current threshold
       unsigned mk[kN / 32];
