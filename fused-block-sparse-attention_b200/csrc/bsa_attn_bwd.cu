@@ -685,6 +685,33 @@ __global__ void dkdv_reduce_kernel(const AttnParams p, const BwdPlan pl, int BS,
   const int hk = hs * pl.Y + blockIdx.y;
   T *dkp = reinterpret_cast<T *>(p.dk) + b * p.dk_sb + hk * p.dk_sh;
   T *dvp = reinterpret_cast<T *>(p.dv) + b * p.dv_sb + hk * p.dv_sh;
+  if constexpr (sizeof(T) == 2) if ((D & 3) == 0 && (p.dk_sl & 3) == 0 && (p.dv_sl & 3) == 0 &&
+      (reinterpret_cast<uintptr_t>(dkp) & 7) == 0 && (reinterpret_cast<uintptr_t>(dvp) & 7) == 0) {
+    // four columns per thread: float4 partial loads, 8-byte stores (same
+    // summation order per element as below)
+    for (int i = 4 * threadIdx.x; i < BS * D; i += 4 * blockDim.x) {
+      const int r = i / D, d = i % D;
+      float4 sk = make_float4(0.f, 0.f, 0.f, 0.f), sv = sk;
+      for (unsigned c = 0; c < nch; ++c) {
+        const float *part =
+            pl.part + ((long long)(part_off + c) * pl.Y + blockIdx.y) * (2LL * BS * D);
+        const float4 a = *reinterpret_cast<const float4 *>(part + i);
+        const float4 v = *reinterpret_cast<const float4 *>(part + BS * D + i);
+        sk.x += a.x; sk.y += a.y; sk.z += a.z; sk.w += a.w;
+        sv.x += v.x; sv.y += v.y; sv.z += v.z; sv.w += v.w;
+      }
+      const long long g = (long long)kb * p.bs + r;
+      if (g >= p.L) continue;
+      uint2 wk, wv;
+      wk.x = Mma<T>::pack(sk.x * p.scale, sk.y * p.scale);
+      wk.y = Mma<T>::pack(sk.z * p.scale, sk.w * p.scale);
+      wv.x = Mma<T>::pack(sv.x, sv.y);
+      wv.y = Mma<T>::pack(sv.z, sv.w);
+      *reinterpret_cast<uint2 *>(dkp + g * p.dk_sl + d) = wk;
+      *reinterpret_cast<uint2 *>(dvp + g * p.dv_sl + d) = wv;
+    }
+    return;
+  }
   for (int i = threadIdx.x; i < BS * D; i += blockDim.x) {
     const int r = i / D, d = i % D;
     float sk = 0.f, sv = 0.f;
