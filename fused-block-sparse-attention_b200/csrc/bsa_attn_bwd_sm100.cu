@@ -299,9 +299,14 @@ __global__ void __launch_bounds__(352, 1)
     // ================= MMA issuers: warp 9 for tile A, warp 10 for tile B, each
     // polling the tile's S/dP queue and its dV/dK queue (tcgen05.commit tracks
     // the issuing thread's own MMAs; the shared ring stage and K/V buffer are
-    // released by one commit of each)
-    if (lane == 0) {
+    // released by one commit of each).  The whole warp runs the loop, so the
+    // descriptors stay warp-uniform; barrier tests are made uniform by a vote and
+    // one elected lane (always lane 0) issues the MMAs and commits.
+    {
       const int t = warp - 9;
+      auto test = [&](uint64_t *bar, uint32_t par) {
+        return __any_sync(0xffffffffu, mbar_test(bar, par));
+      };
       // descriptors built once; per MMA only a 64-bit add
       const uint64_t dkv0 = tc05::sdesc(smem_u32(sKV), 16, 1024);          // K, V (A, K-major)
       const uint64_t drk0 = tc05::sdesc(smem_u32(sR), 16, 1024);           // Q, dO as K-major B
@@ -316,7 +321,7 @@ __global__ void __launch_bounds__(352, 1)
       while (have_g) {
         bool progress = false;
         // ---- open the next unit of the S queue once its K/V have landed
-        if (have_s && !s_open && mbar_test(&kv_full[nes % NKV], (nes / NKV) & 1)) {
+        if (have_s && !s_open && test(&kv_full[nes % NKV], (nes / NKV) & 1)) {
           sns = s_unit[nes & 7][2];
           sn = s_unit[nes & 7][t];
           if (sns < 0) {
@@ -328,9 +333,9 @@ __global__ void __launch_bounds__(352, 1)
         }
         // ---- dV += P^T dO, dK += dS^T Q, step gsg (its unit neg was opened by
         // the S queue, which runs ahead)
-        if (gsg < gss && mbar_test(&p_full[t][gsg % B5_NSB], (gsg / B5_NSB) & 1) &&
+        if (gsg < gss && test(&p_full[t][gsg % B5_NSB], (gsg / B5_NSB) & 1) &&
             (jg > 0 || neg < B5_NAB ||
-             mbar_test(&acc_empty[t][neg % B5_NAB], ((neg / B5_NAB) - 1) & 1))) {
+             test(&acc_empty[t][neg % B5_NAB], ((neg / B5_NAB) - 1) & 1))) {
           if (jg == 0) {
             gns = s_unit[neg & 7][2];
             gn = s_unit[neg & 7][t];
@@ -345,15 +350,21 @@ __global__ void __launch_bounds__(352, 1)
             const uint32_t ads = tc05::taddr(tmem, 16 * t, B5_DPCOL + 64 * bb);
             const uint32_t dv = tc05::taddr(tmem, 16 * t, B5_DVCOL + 128 * ab);
             const uint32_t dk = tc05::taddr(tmem, 16 * t, B5_DKCOL + 128 * ab);
+            if (tc05::elect_one()) {
 #pragma unroll
-            for (int ks = 0; ks < B5_BS / 16; ++ks) {
-              const uint32_t acc = (jg > 0 || ks > 0) ? 1u : 0u;
-              tc05::mma_f16_ts(dv, ap + ks * 8, tc05::dadd(bdo, ks * 2048), IDESC_KM, acc);
-              tc05::mma_f16_ts(dk, ads + ks * 8, tc05::dadd(bq, ks * 2048), IDESC_KM, acc);
+              for (int ks = 0; ks < B5_BS / 16; ++ks) {
+                const uint32_t acc = (jg > 0 || ks > 0) ? 1u : 0u;
+                tc05::mma_f16_ts(dv, ap + ks * 8, tc05::dadd(bdo, ks * 2048), IDESC_KM, acc);
+                tc05::mma_f16_ts(dk, ads + ks * 8, tc05::dadd(bq, ks * 2048), IDESC_KM, acc);
+              }
             }
+            __syncwarp();
           }
-          tc05::commit(&r_empty[st]);  // count 2: the stage is free once both tiles are done
-          tc05::commit(&s_empty[t][bb]);
+          if (tc05::elect_one()) {
+            tc05::commit(&r_empty[st]);  // count 2: the stage is free once both tiles are done
+            tc05::commit(&s_empty[t][bb]);
+          }
+          __syncwarp();
           ++gsg;
           if (++jg == gns) {
             jg = 0;
@@ -364,8 +375,8 @@ __global__ void __launch_bounds__(352, 1)
           have_g = false;  // every opened step is done and no unit follows
         }
         // ---- S^T = K Q^T, dP^T = V dO^T, step gss
-        if (s_open && mbar_test(&r_full[gss % B5_NST], (gss / B5_NST) & 1) &&
-            (gss < B5_NSB || mbar_test(&s_empty[t][gss % B5_NSB], ((gss / B5_NSB) - 1) & 1))) {
+        if (s_open && test(&r_full[gss % B5_NST], (gss / B5_NST) & 1) &&
+            (gss < B5_NSB || test(&s_empty[t][gss % B5_NSB], ((gss / B5_NSB) - 1) & 1))) {
           const int st = gss % B5_NST, bb = gss % B5_NSB;
           tc05::fence_after();
           if (js < sn) {
@@ -375,16 +386,23 @@ __global__ void __launch_bounds__(352, 1)
             const uint64_t bq = tc05::dadd(drk0, roff), bdo = tc05::dadd(drk0, roff + B5_TILE);
             const uint32_t ds = tc05::taddr(tmem, 16 * t, B5_SCOL + 64 * bb);
             const uint32_t ddp = tc05::taddr(tmem, 16 * t, B5_DPCOL + 64 * bb);
+            if (tc05::elect_one()) {
 #pragma unroll
-            for (int ks = 0; ks < B5_D / 16; ++ks) {
-              tc05::mma_f16(ds, tc05::dadd(ak, ks * 32), tc05::dadd(bq, ks * 32), IDESC_KK, ks > 0);
-              tc05::mma_f16(ddp, tc05::dadd(av, ks * 32), tc05::dadd(bdo, ks * 32), IDESC_KK, ks > 0);
+              for (int ks = 0; ks < B5_D / 16; ++ks) {
+                tc05::mma_f16(ds, tc05::dadd(ak, ks * 32), tc05::dadd(bq, ks * 32), IDESC_KK, ks > 0);
+                tc05::mma_f16(ddp, tc05::dadd(av, ks * 32), tc05::dadd(bdo, ks * 32), IDESC_KK, ks > 0);
+              }
             }
+            __syncwarp();
           }
-          tc05::commit(&s_full[t][bb]);
+          const bool last = js + 1 == sns;
+          if (tc05::elect_one()) {
+            tc05::commit(&s_full[t][bb]);
+            if (last) tc05::commit(&kv_empty[nes % NKV]);  // count 2: last readers of the K/V buffer
+          }
+          __syncwarp();
           ++gss;
           if (++js == sns) {
-            tc05::commit(&kv_empty[nes % NKV]);  // count 2: last readers of the K/V buffer
             js = 0;
             ++nes;
             s_open = false;

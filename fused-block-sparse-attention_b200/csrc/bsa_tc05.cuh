@@ -53,6 +53,14 @@ __device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64
       : "memory");
 }
 
+// One thread of the (converged) warp, the same one every call: the lowest lane.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t p;
+  asm volatile("{\n\t.reg .pred e;\n\telect.sync _|e, 0xffffffff;\n\tselp.u32 %0, 1, 0, e;\n\t}"
+               : "=r"(p));
+  return p != 0;
+}
+
 // D[tmem] (+)= A[tmem] * B[smem], kind::f16: A (M x K, K-major) in the data-path
 // layout of D with two 16-bit elements per 32-bit column; a K-step of 16 spans 8
 // columns.
