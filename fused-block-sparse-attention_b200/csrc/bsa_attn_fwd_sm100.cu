@@ -187,8 +187,14 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
   } else if (warp == 5) {
-    // ================= MMA issuer (S and PV queues, polled)
-    if (lane == 0) {
+    // ================= MMA issuer (S and PV queues, polled).  The whole warp runs
+    // the loop, so the descriptors stay warp-uniform; barrier tests are made
+    // uniform by a vote and one elected lane (always lane 0) issues the MMAs and
+    // commits.
+    {
+      auto test = [&](uint64_t *bar, uint32_t par) {
+        return __any_sync(0xffffffffu, mbar_test(bar, par));
+      };
       if (!mbar_wait(&bar_q, 0)) report(p.status, BSA_DEVERR_TIMEOUT);
       // descriptors built once; per MMA only a 64-bit add (the issuing thread's
       // scalar work is on the critical path of every step)
@@ -199,8 +205,7 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t idle = 0;
       while (js < nsteps || jp < nsteps) {
         bool progress = false;
-        if (jp < js && mbar_test(&p_full[jp & 1], (jp >> 1) & 1) &&
-            mbar_test(&v_full[jp % NV], (jp / NV) & 1)) {
+        if (jp < js && test(&p_full[jp & 1], (jp >> 1) & 1) && test(&v_full[jp % NV], (jp / NV) & 1)) {
           const int st = jp % NV, bb = jp & 1;
           tc05::fence_after();
           for (int t = 0; t < 2; ++t) {
@@ -209,20 +214,26 @@ __global__ void __launch_bounds__(192, 1)
             const uint32_t ta = tc05::taddr(tmem, 16 * t, F5_SCOL0 + 64 * bb);
             const uint64_t db = tc05::dadd(dv0, (st * 2 + t) * F5_TILE);
             const uint32_t d = tc05::taddr(tmem, 16 * t, F5_OCOL);
+            if (tc05::elect_one()) {
 #pragma unroll
-            for (int ks = 0; ks < F5_BS / 16; ++ks)
-              tc05::mma_f16_ts(d, ta + ks * 8, tc05::dadd(db, ks * 2048), IDESC_PV,
-                               (jp > 0 || ks > 0) ? 1u : 0u);
+              for (int ks = 0; ks < F5_BS / 16; ++ks)
+                tc05::mma_f16_ts(d, ta + ks * 8, tc05::dadd(db, ks * 2048), IDESC_PV,
+                                 (jp > 0 || ks > 0) ? 1u : 0u);
+            }
+            __syncwarp();
           }
-          tc05::commit(&v_empty[st]);
-          tc05::commit(&s_empty[bb]);
-          tc05::commit(&o_done);
-          if (jp == nsteps - 1) tc05::commit(&o_final);
+          if (tc05::elect_one()) {
+            tc05::commit(&v_empty[st]);
+            tc05::commit(&s_empty[bb]);
+            tc05::commit(&o_done);
+            if (jp == nsteps - 1) tc05::commit(&o_final);
+          }
+          __syncwarp();
           ++jp;
           progress = true;
         }
-        if (js < nsteps && mbar_test(&k_full[js % NK], (js / NK) & 1) &&
-            (js < 2 || mbar_test(&s_empty[js & 1], ((js >> 1) - 1) & 1))) {
+        if (js < nsteps && test(&k_full[js % NK], (js / NK) & 1) &&
+            (js < 2 || test(&s_empty[js & 1], ((js >> 1) - 1) & 1))) {
           const int st = js % NK, bb = js & 1;
           tc05::fence_after();
           for (int t = 0; t < 2; ++t) {
@@ -230,12 +241,18 @@ __global__ void __launch_bounds__(192, 1)
             const uint64_t da = tc05::dadd(dq0, t * F5_TILE);
             const uint64_t db = tc05::dadd(dk0, (st * 2 + t) * F5_TILE);
             const uint32_t d = tc05::taddr(tmem, 16 * t, F5_SCOL0 + 64 * bb);
+            if (tc05::elect_one()) {
 #pragma unroll
-            for (int ks = 0; ks < F5_D / 16; ++ks)
-              tc05::mma_f16(d, tc05::dadd(da, ks * 32), tc05::dadd(db, ks * 32), IDESC_S, ks > 0);
+              for (int ks = 0; ks < F5_D / 16; ++ks)
+                tc05::mma_f16(d, tc05::dadd(da, ks * 32), tc05::dadd(db, ks * 32), IDESC_S, ks > 0);
+            }
+            __syncwarp();
           }
-          tc05::commit(&s_full[bb]);
-          tc05::commit(&k_empty[st]);
+          if (tc05::elect_one()) {
+            tc05::commit(&s_full[bb]);
+            tc05::commit(&k_empty[st]);
+          }
+          __syncwarp();
           ++js;
           progress = true;
         }
