@@ -135,16 +135,16 @@ __global__ void __launch_bounds__(192, 2)
       }
     }
   } else if (warp == 5) {
-    // ================= MMA issuer
-    if (lane == 0) {
+    // ================= MMA issuer: the whole warp walks the steps (warp-uniform
+    // descriptors and waits); one elected lane, always lane 0, issues the MMAs
+    // and commits
+    {
       // both operands MN-major: rows are keys (the K dimension), 128 B of M/N
       const uint64_t d0 = tc05::sdesc(smem_u32(smem), DS_BS * 128, 1024);
-      bool ok = true;
-      for (int j = 0; j < nsteps && ok; ++j) {
+      for (int j = 0; j < nsteps; ++j) {
         const int st = j % DS_NST;
-        if (!mbar_wait(&full[st], (j / DS_NST) & 1)) {
+        if (!mbar_wait_warp(&full[st], (j / DS_NST) & 1)) {
           report(p.status, BSA_DEVERR_TIMEOUT);
-          ok = false;
           break;
         }
         tc05::fence_after();
@@ -153,14 +153,19 @@ __global__ void __launch_bounds__(192, 2)
           const uint64_t da = tc05::dadd(d0, (st * 4 + t) * DS_TILE);
           const uint64_t db = tc05::dadd(d0, (st * 4 + 2 + t) * DS_TILE);
           const uint32_t d = tc05::taddr(tmem, 16 * t, 0);
+          if (tc05::elect_one()) {
 #pragma unroll
-          for (int ks = 0; ks < DS_BS / 16; ++ks)
-            tc05::mma_f16(d, tc05::dadd(da, ks * 2048), tc05::dadd(db, ks * 2048), IDESC,
-                          (j > 0 || ks > 0) ? 1u : 0u);
+            for (int ks = 0; ks < DS_BS / 16; ++ks)
+              tc05::mma_f16(d, tc05::dadd(da, ks * 2048), tc05::dadd(db, ks * 2048), IDESC,
+                            (j > 0 || ks > 0) ? 1u : 0u);
+          }
+          __syncwarp();
         }
-        tc05::commit(&empty[st]);
+        if (tc05::elect_one()) tc05::commit(&empty[st]);
+        __syncwarp();
       }
-      tc05::commit(&done);  // arrives once every MMA issued above has completed
+      if (tc05::elect_one()) tc05::commit(&done);  // arrives once every MMA issued above has completed
+      __syncwarp();
     }
   } else {
     // ================= epilogue warps 0-3: dQ * scale

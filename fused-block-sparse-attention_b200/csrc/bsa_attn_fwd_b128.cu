@@ -172,45 +172,55 @@ __global__ void __launch_bounds__(G8_THREADS, G8<D>::MINB)
       }
     }
   } else if (warp == G8_WMMA) {
-    // ================= MMA issuer
-    if (lane == 0) {
-      if (!mbar_wait((D == 256 && p.rope_cos) ? &q_ready : &bar_q, 0))
+    // ================= MMA issuer: the whole warp runs the sequence (warp-uniform
+    // descriptors and waits); one elected lane, always lane 0, issues the MMAs
+    // and commits
+    {
+      if (!mbar_wait_warp((D == 256 && p.rope_cos) ? &q_ready : &bar_q, 0))
         report(p.status, BSA_DEVERR_TIMEOUT);
       const uint64_t dq = tc05::sdesc(smem_u32(sQ), 16, 1024);
       int n = 0;
       auto issue_s = [&](int js) {
-        if (js >= 1 && !mbar_wait(&s_empty, (js - 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
+        if (js >= 1 && !mbar_wait_warp(&s_empty, (js - 1) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
         for (int c = 0; c < NCH; ++c, ++n) {
           const int sl = n % NSL;
-          if (!mbar_wait(&r_full[sl], (n / NSL) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
+          if (!mbar_wait_warp(&r_full[sl], (n / NSL) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
           tc05::fence_after();
           const uint64_t dk = tc05::sdesc(smem_u32(sR + sl * G8_TILE), 16, 1024);
           const uint64_t dqc = dq + c * (G8_TILE >> 4);
+          if (tc05::elect_one()) {
 #pragma unroll
-          for (int ks = 0; ks < 4; ++ks)
-            tc05::mma_f16(tc05::taddr(tmem, 0, G8_SCOL), dqc + 2 * ks, dk + 2 * ks, IDESC_S,
-                          (c > 0 || ks > 0) ? 1u : 0u);
-          tc05::commit(&r_empty[sl]);
+            for (int ks = 0; ks < 4; ++ks)
+              tc05::mma_f16(tc05::taddr(tmem, 0, G8_SCOL), dqc + 2 * ks, dk + 2 * ks, IDESC_S,
+                            (c > 0 || ks > 0) ? 1u : 0u);
+            tc05::commit(&r_empty[sl]);
+          }
+          __syncwarp();
         }
-        tc05::commit(&s_full);
+        if (tc05::elect_one()) tc05::commit(&s_full);
+        __syncwarp();
       };
       if (nsteps > 0) issue_s(0);
       for (int jp = 0; jp < nsteps; ++jp) {
         if (jp + 1 < nsteps) issue_s(jp + 1);
-        if (!mbar_wait(&p_full, jp & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
+        if (!mbar_wait_warp(&p_full, jp & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
         for (int c = 0; c < NCH; ++c, ++n) {
           const int sl = n % NSL;
-          if (!mbar_wait(&r_full[sl], (n / NSL) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
+          if (!mbar_wait_warp(&r_full[sl], (n / NSL) & 1)) report(p.status, BSA_DEVERR_TIMEOUT);
           tc05::fence_after();
           const uint64_t dv = tc05::sdesc(smem_u32(sR + sl * G8_TILE), G8_TILE, 1024);
+          if (tc05::elect_one()) {
 #pragma unroll
-          for (int ks = 0; ks < G8_BS / 16; ++ks)  // keys 16*ks: P columns 8*ks (16-bit pairs)
-            tc05::mma_f16_ts(tc05::taddr(tmem, 0, G8_OCOL + 64 * c),
-                             tc05::taddr(tmem, 0, G8_PCOL + 8 * ks), dv + 128 * ks, IDESC_PV,
-                             (jp > 0 || ks > 0) ? 1u : 0u);
-          tc05::commit(&r_empty[sl]);
+            for (int ks = 0; ks < G8_BS / 16; ++ks)  // keys 16*ks: P columns 8*ks (16-bit pairs)
+              tc05::mma_f16_ts(tc05::taddr(tmem, 0, G8_OCOL + 64 * c),
+                               tc05::taddr(tmem, 0, G8_PCOL + 8 * ks), dv + 128 * ks, IDESC_PV,
+                               (jp > 0 || ks > 0) ? 1u : 0u);
+            tc05::commit(&r_empty[sl]);
+          }
+          __syncwarp();
         }
-        tc05::commit(&o_done);
+        if (tc05::elect_one()) tc05::commit(&o_done);
+        __syncwarp();
       }
     }
   } else {

@@ -76,6 +76,14 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity) {
   return false;
 }
 
+// The same bounded wait for a whole converged warp: the lanes poll together and
+// a vote makes the outcome warp-uniform.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i)
+    if (__any_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+  return false;
+}
+
 // 4-D tiled TMA load (no multicast) of one box into shared memory, completing
 // on `bar` with the box's byte count.
 __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *map, uint64_t *bar,
