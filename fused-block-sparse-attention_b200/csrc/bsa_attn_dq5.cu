@@ -170,9 +170,14 @@ __global__ void __launch_bounds__(192, 2)
       }
     }
   } else if (warp == 5) {
-    // ================= MMA issuer: S/dP queue and dQ queue, polled
-    if (lane == 0) {
-      if (!mbar_wait(&bar_q, 0)) report(p.status, BSA_DEVERR_TIMEOUT);
+    // ================= MMA issuer: S/dP queue and dQ queue, polled by the whole
+    // warp (warp-uniform descriptors; barrier tests made uniform by a vote); one
+    // elected lane, always lane 0, issues the MMAs and commits
+    {
+      auto test = [&](uint64_t *bar, uint32_t par) {
+        return __any_sync(0xffffffffu, mbar_test(bar, par));
+      };
+      if (!mbar_wait_warp(&bar_q, 0)) report(p.status, BSA_DEVERR_TIMEOUT);
       // descriptors built once; per MMA only a 64-bit add
       const uint64_t dq0 = tc05::sdesc(smem_u32(sQ), 16, 1024);
       const uint64_t ddo0 = tc05::sdesc(smem_u32(sDO), 16, 1024);
@@ -185,7 +190,7 @@ __global__ void __launch_bounds__(192, 2)
       while (jg < nsteps) {
         bool progress = false;
         // dQ += dS_jg K_jg once the elementwise warps have written dS_jg
-        if (jg < js && mbar_test(&ds_full, jg & 1)) {
+        if (jg < js && test(&ds_full, jg & 1)) {
           const int st = jg % D5_KST;
           tc05::fence_after();
           for (int t = 0; t < 2; ++t) {
@@ -194,19 +199,25 @@ __global__ void __launch_bounds__(192, 2)
             const uint64_t db = tc05::dadd(dkm0, (st * 2 + t) * D5_TILE);
             const uint32_t d = tc05::taddr(tmem, 16 * t, D5_DQCOL);
             // a tile's first live step starts its accumulator
+            if (tc05::elect_one()) {
 #pragma unroll
-            for (int ks = 0; ks < D5_BS / 16; ++ks)
-              tc05::mma_f16(d, tc05::dadd(da, ks * 32), tc05::dadd(db, ks * 2048), IDESC_DQ,
-                            (jg > 0 || ks > 0) ? 1u : 0u);
+              for (int ks = 0; ks < D5_BS / 16; ++ks)
+                tc05::mma_f16(d, tc05::dadd(da, ks * 32), tc05::dadd(db, ks * 2048), IDESC_DQ,
+                              (jg > 0 || ks > 0) ? 1u : 0u);
+            }
+            __syncwarp();
           }
-          tc05::commit(&k_empty[st]);
-          tc05::commit(&dq_done);
+          if (tc05::elect_one()) {
+            tc05::commit(&k_empty[st]);
+            tc05::commit(&dq_done);
+          }
+          __syncwarp();
           ++jg;
           progress = true;
         }
         // S_js, dP_js once K_js, V_js have landed and S/dP of js-1 have been read
-        if (js < nsteps && mbar_test(&k_full[js % D5_KST], (js / D5_KST) & 1) &&
-            mbar_test(&v_full, js & 1) && (js < 1 || mbar_test(&sd_empty, (js - 1) & 1))) {
+        if (js < nsteps && test(&k_full[js % D5_KST], (js / D5_KST) & 1) &&
+            test(&v_full, js & 1) && (js < 1 || test(&sd_empty, (js - 1) & 1))) {
           const int st = js % D5_KST;
           tc05::fence_after();
           for (int t = 0; t < 2; ++t) {
@@ -215,14 +226,20 @@ __global__ void __launch_bounds__(192, 2)
             const uint64_t bk = tc05::dadd(dk0, (st * 2 + t) * D5_TILE), bv = tc05::dadd(dv0, t * D5_TILE);
             const uint32_t ds = tc05::taddr(tmem, 16 * t, D5_SCOL);
             const uint32_t ddp = tc05::taddr(tmem, 16 * t, D5_DPCOL);
+            if (tc05::elect_one()) {
 #pragma unroll
-            for (int ks = 0; ks < D5_D / 16; ++ks) {
-              tc05::mma_f16(ds, tc05::dadd(aq, ks * 32), tc05::dadd(bk, ks * 32), IDESC_S, ks > 0);
-              tc05::mma_f16(ddp, tc05::dadd(ado, ks * 32), tc05::dadd(bv, ks * 32), IDESC_S, ks > 0);
+              for (int ks = 0; ks < D5_D / 16; ++ks) {
+                tc05::mma_f16(ds, tc05::dadd(aq, ks * 32), tc05::dadd(bk, ks * 32), IDESC_S, ks > 0);
+                tc05::mma_f16(ddp, tc05::dadd(ado, ks * 32), tc05::dadd(bv, ks * 32), IDESC_S, ks > 0);
+              }
             }
+            __syncwarp();
           }
-          tc05::commit(&sd_full);
-          tc05::commit(&v_empty);
+          if (tc05::elect_one()) {
+            tc05::commit(&sd_full);
+            tc05::commit(&v_empty);
+          }
+          __syncwarp();
           ++js;
           progress = true;
         }
