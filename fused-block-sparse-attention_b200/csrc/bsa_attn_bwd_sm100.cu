@@ -172,11 +172,11 @@ __global__ void __launch_bounds__(352, 1)
   if (warp == 8) {
     // ================= producer: K/V per unit (2 buffers), Q/dO/lse/Dvec per step (ring).
     // The whole warp reads a unit's CSR entries (<= 32 per tile) and gate values
-    // at once; lane 0 then issues the loads step by step from shared memory.
+    // at once; one elected lane then issues the loads step by step from shared
+    // memory while the warp waits with it.
     __shared__ int s_pq[2][32], s_ps[2][32];
     __shared__ float s_pg[2][32];
     int gs = 0, ne = 0, iu = 0;
-    uint32_t idle = 0;
     for (int u = blockIdx.x; u < nunits; u += gridDim.x, ++iu) {
       B5Unit w;
       b5_unit(pl, p, total, u, w);
@@ -228,36 +228,35 @@ __global__ void __launch_bounds__(352, 1)
         }
       }
       __syncwarp();
-      if (lane != 0) continue;
-      // single K/V buffer: the previous unit's last S/dP MMAs must be done
+      // the loads are issued by one elected lane (lane 0); the warp stays
+      // converged so that the waits and addresses are warp-uniform
       const int kvb = ne % NKV;
-      if (ne >= NKV && !mbar_wait(&kv_empty[kvb], ((ne / NKV) - 1) & 1))
+      // K/V buffer: the earlier unit's last S/dP MMAs on it must be done
+      if (ne >= NKV && !mbar_wait_warp(&kv_empty[kvb], ((ne / NKV) - 1) & 1))
         report(p.status, BSA_DEVERR_TIMEOUT);
-      s_unit[ne & 7][0] = w.n[0];
-      s_unit[ne & 7][1] = w.n[1];
-      s_unit[ne & 7][2] = ns;
-      mbar_expect_tx(&kv_full[kvb], ((w.n[0] > 0) + (w.n[1] > 0)) * 2 * B5_TILE);
-      #pragma unroll
-      for (int t = 0; t < 2; ++t) {
-        if (w.n[t] == 0) continue;
-        uint8_t *dst = sKV + (kvb * 2 + t) * 2 * B5_TILE;
-        tma_load_rhb(dst, &tk, &kv_full[kvb], perm_k, 0, w.kb[t] * p.bs, w.hk[t], w.b[t]);
-        tma_load_rhb(dst + B5_TILE, &tv, &kv_full[kvb], perm_v, 0, w.kb[t] * p.bs, w.hk[t], w.b[t]);
+      if (tc05::elect_one()) {
+        s_unit[ne & 7][0] = w.n[0];
+        s_unit[ne & 7][1] = w.n[1];
+        s_unit[ne & 7][2] = ns;
+        mbar_expect_tx(&kv_full[kvb], ((w.n[0] > 0) + (w.n[1] > 0)) * 2 * B5_TILE);
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          if (w.n[t] == 0) continue;
+          uint8_t *dst = sKV + (kvb * 2 + t) * 2 * B5_TILE;
+          tma_load_rhb(dst, &tk, &kv_full[kvb], perm_k, 0, w.kb[t] * p.bs, w.hk[t], w.b[t]);
+          tma_load_rhb(dst + B5_TILE, &tv, &kv_full[kvb], perm_v, 0, w.kb[t] * p.bs, w.hk[t], w.b[t]);
+        }
       }
+      __syncwarp();
       ++ne;
       for (int j = 0; j < ns; ++j, ++gs) {
-          const int st = gs % B5_NST;
-          while (gs >= B5_NST && !mbar_test(&r_empty[st], ((gs / B5_NST) - 1) & 1)) {
-            if (++idle > kSpinLimit) {
-              report(p.status, BSA_DEVERR_TIMEOUT);
-              break;
-            }
-            __nanosleep(32);
-          }
-          idle = 0;
+        const int st = gs % B5_NST;
+        if (gs >= B5_NST && !mbar_wait_warp(&r_empty[st], ((gs / B5_NST) - 1) & 1))
+          report(p.status, BSA_DEVERR_TIMEOUT);
+        if (tc05::elect_one()) {
           const int act = (j < w.n[0]) + (j < w.n[1]);
           int mq[2], mh[2];
-          #pragma unroll
+#pragma unroll
           for (int t = 0; t < 2; ++t) {
             if (j >= w.n[t]) continue;
             const int en = j / p.grp;
@@ -271,7 +270,7 @@ __global__ void __launch_bounds__(352, 1)
           }
           // the arrive below releases the metadata stores to the r_full waiters
           mbar_expect_tx(&r_full[st], act * (2 * B5_TILE + 2 * B5_ROWB));
-          #pragma unroll
+#pragma unroll
           for (int t = 0; t < 2; ++t) {
             if (j >= w.n[t]) continue;
             const int qblk = mq[t], h = mh[t];
@@ -285,6 +284,8 @@ __global__ void __launch_bounds__(352, 1)
             bulk_load(rw + B5_BS, p.dvec + rb, B5_ROWB, &r_full[st]);
           }
         }
+        __syncwarp();
+      }
     }
     if (lane == 0) {
       // end of the unit sequence for the MMA issuer
