@@ -124,15 +124,22 @@ __global__ void __launch_bounds__(192, 2)
   const int nsteps = nA > nB ? nA : nB;
 
   if (warp == 4) {
-    // ================= TMA producer
-    if (lane == 0) {
-      mbar_expect_tx(&bar_q, (validB ? 4 : 2) * D5_TILE);
-      tma_load_rhb(sQ, &tq, &bar_q, perm_q, 0, qb0 * p.bs, h, b);
-      tma_load_rhb(sDO, &tdo, &bar_q, perm_do, 0, qb0 * p.bs, h, b);
-      if (validB) {
-        tma_load_rhb(sQ + D5_TILE, &tq, &bar_q, perm_q, 0, (qb0 + 1) * p.bs, h, b);
-        tma_load_rhb(sDO + D5_TILE, &tdo, &bar_q, perm_do, 0, (qb0 + 1) * p.bs, h, b);
+    // ================= TMA producer: the warp polls together (voted tests), one
+    // elected lane (lane 0) issues the loads
+    {
+      auto test = [&](uint64_t *bar, uint32_t par) {
+        return __any_sync(0xffffffffu, mbar_test(bar, par));
+      };
+      if (tc05::elect_one()) {
+        mbar_expect_tx(&bar_q, (validB ? 4 : 2) * D5_TILE);
+        tma_load_rhb(sQ, &tq, &bar_q, perm_q, 0, qb0 * p.bs, h, b);
+        tma_load_rhb(sDO, &tdo, &bar_q, perm_do, 0, qb0 * p.bs, h, b);
+        if (validB) {
+          tma_load_rhb(sQ + D5_TILE, &tq, &bar_q, perm_q, 0, (qb0 + 1) * p.bs, h, b);
+          tma_load_rhb(sDO + D5_TILE, &tdo, &bar_q, perm_do, 0, (qb0 + 1) * p.bs, h, b);
+        }
       }
+      __syncwarp();
       int jk = 0, jv = 0;
       uint32_t idle = 0;
       auto issue = [&](bool isv, int j) {
@@ -140,21 +147,24 @@ __global__ void __launch_bounds__(192, 2)
         uint64_t *full = isv ? &v_full : &k_full[st];
         uint8_t *ring = isv ? sV : sK + st * 2 * D5_TILE;
         const int act = (j < nA ? 1 : 0) + (j < nB ? 1 : 0);
-        mbar_expect_tx(full, act * D5_TILE);
-        for (int t = 0; t < 2; ++t) {
-          if (j >= (t ? nB : nA)) continue;
-          tma_load_rhb(ring + t * D5_TILE, isv ? &tv : &tk, full, isv ? perm_v : perm_k, 0,
-                       (s_item[t][j] >> 3) * p.bs, hk, b);
+        if (tc05::elect_one()) {
+          mbar_expect_tx(full, act * D5_TILE);
+          for (int t = 0; t < 2; ++t) {
+            if (j >= (t ? nB : nA)) continue;
+            tma_load_rhb(ring + t * D5_TILE, isv ? &tv : &tk, full, isv ? perm_v : perm_k, 0,
+                         (s_item[t][j] >> 3) * p.bs, hk, b);
+          }
         }
+        __syncwarp();
       };
       while (jk < nsteps || jv < nsteps) {
         bool progress = false;
         if (jk < nsteps &&
-            (jk < D5_KST || mbar_test(&k_empty[jk % D5_KST], ((jk / D5_KST) - 1) & 1))) {
+            (jk < D5_KST || test(&k_empty[jk % D5_KST], ((jk / D5_KST) - 1) & 1))) {
           issue(false, jk++);
           progress = true;
         }
-        if (jv < nsteps && (jv < 1 || mbar_test(&v_empty, (jv - 1) & 1))) {
+        if (jv < nsteps && (jv < 1 || test(&v_empty, (jv - 1) & 1))) {
           issue(true, jv++);
           progress = true;
         }

@@ -113,25 +113,29 @@ __global__ void __launch_bounds__(192, 2)
   const int nsteps = nA > nB ? nA : nB;
 
   if (warp == 4) {
-    // ================= TMA producer
-    if (lane == 0) {
+    // ================= TMA producer: the warp waits together (voted), one
+    // elected lane (lane 0) issues the loads
+    {
       for (int j = 0; j < nsteps; ++j) {
         const int st = j % DS_NST;
-        if (j >= DS_NST && !mbar_wait(&empty[st], ((j / DS_NST) - 1) & 1)) {
+        if (j >= DS_NST && !mbar_wait_warp(&empty[st], ((j / DS_NST) - 1) & 1)) {
           report(p.status, BSA_DEVERR_TIMEOUT);
           break;
         }
-        const int act = (j < nA ? 1 : 0) + (j < nB ? 1 : 0);
-        mbar_expect_tx(&full[st], act * 2 * DS_TILE);
-        uint8_t *ring = smem + st * 4 * DS_TILE;
-        for (int t = 0; t < 2; ++t) {
-          if (j >= (t ? nB : nA)) continue;
-          const long long e =
-              (((long long)b * p.Hq + h) * p.nq + (qb0 + t)) * p.kk + s_slot[t][j];
-          tma_load_rhb(ring + t * DS_TILE, &tds, &full[st], perm_ds, 0, (int)(e * DS_BS), 0, 0);
-          tma_load_rhb(ring + (2 + t) * DS_TILE, &tk, &full[st], perm_k, 0, s_kb[t][j] * p.bs, hk,
-                       b);
+        if (tc05::elect_one()) {
+          const int act = (j < nA ? 1 : 0) + (j < nB ? 1 : 0);
+          mbar_expect_tx(&full[st], act * 2 * DS_TILE);
+          uint8_t *ring = smem + st * 4 * DS_TILE;
+          for (int t = 0; t < 2; ++t) {
+            if (j >= (t ? nB : nA)) continue;
+            const long long e =
+                (((long long)b * p.Hq + h) * p.nq + (qb0 + t)) * p.kk + s_slot[t][j];
+            tma_load_rhb(ring + t * DS_TILE, &tds, &full[st], perm_ds, 0, (int)(e * DS_BS), 0, 0);
+            tma_load_rhb(ring + (2 + t) * DS_TILE, &tk, &full[st], perm_k, 0, s_kb[t][j] * p.bs,
+                         hk, b);
+          }
         }
+        __syncwarp();
       }
     }
   } else if (warp == 5) {

@@ -149,20 +149,27 @@ __global__ void __launch_bounds__(G8_THREADS, G8<D>::MINB)
   // j + 1 (if any) and the V chunks of step j; item number n uses slot n % NSL.
   // Producer and MMA issuer walk the same sequence with their own counters.
   if (warp == G8_WPROD) {
-    // ================= TMA producer
-    if (lane == 0) {
-      mbar_expect_tx(&bar_q, NCH * G8_TILE);
-      for (int c = 0; c < NCH; ++c)
-        tma_load_rhb(sQ + c * G8_TILE, &tq, &bar_q, perm_q, 64 * c, qi * p.bs, h, b);
+    // ================= TMA producer: the warp waits together (voted), one
+    // elected lane (lane 0) issues the loads
+    {
+      if (tc05::elect_one()) {
+        mbar_expect_tx(&bar_q, NCH * G8_TILE);
+        for (int c = 0; c < NCH; ++c)
+          tma_load_rhb(sQ + c * G8_TILE, &tq, &bar_q, perm_q, 64 * c, qi * p.bs, h, b);
+      }
+      __syncwarp();
       int n = 0;
       auto load = [&](bool isv, int j) {
         for (int c = 0; c < NCH; ++c, ++n) {
           const int sl = n % NSL;
-          if (n >= NSL && !mbar_wait(&r_empty[sl], ((n / NSL) - 1) & 1))
+          if (n >= NSL && !mbar_wait_warp(&r_empty[sl], ((n / NSL) - 1) & 1))
             report(p.status, BSA_DEVERR_TIMEOUT);
-          mbar_expect_tx(&r_full[sl], G8_TILE);
-          tma_load_rhb(sR + sl * G8_TILE, isv ? &tv : &tk, &r_full[sl], isv ? perm_v : perm_k,
-                       64 * c, (s_item[j] >> 3) * p.bs, hk, b);
+          if (tc05::elect_one()) {
+            mbar_expect_tx(&r_full[sl], G8_TILE);
+            tma_load_rhb(sR + sl * G8_TILE, isv ? &tv : &tk, &r_full[sl], isv ? perm_v : perm_k,
+                         64 * c, (s_item[j] >> 3) * p.bs, hk, b);
+          }
+          __syncwarp();
         }
       };
       if (nsteps > 0) load(false, 0);

@@ -143,13 +143,18 @@ __global__ void __launch_bounds__(192, 1)
   const int nsteps = nA > nB ? nA : nB;
 
   if (warp == 4) {
-    // ================= TMA producers (lane 0: Q and K, lane 1: V)
-    if (lane == 0) {
+    // ================= TMA producer: the warp polls both rings together (voted
+    // tests), one elected lane (lane 0) issues the loads
+    if (tc05::elect_one()) {
       mbar_expect_tx(&bar_q, (validB ? 2 : 1) * F5_TILE);
       tma_load_rhb(sQ, &tq, &bar_q, perm_q, 0, qb0 * p.bs, h, b);
       if (validB) tma_load_rhb(sQ + F5_TILE, &tq, &bar_q, perm_q, 0, (qb0 + 1) * p.bs, h, b);
     }
-    if (lane == 0) {
+    __syncwarp();
+    {
+      auto test = [&](uint64_t *bar, uint32_t par) {
+        return __any_sync(0xffffffffu, mbar_test(bar, par));
+      };
       int jk = 0, jv = 0;
       uint32_t idle = 0;
       auto issue = [&](bool isv, int j) {
@@ -157,21 +162,24 @@ __global__ void __launch_bounds__(192, 1)
         uint64_t *full = isv ? &v_full[st] : &k_full[st];
         uint8_t *ring = isv ? sV : sK;
         const int act = (j < nA ? 1 : 0) + (j < nB ? 1 : 0);
-        mbar_expect_tx(full, act * F5_TILE);
-        for (int t = 0; t < 2; ++t) {
-          if (j >= (t ? nB : nA)) continue;
-          const int kb = s_item[t][j] >> 3;
-          tma_load_rhb(ring + (st * 2 + t) * F5_TILE, isv ? &tv : &tk, full, isv ? perm_v : perm_k,
-                       0, kb * p.bs, hk, b);
+        if (tc05::elect_one()) {
+          mbar_expect_tx(full, act * F5_TILE);
+          for (int t = 0; t < 2; ++t) {
+            if (j >= (t ? nB : nA)) continue;
+            const int kb = s_item[t][j] >> 3;
+            tma_load_rhb(ring + (st * 2 + t) * F5_TILE, isv ? &tv : &tk, full, isv ? perm_v : perm_k,
+                         0, kb * p.bs, hk, b);
+          }
         }
+        __syncwarp();
       };
       while (jk < nsteps || jv < nsteps) {
         bool progress = false;
-        if (jk < nsteps && (jk < NK || mbar_test(&k_empty[jk % NK], ((jk / NK) - 1) & 1))) {
+        if (jk < nsteps && (jk < NK || test(&k_empty[jk % NK], ((jk / NK) - 1) & 1))) {
           issue(false, jk++);
           progress = true;
         }
-        if (jv < nsteps && (jv < NV || mbar_test(&v_empty[jv % NV], ((jv / NV) - 1) & 1))) {
+        if (jv < nsteps && (jv < NV || test(&v_empty[jv % NV], ((jv / NV) - 1) & 1))) {
           issue(true, jv++);
           progress = true;
         }
