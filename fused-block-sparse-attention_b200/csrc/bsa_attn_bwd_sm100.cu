@@ -461,17 +461,15 @@ __global__ void __launch_bounds__(352, 1)
         const float g2 = GATE ? s_g2[st][t] : 0.f;
         const float *lsep = sRow + (st * 2 + t) * 2 * B5_BS;
         float sv[2][16], dp[2][16];
+        // all four TMEM loads in flight before one wait
         tc05::ld16x2(tmem + lane_base + B5_SCOL + 64 * bb, sv[0]);
         tc05::ld16x2(tmem + lane_base + B5_DPCOL + 64 * bb, dp[0]);
+        tc05::ld16x2(tmem + lane_base + B5_SCOL + 64 * bb + 32, sv[1]);
+        tc05::ld16x2(tmem + lane_base + B5_DPCOL + 64 * bb + 32, dp[1]);
         tc05::wait_ld();
 #pragma unroll
         for (int g = 0; g < 2; ++g) {
           const int cg = 32 * g + 16 * hh;  // first query column of this group
-          if (g == 1) {
-            tc05::ld16x2(tmem + lane_base + B5_SCOL + 64 * bb + 32, sv[1]);
-            tc05::ld16x2(tmem + lane_base + B5_DPCOL + 64 * bb + 32, dp[1]);
-            tc05::wait_ld();
-          }
           if (active) {
             const long long q0 = (long long)qblk * p.bs + cg;
             if (triu || !key_ok || q0 + 16 > p.Lq) {  // diagonal / padded steps: explicit masks
