@@ -49,8 +49,8 @@ METRIC = "fwd+bwd tokens/s at 262k tok (selection+forward+backward)"
 # this bench (cold cache), and the source revision that capture was taken at.
 # A recorded figure, not measured by this run: it is printed with its revision so
 # that a stale figure is visible.
-TRAFFIC_262K = {"attn_bwd": 14.70e9, "attn_fwd": 1.17e9, "select": 0.57e9}
-TRAFFIC_REV = "d79a424"
+TRAFFIC_262K = {"attn_bwd": 14.70e9, "attn_fwd": 1.16e9, "select": 0.57e9}
+TRAFFIC_REV = "23a77c5"
 UNIT = "tokens/s"
 
 
