@@ -201,57 +201,71 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 4) {
     // ------------------------------------------------------------ TMA producer
-    if (lane == 0 && ntile > 0) {
-      prefetch_tmap(&map_a);
-      prefetch_tmap(&map_b);
-      mbar_expect_tx(a_full, TB);
-      for (int c = 0; c < NCH; ++c) tma_load_3d(sm + L.a + c * kM * 128, &map_a, a_full, c * 32, q0, g);
+    // (the warp waits together, one elected lane issues)
+    if (ntile > 0) {
+      if (tc05::elect_one()) {
+        prefetch_tmap(&map_a);
+        prefetch_tmap(&map_b);
+        mbar_expect_tx(a_full, TB);
+        for (int c = 0; c < NCH; ++c) tma_load_3d(sm + L.a + c * kM * 128, &map_a, a_full, c * 32, q0, g);
+      }
+      __syncwarp();
       int issued = 0;
       for (int t = 0; t < ntile; ++t) {
         const int s = t % NS;
-        if (t >= NS && !mbar_wait(&b_empty[s], ((t / NS) - 1) & 1)) {
-          report(a.status, BSA_DEVERR_TIMEOUT);
-          atomicOr(&s_err, 1);
+        if (t >= NS && !mbar_wait_warp(&b_empty[s], ((t / NS) - 1) & 1)) {
+          if (lane == 0) {
+            report(a.status, BSA_DEVERR_TIMEOUT);
+            atomicOr(&s_err, 1);
+          }
           break;
         }
         const int k0 = ((int)rank + t * C) * kN;
-        mbar_expect_tx(&b_full[s], TB);
-        for (int c = 0; c < NCH; ++c)
-          tma_load_3d(sm + L.b + s * TB + c * kM * 128, &map_b, &b_full[s], c * 32, k0, g);
+        if (tc05::elect_one()) {
+          mbar_expect_tx(&b_full[s], TB);
+          for (int c = 0; c < NCH; ++c)
+            tma_load_3d(sm + L.b + s * TB + c * kM * 128, &map_b, &b_full[s], c * 32, k0, g);
+        }
+        __syncwarp();
         issued = t + 1;
       }
       // every issued load has landed before the CTA can exit: the last NS
       // issued stages are waited for here (consumed ones complete at once)
       for (int t = max(0, issued - NS); t < issued; ++t)
-        if (!mbar_wait(&b_full[t % NS], (t / NS) & 1)) report(a.status, BSA_DEVERR_TIMEOUT);
-      mbar_wait(a_full, 0);
+        if (!mbar_wait_warp(&b_full[t % NS], (t / NS) & 1) && lane == 0)
+          report(a.status, BSA_DEVERR_TIMEOUT);
+      mbar_wait_warp(a_full, 0);
     }
   } else if (warp == 5) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0 && ntile > 0) {
+    // (the warp waits together, one elected lane issues the MMAs and commits)
+    if (ntile > 0) {
       constexpr uint32_t idesc = idesc_tf32(kM, kN);
-      bool ok = mbar_wait(a_full, 0);
+      bool ok = mbar_wait_warp(a_full, 0);
       const uint64_t adesc = tc05::sdesc(smem_u32(sm + L.a), 16, 1024);
       for (int t = 0; t < ntile && ok; ++t) {
         const int s = t % NS, b = t & 1;
-        if (t >= 2 && !mbar_wait(&acc_empty[b], ((t >> 1) - 1) & 1)) {
+        if (t >= 2 && !mbar_wait_warp(&acc_empty[b], ((t >> 1) - 1) & 1)) {
           ok = false;
           break;
         }
-        if (!mbar_wait(&b_full[s], (t / NS) & 1)) {
+        if (!mbar_wait_warp(&b_full[s], (t / NS) & 1)) {
           ok = false;
           break;
         }
         tc05::fence_after();
         const uint64_t bdesc = tc05::sdesc(smem_u32(sm + L.b + s * TB), 16, 1024);
+        if (tc05::elect_one()) {
 #pragma unroll
-        for (int k = 0; k < DIM / 8; ++k) {
-          const uint32_t koff = (uint32_t)((k >> 2) * kM * 128 + (k & 3) * 32);
-          mma_tf32(tmem + b * kN, tc05::dadd(adesc, koff), tc05::dadd(bdesc, koff), idesc, k > 0);
+          for (int k = 0; k < DIM / 8; ++k) {
+            const uint32_t koff = (uint32_t)((k >> 2) * kM * 128 + (k & 3) * 32);
+            mma_tf32(tmem + b * kN, tc05::dadd(adesc, koff), tc05::dadd(bdesc, koff), idesc, k > 0);
+          }
+          tc05::commit(&acc_full[b]);
         }
-        tc05::commit(&acc_full[b]);
+        __syncwarp();
       }
-      if (!ok) {
+      if (!ok && lane == 0) {
         report(a.status, BSA_DEVERR_TIMEOUT);
         atomicOr(&s_err, 1);
       }
