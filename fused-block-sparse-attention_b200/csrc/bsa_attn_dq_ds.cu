@@ -71,27 +71,19 @@ __global__ void __launch_bounds__(192, 2)
   const bool validB = qb0 + 1 < p.nq;
 
   // live slots: the entries the dK/dV kernel processed (same classification)
-  if (tid == 0 || tid == 32) {
-    const int t = tid >> 5;
+  if (warp < 2) {  // warp 0: tile A, warp 1: tile B
+    const int t = warp;
     const int qi = qb0 + t, qblk = p.q0 + qi;
     int n = 0;
     if (t == 0 || validB) {
       const int32_t *selrow = p.sel + b * p.sel_sb + hk * p.sel_sh + (long long)qi * p.sel_sn;
-      for (int slot = 0; slot < p.kk; ++slot) {
-        const int kb = __ldg(selrow + slot);
-        bool dup = false;
-        if (p.mask_mode == BSA_MASK_TOKEN)
-          for (int i = 0; i < slot && !dup; ++i) dup = __ldg(selrow + i) == kb;
-        const int kind =
-            slot_kind(kb, slot, dup, qblk, p.nblk, p.bs, p.L, p.mask_mode, p.causal, p.status);
-        if (kind != KIND_SKIP && n < DS_MAXN) {
-          s_kb[t][n] = kb;
-          s_slot[t][n] = slot;
-          ++n;
-        }
-      }
+      n = warp_live_slots(selrow, p.kk, DS_MAXN, qblk, p.nblk, p.bs, p.L, p.mask_mode, p.causal,
+                          p.status, [&](int pos, int kb, int, int slot) {
+                            s_kb[t][pos] = kb;
+                            s_slot[t][pos] = slot;
+                          });
     }
-    s_n[t] = n;
+    if (lane == 0) s_n[t] = n;
   }
   if (tid == 0) {
     for (int s = 0; s < DS_NST; ++s) {

@@ -94,35 +94,18 @@ __global__ void __launch_bounds__(G8_THREADS, G8<D>::MINB)
   const int qblk = p.q0 + qi;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
+  if (warp == 0) {  // live-slot list, built by the whole warp
+    const int32_t *selrow =
+        p.sel ? p.sel + b * p.sel_sb + hk * p.sel_sh + (long long)qi * p.sel_sn : nullptr;
+    const int n = warp_live_slots(selrow, p.sel ? p.kk : p.nblk, MAXN, qblk, p.nblk, p.bs, p.L,
+                                  p.mask_mode, p.causal, p.status,
+                                  [&](int pos, int kb, int kind, int slot) {
+                                    s_item[pos] = (kb << 3) | kind;
+                                    s_islot[pos] = slot;
+                                  });
+    if (lane == 0) s_n = n;
+  }
   if (tid == 0) {
-    int n = 0;
-    if (p.sel) {
-      const int32_t *selrow = p.sel + b * p.sel_sb + hk * p.sel_sh + (long long)qi * p.sel_sn;
-      for (int slot = 0; slot < p.kk; ++slot) {
-        const int kb = __ldg(selrow + slot);
-        bool dup = false;
-        if (p.mask_mode == BSA_MASK_TOKEN)
-          for (int i = 0; i < slot && !dup; ++i) dup = __ldg(selrow + i) == kb;
-        const int kind =
-            slot_kind(kb, slot, dup, qblk, p.nblk, p.bs, p.L, p.mask_mode, p.causal, p.status);
-        if (kind != KIND_SKIP && n < MAXN) {
-          s_item[n] = (kb << 3) | kind;
-          s_islot[n] = slot;
-          ++n;
-        }
-      }
-    } else {  // identity selection: slot j is block j
-      for (int kb = 0; kb < p.nblk && n < MAXN; ++kb) {
-        const int kind = slot_kind(kb, kb, false, qblk, p.nblk, p.bs, p.L, p.mask_mode, p.causal,
-                                   p.status);
-        if (kind != KIND_SKIP) {
-          s_item[n] = (kb << 3) | kind;
-          s_islot[n] = kb;
-          ++n;
-        }
-      }
-    }
-    s_n = n;
     mbar_init(&bar_q, 1);
     for (int s = 0; s < NSL; ++s) {
       mbar_init(&r_full[s], 1);

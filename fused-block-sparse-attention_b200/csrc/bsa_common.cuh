@@ -309,6 +309,42 @@ __device__ __forceinline__ int slot_kind(int kblk, int slot, bool dup, int qblk,
   return k;
 }
 
+// Live-slot list of one selection row, built by a whole warp: lane l classifies
+// slots l, l + 32, ... (slot_kind, with the TOKEN-mode duplicate test), and a
+// ballot compacts the live ones in slot order, so put(pos, kblk, kind, slot) sees
+// exactly the sequence a serial walk over the slots would produce.  selrow ==
+// nullptr is the identity selection (slot j is key block j, kk = nblk).  At most
+// maxn entries are kept; the return value (the same in every lane) is their
+// count.  One global load per lane instead of kk dependent ones on one thread.
+template <typename Put>
+__device__ __forceinline__ int warp_live_slots(const int32_t *selrow, int kk, int maxn, int qblk,
+                                               int nblk, int bs, int L, int mask_mode, int causal,
+                                               int32_t *status, Put put) {
+  const int lane = threadIdx.x & 31;
+  int n = 0;
+  for (int j0 = 0; j0 < kk && n < maxn; j0 += 32) {
+    const int j = j0 + lane;
+    int kb = 0, kind = KIND_SKIP;
+    if (j < kk) {
+      if (selrow) {
+        kb = __ldg(selrow + j);
+        bool dup = false;
+        if (mask_mode == BSA_MASK_TOKEN)
+          for (int i = 0; i < j && !dup; ++i) dup = __ldg(selrow + i) == kb;
+        kind = slot_kind(kb, j, dup, qblk, nblk, bs, L, mask_mode, causal, status);
+      } else {
+        kb = j;
+        kind = slot_kind(kb, kb, false, qblk, nblk, bs, L, mask_mode, causal, status);
+      }
+    }
+    const unsigned live = __ballot_sync(0xffffffffu, kind != KIND_SKIP);
+    const int pos = n + __popc(live & ((1u << lane) - 1u));
+    if (kind != KIND_SKIP && pos < maxn) put(pos, kb, kind, j);
+    n += __popc(live);
+  }
+  return n < maxn ? n : maxn;
+}
+
 // Largest kk for an explicit selection (slot table kept in shared memory).
 constexpr int kMaxKK = 512;
 
