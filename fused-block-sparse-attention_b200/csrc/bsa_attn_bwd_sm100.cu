@@ -135,6 +135,11 @@ __global__ void __launch_bounds__(352, 1)
   const int nunits = (int)((total + 1) / 2) * pl.Y;
 
   if (tid == 0) {
+    // descriptors fetched ahead of the first TMA load
+    prefetch_tmap(&tq);
+    prefetch_tmap(&tdo);
+    prefetch_tmap(&tk);
+    prefetch_tmap(&tv);
     // per tile t: s_full/p_full/s_empty (S^T, dP^T buffers and the P^T, dS^T
     // written over them), acc_empty (dK/dV accumulators); the ring stage and the K/V buffer are
     // released by both tiles' MMAs (two commits each)

@@ -60,6 +60,7 @@ __global__ void __launch_bounds__(192, 2)
   __shared__ uint32_t tmem_base_sh;
   __shared__ int s_item[2][D5_MAXN];
   __shared__ int s_islot[2][D5_MAXN];
+  __shared__ float s_gv[2][D5_MAXN];  // gate value of the j-th live slot
   __shared__ int s_n[2];
   __shared__ float s_dg[2][D5_MAXN][4];  // dgate partials: (tile, step, warp)
 
@@ -82,15 +83,23 @@ __global__ void __launch_bounds__(192, 2)
     int n = 0;
     if (t == 0 || validB) {
       const int32_t *selrow = p.sel + b * p.sel_sb + hk * p.sel_sh + (long long)qi * p.sel_sn;
+      const float *grow = p.gate ? p.gate + b * p.gate_sb + hk * p.gate_sh + (long long)qi * p.gate_sn
+                                 : nullptr;
       n = warp_live_slots(selrow, p.kk, D5_MAXN, qblk, p.nblk, p.bs, p.L, p.mask_mode, p.causal,
                           p.status, [&](int pos, int kb, int kind, int slot) {
                             s_item[t][pos] = (kb << 3) | kind;
                             s_islot[t][pos] = slot;
+                            s_gv[t][pos] = grow ? __ldg(grow + slot) : 0.f;
                           });
     }
     if (lane == 0) s_n[t] = n;
   }
   if (tid == 0) {
+    // descriptors fetched ahead of the first TMA load
+    prefetch_tmap(&tq);
+    prefetch_tmap(&tdo);
+    prefetch_tmap(&tk);
+    prefetch_tmap(&tv);
     mbar_init(&bar_q, 1);
     for (int s = 0; s < D5_KST; ++s) {
       mbar_init(&k_full[s], 1);
@@ -282,7 +291,7 @@ __global__ void __launch_bounds__(192, 2)
         const int item = s_item[t][j];
         kind = item & 7;
         kb = item >> 3;
-        g2 = gaterow ? __ldg(gaterow + s_islot[t][j]) * kLog2e : 0.f;
+        g2 = gaterow ? s_gv[t][j] * kLog2e : 0.f;
       }
       const float off = g2 - lse;  // exponent offset of this row and step
       uint32_t w[32];

@@ -86,6 +86,9 @@ __global__ void __launch_bounds__(192, 2)
     if (lane == 0) s_n[t] = n;
   }
   if (tid == 0) {
+    // descriptors fetched ahead of the first TMA load
+    prefetch_tmap(&tds);
+    prefetch_tmap(&tk);
     for (int s = 0; s < DS_NST; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);

@@ -79,7 +79,7 @@ __global__ void __launch_bounds__(G8_THREADS, G8<D>::MINB)
   __shared__ uint32_t tmem_base_sh;
   constexpr int MAXN = G8<D>::MAXN;
   __shared__ int s_item[MAXN];   // (kb << 3) | kind of the j-th live slot
-  __shared__ int s_islot[MAXN];
+  __shared__ float s_gv[MAXN];  // its gate value (read with the list)
   __shared__ int s_n;
   __shared__ float s_xch[3][4][2][32];  // half-row maxima (by step parity), row sums
 
@@ -97,15 +97,22 @@ __global__ void __launch_bounds__(G8_THREADS, G8<D>::MINB)
   if (warp == 0) {  // live-slot list, built by the whole warp
     const int32_t *selrow =
         p.sel ? p.sel + b * p.sel_sb + hk * p.sel_sh + (long long)qi * p.sel_sn : nullptr;
+    const float *grow = (p.gate && p.sel)
+                            ? p.gate + b * p.gate_sb + hk * p.gate_sh + (long long)qi * p.gate_sn
+                            : nullptr;
     const int n = warp_live_slots(selrow, p.sel ? p.kk : p.nblk, MAXN, qblk, p.nblk, p.bs, p.L,
                                   p.mask_mode, p.causal, p.status,
                                   [&](int pos, int kb, int kind, int slot) {
                                     s_item[pos] = (kb << 3) | kind;
-                                    s_islot[pos] = slot;
+                                    s_gv[pos] = grow ? __ldg(grow + slot) : 0.f;
                                   });
     if (lane == 0) s_n = n;
   }
   if (tid == 0) {
+    // descriptors fetched ahead of the first TMA load
+    prefetch_tmap(&tq);
+    prefetch_tmap(&tk);
+    prefetch_tmap(&tv);
     mbar_init(&bar_q, 1);
     for (int s = 0; s < NSL; ++s) {
       mbar_init(&r_full[s], 1);
@@ -266,7 +273,7 @@ __global__ void __launch_bounds__(G8_THREADS, G8<D>::MINB)
       if (lane == 0) tc05::mbar_arrive(&s_empty);
       const int item = s_item[j];
       const int kind = item & 7, kb = item >> 3;
-      const float g2 = gaterow ? __ldg(gaterow + s_islot[j]) * kLog2e : 0.f;
+      const float g2 = gaterow ? s_gv[j] * kLog2e : 0.f;
       if (kind & (KIND_TRIU | KIND_PAD)) {
 #pragma unroll
         for (int c = 0; c < 64; ++c)

@@ -72,7 +72,7 @@ __global__ void __launch_bounds__(192, 1)
       s_full[2], s_empty[2], p_full[2], o_done, o_final;
   __shared__ uint32_t tmem_base_sh;
   __shared__ int s_item[2][F5_MAXN];  // (kb << 3) | kind of the j-th live slot
-  __shared__ int s_islot[2][F5_MAXN];
+  __shared__ float s_gv[2][F5_MAXN];  // its gate value (read with the list)
   __shared__ int s_n[2];
 
   // ---- CTA coordinates: (b, kv head, query-block pair, head in group)
@@ -96,15 +96,21 @@ __global__ void __launch_bounds__(192, 1)
     int n = 0;
     if (t == 0 || validB) {
       const int32_t *selrow = p.sel + b * p.sel_sb + hk * p.sel_sh + (long long)qi * p.sel_sn;
+      const float *grow = p.gate ? p.gate + b * p.gate_sb + hk * p.gate_sh + (long long)qi * p.gate_sn
+                                 : nullptr;
       n = warp_live_slots(selrow, p.kk, F5_MAXN, qblk, p.nblk, p.bs, p.L, p.mask_mode, p.causal,
                           p.status, [&](int pos, int kb, int kind, int slot) {
                             s_item[t][pos] = (kb << 3) | kind;
-                            s_islot[t][pos] = slot;
+                            s_gv[t][pos] = grow ? __ldg(grow + slot) : 0.f;
                           });
     }
     if (lane == 0) s_n[t] = n;
   }
   if (tid == 0) {
+    // descriptors fetched ahead of the first TMA load
+    prefetch_tmap(&tq);
+    prefetch_tmap(&tk);
+    prefetch_tmap(&tv);
     mbar_init(&bar_q, 1);
     for (int s = 0; s < NK; ++s) {
       mbar_init(&k_full[s], 1);
@@ -292,7 +298,7 @@ __global__ void __launch_bounds__(192, 1)
       if (active) {
         const int item = s_item[t][j];
         const int kind = item & 7, kb = item >> 3;
-        g2 = gaterow ? __ldg(gaterow + s_islot[t][j]) * kLog2e : 0.f;
+        g2 = gaterow ? s_gv[t][j] * kLog2e : 0.f;
         if (kind & (KIND_TRIU | KIND_PAD)) {  // diagonal / padded block only
 #pragma unroll
           for (int c = 0; c < 64; ++c)
