@@ -91,53 +91,65 @@ def flops(cfg, heads):
 
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
-    """Samples nvidia-smi clocks / throttle reasons while the timed loop runs."""
+    """Samples nvidia-smi clocks / throttle reasons every 20 ms while the timed loop
+    runs.  The sampler starts half a second before the timed region (nvidia-smi
+    needs that long to come up) and only the samples whose timestamps fall inside
+    the region are summarised, so idle samples around it do not count."""
 
     def __init__(self, index):
         self.index = index
         self.proc = None
+        self.t0 = self.t1 = None
         self.path = os.path.join(tempfile.gettempdir(), "bsa_bench_clocks_%d_%d.csv" % (index, os.getpid()))
 
     def __enter__(self):
-        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+        q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), "--query-gpu=" + q,
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", "20"],
                                          stdout=self.f, stderr=subprocess.DEVNULL)
+            time.sleep(0.5)
         except Exception:
             self.proc = None
+        self.t0 = time.time()
         return self
 
     def __exit__(self, *exc):
+        self.t1 = time.time()
         if self.proc is not None:
             self.proc.terminate()
             self.proc.wait()
             self.f.close()
 
     def summary(self):
+        import datetime
         if self.proc is None or not os.path.exists(self.path):
             return None
-        sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        rows = []
         for line in open(self.path):
             f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
+            if len(f) < 10:
                 continue
             try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
+                ts = datetime.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                rows.append((ts, float(f[2]), float(f[3]), f[6:10]))
             except ValueError:
                 continue
-            for n, v in zip(names, f[5:9]):
+        inside = [r for r in rows if self.t0 - 0.02 <= r[0] <= self.t1 + 0.02]
+        if not inside:
+            return None
+        reasons = set()
+        for r in inside:
+            for n, v in zip(names, r[3]):
                 if v.lower().startswith("active"):
                     reasons.add(n)
-        if not sm:
-            return None
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        return {"sm_mhz": statistics.median(r[1] for r in inside), "sm_max_mhz": inside[-1][2],
+                "reasons": sorted(reasons), "samples": len(inside),
+                "window_ms": round((self.t1 - self.t0) * 1e3, 1)}
 
 
 # ---------------------------------------------------------------- our arm
