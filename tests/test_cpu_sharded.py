@@ -102,7 +102,7 @@ def _worker(rank, world, port, L, out_q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,L,port", [(2, 512, 29631), (4, 1024, 29633)])
+@pytest.mark.parametrize("world,L,port", [(2, 512, 29631), (4, 1024, 29633), (8, 1024, 29637)])
 def test_query_block_sharding_matches_single_process(world, L, port):
     _paths()
     from oracle import oracle as O
