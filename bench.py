@@ -96,8 +96,9 @@ class ClockSampler:
     needs that long to come up) and only the samples whose timestamps fall inside
     the region are summarised, so idle samples around it do not count."""
 
-    def __init__(self, index):
+    def __init__(self, index, enabled=True):
         self.index = index
+        self.enabled = enabled  # only the printing rank samples; every rank waits alike
         self.proc = None
         self.t0 = self.t1 = None
         self.path = os.path.join(tempfile.gettempdir(), "bsa_bench_clocks_%d_%d.csv" % (index, os.getpid()))
@@ -107,13 +108,15 @@ class ClockSampler:
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
         try:
+            if not self.enabled:
+                raise RuntimeError("sampling off on this rank")
             self.f = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), "--query-gpu=" + q,
                                           "--format=csv,noheader,nounits", "-lms", "20"],
                                          stdout=self.f, stderr=subprocess.DEVNULL)
-            time.sleep(0.5)
         except Exception:
             self.proc = None
+        time.sleep(0.5)
         self.t0 = time.time()
         return self
 
@@ -300,7 +303,7 @@ def run_ours(a):
     if dist:
         dist.barrier()
     torch.cuda.synchronize()
-    with ClockSampler(local) as clk:
+    with ClockSampler(local, enabled=rank == 0) as clk:
         for i in range(a.steps):
             flush.zero_()                          # L2 flush between timed steps
             step(cfg, q, k, v, do, evs[i])
@@ -609,7 +612,7 @@ def _timed(fn, steps, warmup, flush, dev_index, phases=1):
         fn(None)
     torch.cuda.synchronize()
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(phases + 1)] for _ in range(steps)]
-    with ClockSampler(dev_index) as clk:
+    with ClockSampler(dev_index, enabled=int(os.environ.get("RANK", "0")) == 0) as clk:
         for i in range(steps):
             flush.zero_()
             fn(evs[i])
